@@ -1,0 +1,119 @@
+/*
+ * moe_gemm_b200.h -- C ABI of the B200 (sm_100a) MoE expert-GEMM library.
+ *
+ * The reference (Steam086/moe-gemm-parallel-bench) is pure Python: its hot path
+ * is the Triton persistent grouped GEMM of kernels/grouped_gemm.py and the
+ * masked single GEMM of kernels/matmul.py.  This header is the native boundary
+ * that replaces those Triton launches.  Every entry point takes plain device
+ * pointers, sizes and a CUDA stream handle (cudaStream_t passed as void*); no
+ * framework types cross it.  The Python package `kernels` (same module and
+ * function names as the reference) binds it through ctypes.
+ *
+ * Element types, precisions and the tile record follow the reference:
+ *   dtype      fp16 | bf16 | fp32           utils/benchmark.py:35-38
+ *   precision  "ieee" | "tf32"              kernels/matmul.py:268, grouped_gemm.py:389,475
+ *   tile       KernelConfig fields          kernels/matmul.py:19-32
+ * All launches are asynchronous on `stream`, allocate nothing, synchronise
+ * nothing, and may be recorded into a CUDA graph.
+ */
+#ifndef MOE_GEMM_B200_H
+#define MOE_GEMM_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum mgb_dtype { MGB_FP16 = 0, MGB_BF16 = 1, MGB_FP32 = 2 };
+enum mgb_precision { MGB_IEEE = 0, MGB_TF32 = 1 };
+
+enum mgb_status {
+  MGB_OK = 0,
+  MGB_ERR_INVALID = 1,     /* bad argument (shape, dtype, null pointer): the reference's ValueError */
+  MGB_ERR_UNSUPPORTED = 2, /* no native kernel for this request: the reference's RuntimeError */
+  MGB_ERR_CUDA = 3,        /* a CUDA runtime / driver call failed */
+  MGB_ERR_SCRATCH = 4      /* scratch buffer missing or smaller than grouped_gemm_scratch_bytes() */
+};
+
+/* The fields of the reference's KernelConfig (kernels/matmul.py:19-32).  The
+ * library maps block_m / block_n to one of its native tiles; the other fields
+ * are accepted for provenance and do not change the kernel that runs. */
+typedef struct mgb_tile_config {
+  int32_t block_m, block_n, block_k, group_size_m, num_warps, num_stages, cta_multiplier;
+} mgb_tile_config;
+
+/* What a launch actually ran (filled when the pointer is non-null). */
+typedef struct mgb_launch_info {
+  int32_t path;    /* 0 = TMA + tcgen05 tensor-core kernel, 1 = generic-stride SIMT kernel */
+  int32_t swap_ab; /* 1 when the weight dimension is the MMA M dimension (narrow-M variant) */
+  int32_t tile_m, tile_n, tile_k, stages, grid;
+} mgb_launch_info;
+
+/* Bytes of scratch a grouped launch may need on a device with `sm_count` SMs
+ * (per-CTA tensor-map slots of the TMA path).  Replaces nothing in the
+ * reference: Triton kernels there take raw pointers and need no descriptors. */
+size_t grouped_gemm_scratch_bytes(int32_t problem_count, int32_t sm_count);
+
+/* One launch of the persistent grouped GEMM: for e in [0, problem_count)
+ *   C_e[M_e, N_e] = A_e[M_e, K_e] @ B_e[K_e, N_e]   (fp32 accumulate, cast on store)
+ * Replaces the Triton launches of launch_grouped (kernels/grouped_gemm.py:618-760,
+ * kernels _homogeneous_grouped_kernel_impl :321-397 and
+ * _generic_grouped_kernel_impl :399-482).  The tables are the reference
+ * workspace's device tensors (kernels/grouped_gemm.py:530-544):
+ *   a_ptrs, b_ptrs, c_ptrs   int64 [problem_count]   device addresses
+ *   dims                     int32 [problem_count, 3] (M, N, K) -- note the M, N, K order
+ *   strides                  int64 [problem_count, 6] (am, ak, bk, bn, cm, cn), in elements
+ * They are read on the device at run time, so an entry changed after the
+ * workspace was built is honoured by the next launch.
+ *   homogeneous  1 when every problem is (m, n, k) with contiguous strides
+ *                (the reference's `homogeneous` flag, :550-552); then dims and
+ *                strides are not read.  Otherwise (m, n, k) are the maxima
+ *                (MAX_M / MAX_N / MAX_K, :641-649) and size the grid.
+ *   operands_tma_aligned  the caller's promise that every A_e / B_e has a
+ *                16-byte aligned base, unit inner stride and 16-byte multiple
+ *                row pitch.  Then the tensor-core path runs; a table entry that
+ *                breaks the promise is skipped on the device and reported in the
+ *                error word (never dereferenced).  0 selects the generic path.
+ *   scratch      device buffer of at least grouped_gemm_scratch_bytes() bytes,
+ *                owned by the caller; not shared by launches that overlap.
+ */
+int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs,
+                        const int32_t* dims, const int64_t* strides, int32_t problem_count,
+                        int32_t homogeneous, int64_t m, int64_t n, int64_t k, int32_t dtype,
+                        int32_t precision, int32_t operands_tma_aligned, const mgb_tile_config* config,
+                        void* scratch, size_t scratch_bytes, void* stream, mgb_launch_info* info);
+
+/* Masked single GEMM C[m, n] = A[m, k] @ B[k, n] with arbitrary element strides.
+ * Replaces the Triton launch of launch_matmul (kernels/matmul.py:332-392,
+ * kernel _matmul_kernel_impl :223-273).  Operands that satisfy the TMA rules
+ * run on the tensor cores; others on the generic-stride kernel. */
+int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k, int64_t stride_am,
+                  int64_t stride_ak, int64_t stride_bk, int64_t stride_bn, int64_t stride_cm, int64_t stride_cn,
+                  int32_t dtype, int32_t precision, const mgb_tile_config* config, void* stream,
+                  mgb_launch_info* info);
+
+/* Reads and clears the device's error word: OR of the bits the kernels raised
+ * since the last call (bounded waits that gave up, table entries that broke
+ * the TMA promise).  Synchronous.  The reference has no counterpart: Triton
+ * kernels there cannot report device-side failures. */
+int read_and_clear_error_word(int32_t device, uint32_t* word);
+
+/* Test hook: the wait budget (SM clock cycles) of every bounded barrier wait
+ * and test flags for later launches in this process (bit 0: make the epilogue
+ * wait on a barrier nothing arrives on, which must time out and be reported).
+ * budget <= 0 restores the default. */
+int mgb_set_debug(int64_t wait_budget_cycles, int32_t test_flags);
+
+/* Human-readable text for an mgb_status value. */
+const char* mgb_status_string(int32_t status);
+
+/* ABI version of this header (bumped on any signature change). */
+int32_t mgb_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_GEMM_B200_H */

@@ -1,0 +1,335 @@
+// C ABI of the library (declared in include/moe_gemm_b200.h): argument checks,
+// native tile selection, tensor-map encoding and the launches.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/moe_gemm_b200.h"
+#include "mgb_common.cuh"
+#include "mgb_dispatch.cuh"
+#include "mgb_ptx.cuh"
+
+namespace {
+
+using mgb::GroupedParams;
+using mgb::TcVariant;
+using mgb::TcVariantInfo;
+
+// One error word per device (module-scope __device__ storage is per device).
+__device__ uint32_t g_error_word;
+
+constexpr int kMaxDevices = 128;
+constexpr int kMaxSlotsPerCta = 16;              // >= every variant's kSlots
+constexpr size_t kSlotBytes = 2 * sizeof(CUtensorMap);  // act + wgt maps
+constexpr long long kDefaultWaitBudget = 2000000000ll;  // ~1 s of SM clock
+
+std::mutex g_mutex;
+uint32_t* g_error_ptr[kMaxDevices] = {};
+int g_sm_count[kMaxDevices] = {};
+long long g_wait_budget = kDefaultWaitBudget;
+int g_test_flags = 0;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+struct DeviceState {
+  int device;
+  int sm_count;
+  uint32_t* error_word;
+};
+
+// Per-device facts resolved once, on the first launch on that device.
+int device_state(DeviceState* out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return MGB_ERR_CUDA;
+  std::lock_guard<std::mutex> lock(g_mutex);
+  if (g_error_ptr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_error_word) != cudaSuccess) return MGB_ERR_CUDA;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || sms <= 0) {
+      return MGB_ERR_CUDA;
+    }
+    g_sm_count[dev] = sms;
+    g_error_ptr[dev] = static_cast<uint32_t*>(ptr);
+  }
+  if (g_encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000, cudaEnableDefault, &q) !=
+            cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || fn == nullptr) {
+      return MGB_ERR_CUDA;
+    }
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  out->device = dev;
+  out->sm_count = g_sm_count[dev];
+  out->error_word = g_error_ptr[dev];
+  return MGB_OK;
+}
+
+int elem_size(int dtype) { return dtype == MGB_FP32 ? 4 : 2; }
+
+CUtensorMapDataType map_type(int dtype) {
+  return dtype == MGB_FP32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+         : dtype == MGB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                             : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+// 2-D row-major map: `inner` contiguous elements per row, `outer` rows,
+// `pitch` bytes between rows; 128-byte swizzled boxes of box_inner x box_outer.
+bool encode_2d(CUtensorMap* map, int dtype, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
+               uint32_t box_inner, uint32_t box_outer) {
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {pitch};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode(map, map_type(dtype), 2, const_cast<void*>(base), dims, strides, box, estr,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Maps the reference's KernelConfig tile to a native tensor-core tile.
+// block_m <= 64 selects the swap-AB (weight-streaming) family with that many
+// tokens per tile; block_m == 128 the MMA-M = 128 token family; larger
+// block_m the swap-AB 256-token tile.  block_n picks the weight tile.
+TcVariant pick_variant(const mgb_tile_config* cfg) {
+  const int bm = cfg ? cfg->block_m : 64;
+  const int bn = cfg ? cfg->block_n : 128;
+  const int wide = bn >= 256 ? 256 : 128;
+  if (bm <= 16) return {true, 16, wide};
+  if (bm <= 32) return {true, 32, wide};
+  if (bm <= 64) return {true, 64, wide};
+  if (bm <= 128) return {false, 128, bn <= 64 ? 64 : (bn <= 128 ? 128 : 256)};
+  return {true, 256, 128};
+}
+
+bool variant_info(int dtype, const TcVariant& v, TcVariantInfo* info) {
+  switch (dtype) {
+    case MGB_FP16: return mgb::tc_variant_info<__half>(v, info);
+    case MGB_BF16: return mgb::tc_variant_info<__nv_bfloat16>(v, info);
+    default: return mgb::tc_variant_info<float>(v, info);
+  }
+}
+
+int tc_launch_typed(int dtype, const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt,
+                    const GroupedParams& p, int grid, cudaStream_t s) {
+  switch (dtype) {
+    case MGB_FP16: return mgb::tc_launch<__half>(v, act, wgt, p, grid, s);
+    case MGB_BF16: return mgb::tc_launch<__nv_bfloat16>(v, act, wgt, p, grid, s);
+    default: return mgb::tc_launch<float>(v, act, wgt, p, grid, s);
+  }
+}
+
+int simt_launch_typed(int dtype, const GroupedParams& p, int grid, cudaStream_t s) {
+  switch (dtype) {
+    case MGB_FP16: return mgb::simt_launch<__half>(p, grid, s);
+    case MGB_BF16: return mgb::simt_launch<__nv_bfloat16>(p, grid, s);
+    default: return mgb::simt_launch<float>(p, grid, s);
+  }
+}
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Upper bound on the tiles of a launch: problems x tiles of the largest problem.
+int grid_for(int64_t problems, int64_t m, int64_t n, int tm, int tn, int64_t cap) {
+  const int64_t tiles = problems * cdiv(std::max<int64_t>(m, 1), tm) * cdiv(std::max<int64_t>(n, 1), tn);
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, cap)));
+}
+
+void fill_info(mgb_launch_info* info, int path, const TcVariant& v, const TcVariantInfo& vi, int grid) {
+  if (info == nullptr) return;
+  info->path = path;
+  info->swap_ab = path == 0 && v.swap ? 1 : 0;
+  info->tile_m = path == 0 ? v.tm : mgb::kSimtBM;
+  info->tile_n = path == 0 ? v.tn : mgb::kSimtBN;
+  info->tile_k = path == 0 ? vi.bk : mgb::kSimtBK;
+  info->stages = path == 0 ? vi.stages : 1;
+  info->grid = grid;
+}
+
+bool valid_dtype(int dtype, int precision) {
+  return (dtype == MGB_FP16 || dtype == MGB_BF16 || dtype == MGB_FP32) &&
+         (precision == MGB_IEEE || precision == MGB_TF32);
+}
+
+}  // namespace
+
+extern "C" {
+
+size_t grouped_gemm_scratch_bytes(int32_t problem_count, int32_t sm_count) {
+  (void)problem_count;
+  const size_t ctas = sm_count > 0 ? static_cast<size_t>(sm_count) : 1;
+  return ctas * kMaxSlotsPerCta * kSlotBytes;
+}
+
+int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs, const int32_t* dims,
+                        const int64_t* strides, int32_t problem_count, int32_t homogeneous, int64_t m, int64_t n,
+                        int64_t k, int32_t dtype, int32_t precision, int32_t operands_tma_aligned,
+                        const mgb_tile_config* config, void* scratch, size_t scratch_bytes, void* stream,
+                        mgb_launch_info* info) {
+  if (!valid_dtype(dtype, precision) || problem_count <= 0 || a_ptrs == nullptr || b_ptrs == nullptr ||
+      c_ptrs == nullptr || m < 0 || n < 0 || k < 0) {
+    return MGB_ERR_INVALID;
+  }
+  if (!homogeneous && (dims == nullptr || strides == nullptr)) return MGB_ERR_INVALID;
+  DeviceState ds;
+  if (int st = device_state(&ds)) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  GroupedParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.a_ptrs = a_ptrs;
+  p.b_ptrs = b_ptrs;
+  p.c_ptrs = c_ptrs;
+  p.dims = dims;
+  p.strides = strides;
+  p.problem_count = problem_count;
+  p.homogeneous = homogeneous ? 1 : 0;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.wait_budget = g_wait_budget;
+  p.test_flags = g_test_flags;
+  p.error_word = ds.error_word;
+
+  const bool tensor_core = operands_tma_aligned && (dtype != MGB_FP32 || precision == MGB_TF32) && m > 0 &&
+                           n > 0 && k > 0;
+  if (tensor_core) {
+    const TcVariant v = pick_variant(config);
+    TcVariantInfo vi;
+    if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
+    const int grid = grid_for(problem_count, m, n, v.tm, v.tn, ds.sm_count);
+    const size_t need = static_cast<size_t>(grid) * vi.slots * kSlotBytes;
+    if (scratch == nullptr || scratch_bytes < need || reinterpret_cast<uintptr_t>(scratch) % 128 != 0) {
+      return MGB_ERR_SCRATCH;
+    }
+    p.desc_slots = static_cast<uint8_t*>(scratch);
+    // Templates: box shape, swizzle and element type are final; the device
+    // rewrites the base address (and, for heterogeneous groups, the extents
+    // and row pitch) of its copies per problem.  The scratch pointer stands in
+    // as a 16-byte aligned placeholder address; it is never read through.
+    const int es = elem_size(dtype);
+    const uint64_t act_pitch = ((static_cast<uint64_t>(k) * es + 15) / 16) * 16;
+    const uint64_t wgt_pitch = ((static_cast<uint64_t>(n) * es + 15) / 16) * 16;
+    CUtensorMap act, wgt;
+    if (!encode_2d(&act, dtype, scratch, k, m, act_pitch, vi.bk, v.tm) ||
+        !encode_2d(&wgt, dtype, scratch, n, k, wgt_pitch, vi.bk, vi.bk)) {
+      return MGB_ERR_CUDA;
+    }
+    const int e = tc_launch_typed(dtype, v, act, wgt, p, grid, s);
+    if (e != 0) return MGB_ERR_CUDA;
+    fill_info(info, 0, v, vi, grid);
+    return MGB_OK;
+  }
+  const int grid = grid_for(problem_count, m, n, mgb::kSimtBM, mgb::kSimtBN, 4ll * ds.sm_count);
+  const int e = simt_launch_typed(dtype, p, grid, s);
+  if (e != 0) return MGB_ERR_CUDA;
+  fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0, 0}, grid);
+  return MGB_OK;
+}
+
+int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k, int64_t stride_am,
+                  int64_t stride_ak, int64_t stride_bk, int64_t stride_bn, int64_t stride_cm, int64_t stride_cn,
+                  int32_t dtype, int32_t precision, const mgb_tile_config* config, void* stream,
+                  mgb_launch_info* info) {
+  if (!valid_dtype(dtype, precision) || m < 0 || n < 0 || k < 0) return MGB_ERR_INVALID;
+  if ((m > 0 && n > 0) && (c == nullptr || (k > 0 && (a == nullptr || b == nullptr)))) return MGB_ERR_INVALID;
+  DeviceState ds;
+  if (int st = device_state(&ds)) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+
+  GroupedParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.single = 1;
+  p.problem_count = 1;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.a = a;
+  p.b = b;
+  p.c = c;
+  p.sam = stride_am;
+  p.sak = stride_ak;
+  p.sbk = stride_bk;
+  p.sbn = stride_bn;
+  p.scm = stride_cm;
+  p.scn = stride_cn;
+  p.wait_budget = g_wait_budget;
+  p.test_flags = g_test_flags;
+  p.error_word = ds.error_word;
+  if (m == 0 || n == 0) {
+    fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0, 0}, 0);
+    return MGB_OK;
+  }
+
+  const int es = elem_size(dtype);
+  const bool aligned = reinterpret_cast<uintptr_t>(a) % 16 == 0 && reinterpret_cast<uintptr_t>(b) % 16 == 0 &&
+                       stride_ak == 1 && stride_bn == 1 && stride_am > 0 && stride_bk > 0 &&
+                       (stride_am * es) % 16 == 0 && (stride_bk * es) % 16 == 0 && m < (1ll << 31) &&
+                       n < (1ll << 31) && k < (1ll << 31);
+  const bool tensor_core = aligned && k > 0 && (dtype != MGB_FP32 || precision == MGB_TF32);
+  if (tensor_core) {
+    const TcVariant v = pick_variant(config);
+    TcVariantInfo vi;
+    if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
+    CUtensorMap act, wgt;
+    if (!encode_2d(&act, dtype, a, k, m, static_cast<uint64_t>(stride_am) * es, vi.bk, v.tm) ||
+        !encode_2d(&wgt, dtype, b, n, k, static_cast<uint64_t>(stride_bk) * es, vi.bk, vi.bk)) {
+      return MGB_ERR_CUDA;
+    }
+    const int grid = grid_for(1, m, n, v.tm, v.tn, ds.sm_count);
+    const int e = tc_launch_typed(dtype, v, act, wgt, p, grid, s);
+    if (e != 0) return MGB_ERR_CUDA;
+    fill_info(info, 0, v, vi, grid);
+    return MGB_OK;
+  }
+  const int grid = grid_for(1, m, n, mgb::kSimtBM, mgb::kSimtBN, 4ll * ds.sm_count);
+  const int e = simt_launch_typed(dtype, p, grid, s);
+  if (e != 0) return MGB_ERR_CUDA;
+  fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0, 0}, grid);
+  return MGB_OK;
+}
+
+int read_and_clear_error_word(int32_t device, uint32_t* word) {
+  if (word == nullptr) return MGB_ERR_INVALID;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess) return MGB_ERR_CUDA;
+  if (device != prev && cudaSetDevice(device) != cudaSuccess) return MGB_ERR_INVALID;
+  uint32_t value = 0, zero = 0;
+  const bool ok = cudaMemcpyFromSymbol(&value, g_error_word, sizeof(value)) == cudaSuccess &&
+                  cudaMemcpyToSymbol(g_error_word, &zero, sizeof(zero)) == cudaSuccess;
+  if (device != prev) cudaSetDevice(prev);
+  if (!ok) return MGB_ERR_CUDA;
+  *word = value;
+  return MGB_OK;
+}
+
+int mgb_set_debug(int64_t wait_budget_cycles, int32_t test_flags) {
+  std::lock_guard<std::mutex> lock(g_mutex);
+  g_wait_budget = wait_budget_cycles > 0 ? wait_budget_cycles : kDefaultWaitBudget;
+  g_test_flags = test_flags;
+  return MGB_OK;
+}
+
+const char* mgb_status_string(int32_t status) {
+  switch (status) {
+    case MGB_OK: return "ok";
+    case MGB_ERR_INVALID: return "invalid argument";
+    case MGB_ERR_UNSUPPORTED: return "unsupported configuration";
+    case MGB_ERR_CUDA: return "CUDA call failed";
+    case MGB_ERR_SCRATCH: return "scratch buffer missing, misaligned or too small";
+    default: return "unknown status";
+  }
+}
+
+int32_t mgb_abi_version(void) { return 1; }
+
+}  // extern "C"

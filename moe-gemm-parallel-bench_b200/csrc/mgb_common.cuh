@@ -1,0 +1,134 @@
+// Launch parameters and the device-side problem/tile walk shared by the
+// tensor-core kernel and the SIMT kernel.
+//
+// A launch covers `problem_count` independent GEMMs C_e = A_e @ B_e.  The
+// per-problem pointers, dims (M, N, K) and element strides (am, ak, bk, bn,
+// cm, cn) are read on the device from the caller's tables, exactly the tables
+// the reference builds in kernels/grouped_gemm.py:530-544.  Reading them on the
+// device (not on the host) keeps launches graph-capturable and lets callers
+// swap a table entry after the workspace was built.
+#pragma once
+
+#include <cstdint>
+
+namespace mgb {
+
+// Tile of the generic-stride SIMT kernel (mgb_simt_kernel.cuh).
+constexpr int kSimtThreads = 256;
+constexpr int kSimtBM = 64;
+constexpr int kSimtBN = 64;
+constexpr int kSimtBK = 16;
+
+struct GroupedParams {
+  // Table mode (grouped launches).
+  const int64_t* a_ptrs;
+  const int64_t* b_ptrs;
+  const int64_t* c_ptrs;
+  const int32_t* dims;     // [E, 3]: M, N, K
+  const int64_t* strides;  // [E, 6]: am, ak, bk, bn, cm, cn (elements)
+  int32_t problem_count;
+  int32_t homogeneous;  // every problem has (m, n, k) below and contiguous strides
+  int64_t m, n, k;
+  // Inline mode (single GEMM): one problem, pointers and strides passed by value.
+  int32_t single;
+  const void* a;
+  const void* b;
+  void* c;
+  int64_t sam, sak, sbk, sbn, scm, scn;
+  // Scratch for the per-CTA tensor-map slots of the TMA path.
+  uint8_t* desc_slots;
+  long long wait_budget;  // SM clock cycles a barrier wait may take before the launch gives up
+  int32_t test_flags;     // bit 0: make the epilogue wait on a barrier nothing arrives on
+  uint32_t* error_word;   // where error bits are OR-ed (a __device__ word of this library)
+};
+
+struct Problem {
+  int64_t m, n, k;
+  const char* a;
+  const char* b;
+  char* c;
+  int64_t sam, sak, sbk, sbn, scm, scn;
+};
+
+__device__ __forceinline__ Problem load_problem(const GroupedParams& p, int e) {
+  Problem q;
+  if (p.single) {
+    q.m = p.m; q.n = p.n; q.k = p.k;
+    q.a = static_cast<const char*>(p.a);
+    q.b = static_cast<const char*>(p.b);
+    q.c = static_cast<char*>(p.c);
+    q.sam = p.sam; q.sak = p.sak; q.sbk = p.sbk; q.sbn = p.sbn; q.scm = p.scm; q.scn = p.scn;
+    return q;
+  }
+  q.a = reinterpret_cast<const char*>(p.a_ptrs[e]);
+  q.b = reinterpret_cast<const char*>(p.b_ptrs[e]);
+  q.c = reinterpret_cast<char*>(p.c_ptrs[e]);
+  if (p.homogeneous) {
+    q.m = p.m; q.n = p.n; q.k = p.k;
+    q.sam = p.k; q.sak = 1; q.sbk = p.n; q.sbn = 1; q.scm = p.n; q.scn = 1;
+  } else {
+    q.m = p.dims[3 * e + 0];
+    q.n = p.dims[3 * e + 1];
+    q.k = p.dims[3 * e + 2];
+    const int64_t* s = p.strides + 6 * e;
+    q.sam = s[0]; q.sak = s[1]; q.sbk = s[2]; q.sbn = s[3]; q.scm = s[4]; q.scn = s[5];
+  }
+  return q;
+}
+
+__device__ __forceinline__ int64_t ceil_div64(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Walks the flattened tile space problem by problem.  Each CTA visits its
+// tiles in increasing order, so the walk only ever moves forward: the whole
+// launch costs one pass over the problem table per CTA (the reference scans it
+// the same way, kernels/grouped_gemm.py:426-436).  Tiles inside a problem are
+// ordered M-block fastest, so CTAs that run at the same time share a weight
+// column block in L2.
+template <int TM, int TN>
+struct TileWalk {
+  int problem = -1;
+  int64_t first = 0;   // first global tile of `problem`
+  int64_t count = 0;   // tiles of `problem`
+  int64_t m_blocks = 1;
+  Problem prob;
+
+  // Moves to the problem holding global tile `t`; false when `t` is past the end.
+  __device__ __forceinline__ bool seek(const GroupedParams& p, int64_t t) {
+    if (p.single || p.homogeneous) {
+      if (problem < 0) {
+        Problem q = load_problem(p, 0);
+        m_blocks = ceil_div64(q.m, TM);
+        count = (q.m > 0 && q.n > 0) ? m_blocks * ceil_div64(q.n, TN) : 0;
+      }
+      const int total_problems = p.single ? 1 : p.problem_count;
+      if (count == 0) return false;
+      const int64_t e = t / count;
+      if (e >= total_problems) return false;
+      if (e != problem) {
+        problem = static_cast<int>(e);
+        first = e * count;
+        prob = load_problem(p, problem);
+      }
+      return true;
+    }
+    while (problem < 0 || t >= first + count) {
+      first += count;
+      ++problem;
+      if (problem >= p.problem_count) return false;
+      prob = load_problem(p, problem);
+      if (prob.m <= 0 || prob.n <= 0 || prob.k < 0) {
+        count = 0;
+        m_blocks = 1;
+        continue;
+      }
+      m_blocks = ceil_div64(prob.m, TM);
+      count = m_blocks * ceil_div64(prob.n, TN);
+    }
+    return true;
+  }
+
+  __device__ __forceinline__ int64_t m_block(int64_t t) const { return (t - first) % m_blocks; }
+  __device__ __forceinline__ int64_t n_block(int64_t t) const { return (t - first) / m_blocks; }
+};
+
+}  // namespace mgb

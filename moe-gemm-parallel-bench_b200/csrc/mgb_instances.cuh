@@ -1,0 +1,75 @@
+// Instantiates every native variant for one element type (included by the
+// per-type translation units with MGB_ELEM defined).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "mgb_dispatch.cuh"
+#include "mgb_simt_kernel.cuh"
+#include "mgb_tc_kernel.cuh"
+
+namespace mgb {
+
+// The variant list: swap-AB token tiles 16/32/64 (x weight tiles 128/256),
+// swap-AB 256 x 128, and MMA-M = 128 token tiles with weight tiles 64/128/256.
+#define MGB_FOR_EACH_VARIANT(X) \
+  X(true, 16, 128)              \
+  X(true, 16, 256)              \
+  X(true, 32, 128)              \
+  X(true, 32, 256)              \
+  X(true, 64, 128)              \
+  X(true, 64, 256)              \
+  X(true, 256, 128)             \
+  X(false, 128, 64)             \
+  X(false, 128, 128)            \
+  X(false, 128, 256)
+
+template <typename T, bool SWAP, int TM, int TN>
+static int launch_variant(const CUtensorMap& act, const CUtensorMap& wgt, const GroupedParams& p, int grid,
+                          cudaStream_t stream) {
+  using Cfg = TcCfg<T, SWAP, TM, TN>;
+  static bool configured[128] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 128) return static_cast<int>(cudaErrorInvalidDevice);
+  if (!configured[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(tc_grouped_kernel<T, SWAP, TM, TN>,
+                                               cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    configured[dev] = true;
+  }
+  tc_grouped_kernel<T, SWAP, TM, TN><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(act, wgt, p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+template <>
+bool tc_variant_info<MGB_ELEM>(const TcVariant& v, TcVariantInfo* info) {
+#define MGB_INFO(S, M, N)                                          \
+  if (v.swap == S && v.tm == M && v.tn == N) {                     \
+    using Cfg = TcCfg<MGB_ELEM, S, M, N>;                          \
+    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSlots, Cfg::kSmemBytes}; \
+    return true;                                                   \
+  }
+  MGB_FOR_EACH_VARIANT(MGB_INFO)
+#undef MGB_INFO
+  return false;
+}
+
+template <>
+int tc_launch<MGB_ELEM>(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt, const GroupedParams& p,
+                        int grid, cudaStream_t stream) {
+#define MGB_LAUNCH(S, M, N) \
+  if (v.swap == S && v.tm == M && v.tn == N) return launch_variant<MGB_ELEM, S, M, N>(act, wgt, p, grid, stream);
+  MGB_FOR_EACH_VARIANT(MGB_LAUNCH)
+#undef MGB_LAUNCH
+  return static_cast<int>(cudaErrorInvalidValue);
+}
+
+template <>
+int simt_launch<MGB_ELEM>(const GroupedParams& p, int grid, cudaStream_t stream) {
+  simt_grouped_kernel<MGB_ELEM><<<grid, kSimtThreads, 0, stream>>>(p);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace mgb

@@ -1,0 +1,88 @@
+"""Float64 restatement of the reference's per-expert GEMM -- test infrastructure only.
+
+The reference checks every grouped launch against per-expert ``torch.matmul``
+on the same inputs (benchmark_moe.py:259-266): W2 / plain groups are
+``A_e @ B_e``; packed W13 is ``cat(A_e @ B_e[:, :F], A_e @ B_e[:, F:])``.  Its
+kernels accumulate in fp32 and cast on store (kernels/grouped_gemm.py:377,
+392-396; kernels/matmul.py:256-273).  Here the products are summed in float64
+(tighter than any device accumulation) and rounded once to the output type.
+
+numpy has no bfloat16: bf16 data travels as float32 arrays whose values are
+bf16-representable, and ``round_to_dtype`` rounds to nearest-even on the bit
+pattern.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Sequence
+
+import numpy as np
+
+DTYPES = ("fp16", "bf16", "fp32")
+
+
+def bf16_round(values: np.ndarray) -> np.ndarray:
+    """float32 -> nearest-even bfloat16, returned as float32 (NaN stays NaN)."""
+    x = np.ascontiguousarray(values, dtype=np.float32)
+    bits = x.view(np.uint32).astype(np.uint64)
+    lsb = (bits >> 16) & 1
+    rounded = ((bits + 0x7FFF + lsb) & 0xFFFF0000).astype(np.uint32)
+    out = rounded.view(np.float32).copy()
+    nan = np.isnan(x)
+    out[nan] = np.nan
+    return out
+
+
+def round_to_dtype(values: np.ndarray, dtype: str) -> np.ndarray:
+    """Round float64 results once to the output type; returned as float64."""
+    if dtype == "fp32":
+        return values.astype(np.float32).astype(np.float64)
+    if dtype == "fp16":
+        return values.astype(np.float16).astype(np.float64)
+    if dtype == "bf16":
+        return bf16_round(values.astype(np.float32)).astype(np.float64)
+    raise ValueError(f"unknown dtype {dtype}")
+
+
+def quantize_input(values: np.ndarray, dtype: str) -> np.ndarray:
+    """Input values as the device stores them (float64 view of the rounded data)."""
+    return round_to_dtype(np.asarray(values, dtype=np.float64), dtype)
+
+
+def matmul(a: np.ndarray, b: np.ndarray, dtype: str) -> np.ndarray:
+    """C = A @ B, float64 sums, one rounding to `dtype` (kernels/matmul.py:256-273)."""
+    a64 = np.asarray(a, dtype=np.float64)
+    b64 = np.asarray(b, dtype=np.float64)
+    if a64.ndim != 2 or b64.ndim != 2 or a64.shape[1] != b64.shape[0]:
+        raise ValueError(f"shape mismatch: A={a64.shape}, B={b64.shape}")
+    return round_to_dtype(a64 @ b64, dtype)
+
+
+def grouped_gemm(a_list: Sequence[np.ndarray], b_list: Sequence[np.ndarray], dtype: str) -> list[np.ndarray]:
+    """Per-expert C_e = A_e @ B_e (benchmark_moe.py:265-266)."""
+    if len(a_list) != len(b_list) or not a_list:
+        raise ValueError("grouped GEMM requires equally many A and B matrices")
+    return [matmul(a, b, dtype) for a, b in zip(a_list, b_list)]
+
+
+def gate_up(a: np.ndarray, packed_b: np.ndarray, dtype: str) -> np.ndarray:
+    """Packed W13 output [A @ gate | A @ up] (benchmark_moe.py:260-264)."""
+    if packed_b.shape[1] % 2:
+        raise ValueError("packed gate+up weight needs an even output dimension")
+    half = packed_b.shape[1] // 2
+    return np.concatenate((matmul(a, packed_b[:, :half], dtype), matmul(a, packed_b[:, half:], dtype)), axis=1)
+
+
+def exact_integer_outputs(shape: tuple[int, int, int], problems: int) -> list[np.ndarray]:
+    """Known answer of tests/test_gpu.py:127-154: A = 1, B_e = e + 1 gives C_e = K * (e + 1)."""
+    m, k, n = shape
+    return [np.full((m, n), float(k * (e + 1))) for e in range(problems)]
+
+
+def relative_frobenius(actual: np.ndarray, expected: np.ndarray) -> float:
+    """||actual - expected||_F / ||expected||_F (0 when both are zero)."""
+    diff = np.linalg.norm(np.asarray(actual, np.float64) - np.asarray(expected, np.float64))
+    scale = np.linalg.norm(np.asarray(expected, np.float64))
+    if scale == 0.0:
+        return float(diff)
+    return float(diff / scale)

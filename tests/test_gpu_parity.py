@@ -1,0 +1,491 @@
+"""GPU parity of the native kernels against the oracle and the reference's outputs.
+
+Every launch goes through the C ABI (kernels -> ctypes -> libmoe_gemm_b200.so).
+Cases follow the reference's own GPU tests (tests/test_gpu.py in the
+reference, cited per test) plus the golden outputs of the reference's Triton
+kernels and DeepSeek-V3-shaped groups.
+
+Tolerances (written here, applied per case):
+* relative Frobenius error vs the float64 oracle: bf16 <= 1e-2 (the target's
+  bound), fp16 <= 2e-3, fp32 "ieee" <= 1e-5, fp32 "tf32" <= 5e-3;
+* the reference's assert_close (utils/benchmark.py:261-271): fp16 2e-2,
+  bf16 5e-2, fp32 2e-3 (rtol = atol);
+* exact-integer cases: bit-exact.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+
+from tests.conftest import cuda_ready
+
+pytestmark = [pytest.mark.gpu, pytest.mark.skipif(not cuda_ready(), reason="needs a CUDA GPU")]
+
+REL_FRO = {"bf16": 1e-2, "fp16": 2e-3, "fp32": 1e-5, "tf32": 5e-3}
+ASSERT_CLOSE = {"fp16": 2e-2, "bf16": 5e-2, "fp32": 2e-3}
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _dtype(name):
+    torch = _torch()
+    return {"fp16": torch.float16, "bf16": torch.bfloat16, "fp32": torch.float32}[name]
+
+
+def _host(t) -> np.ndarray:
+    return t.detach().float().cpu().numpy().astype(np.float64)
+
+
+def _oracle_check(c, a, b, dtype: str, precision: str = "ieee", gate_up: bool = False):
+    from oracle import gemm as oracle
+
+    a64, b64 = _host(a), _host(b)
+    expected = oracle.gate_up(a64, b64, dtype) if gate_up else oracle.matmul(a64, b64, dtype)
+    got = _host(c)
+    assert np.isfinite(got).all(), "output has non-finite values (unwritten or overflow)"
+    key = "tf32" if (dtype == "fp32" and precision == "tf32") else dtype
+    err = oracle.relative_frobenius(got, expected)
+    assert err <= REL_FRO[key], f"relative Frobenius error {err:.3e} > {REL_FRO[key]:.1e}"
+    tol = ASSERT_CLOSE[dtype]
+    np.testing.assert_allclose(got, expected, rtol=tol, atol=tol)
+    return err
+
+
+def _randn(shape, dtype, gen, scale=0.1):
+    torch = _torch()
+    return (torch.randn(shape, device="cuda", generator=gen) * scale).to(dtype)
+
+
+def _workspace(shapes, dtype_name, seed, b_scale=None):
+    """Seeded per-expert tensors (A ~ N(0,1)*0.1 unless b_scale given: then
+    A ~ N(0,1) and B ~ N(0, b_scale)) wrapped into a grouped workspace."""
+    torch = _torch()
+    from kernels import workspace_from_tensors
+
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    dtype = _dtype(dtype_name)
+    a_list, b_list, c_list = [], [], []
+    for m, k, n in shapes:
+        if b_scale is None:
+            a_list.append(_randn((m, k), dtype, gen))
+            b_list.append(_randn((k, n), dtype, gen))
+        else:
+            a_list.append(_randn((m, k), dtype, gen, 1.0))
+            b_list.append(_randn((k, n), dtype, gen, b_scale))
+        c_list.append(torch.full((m, n), float("nan"), device="cuda", dtype=dtype))
+    return workspace_from_tensors(a_list, b_list, c_list)
+
+
+def _poison(workspace):
+    for c in workspace.c:
+        c.fill_(float("nan"))
+
+
+# --------------------------------------------------------------- plumbing
+def test_native_library_is_loaded_and_tensor_core_path_runs():
+    """The parity below must come from the native library, not a fallback."""
+    torch = _torch()
+    from kernels import KernelConfig, check_device_errors, launch_grouped
+
+    ws = _workspace([(16, 256, 256)] * 2, "bf16", seed=1)
+    launch_grouped(ws, config=KernelConfig(16, 128, 64, 1, 4, 3), autotune=False)
+    torch.cuda.synchronize()
+    maps = open("/proc/self/maps").read()
+    assert "libmoe_gemm_b200.so" in maps
+    assert ws.launch_info["path"] == "tcgen05_tma"
+    assert ws.launch_info["swap_ab"] == 1
+    check_device_errors()
+    for a, b, c in ws.problem_tensors():
+        _oracle_check(c, a, b, "bf16")
+
+
+# ------------------------------------------------------- golden fixtures
+def test_golden_reference_outputs(golden_cases):
+    """Native outputs vs the reference's Triton outputs (interpreter-generated)
+    and vs the oracle, on the same inputs."""
+    torch = _torch()
+    from kernels import KernelConfig, check_device_errors, launch_grouped, launch_matmul, workspace_from_tensors
+
+    configs = (KernelConfig(16, 128, 64, 4, 4, 3), KernelConfig(64, 256, 64, 8, 8, 4), KernelConfig(128, 128, 64, 8, 8, 4))
+    for case in golden_cases:
+        dtype = case["dtype"]
+        tol = 2e-3 if dtype == "fp16" else 1e-4
+        if case["kind"] == "single_strided":
+            a_base = torch.from_numpy(case["a_base"]).cuda()
+            b_base = torch.from_numpy(case["b_base"]).cuda()
+            c_base = torch.full_like(torch.from_numpy(case["c_base"]).cuda(), float("nan"))
+            a, b, c = a_base[:, ::2], b_base[:, ::2], c_base[:, ::2]
+            launch_matmul(a, b, c, input_precision="tf32")
+            torch.cuda.synchronize()
+            expected = torch.from_numpy(case["c_base"])[:, ::2].numpy()
+            np.testing.assert_allclose(_host(c), expected, rtol=2e-3, atol=2e-3)
+            assert torch.isnan(c_base[:, 1::2]).all(), "strided C: untouched columns were written"
+            continue
+        a_list = [torch.from_numpy(x).cuda() for x in case["a"]]
+        b_list = [torch.from_numpy(x).cuda() for x in case["b"]]
+        if case["kind"] == "single":
+            c = torch.full((a_list[0].shape[0], b_list[0].shape[1]), float("nan"), device="cuda",
+                           dtype=a_list[0].dtype)
+            launch_matmul(a_list[0], b_list[0], c, autotune=False)
+            torch.cuda.synchronize()
+            np.testing.assert_allclose(_host(c), case["c"][0].astype(np.float64), rtol=tol, atol=tol,
+                                       err_msg=case["name"])
+            continue
+        c_list = [torch.empty((a.shape[0], b.shape[1]), device="cuda", dtype=a.dtype) for a, b in zip(a_list, b_list)]
+        ws = workspace_from_tensors(a_list, b_list, c_list)
+        for cfg in configs:
+            _poison(ws)
+            launch_grouped(ws, config=cfg, autotune=False)
+            torch.cuda.synchronize()
+            for e, (a, b, c) in enumerate(ws.problem_tensors()):
+                np.testing.assert_allclose(_host(c), case["c"][e].astype(np.float64), rtol=tol, atol=tol,
+                                           err_msg=f"{case['name']} problem {e} config {cfg}")
+                _oracle_check(c, a, b, dtype, gate_up=case["kind"] == "gate_up")
+    check_device_errors()
+
+
+# ------------------------------------------------ reference test_gpu ports
+def test_project_shapes_fp16_vs_fp32_reference():
+    """tests/test_gpu.py:34-52: fp16 groups vs an fp32 reference at 2e-3."""
+    torch = _torch()
+    from kernels import KernelConfig, build_grouped_workspace, launch_grouped
+
+    for shapes in ([(128, 256, 128)] * 3, [(128, 128, 128), (256, 64, 256)]):
+        ws = build_grouped_workspace(shapes, torch.float16, seed=123)
+        for cfg in (KernelConfig(128, 128, 32, 1, 4, 3), KernelConfig(64, 64, 32, 1, 4, 3),
+                    KernelConfig(128, 128, 64, 1, 4, 3), KernelConfig(64, 128, 64, 1, 4, 3)):
+            _poison(ws)
+            launch_grouped(ws, config=cfg, autotune=False)
+            torch.cuda.synchronize()
+            for a, b, c in ws.problem_tensors():
+                reference = (a.float() @ b.float()).half()
+                torch.testing.assert_close(c, reference, rtol=2e-3, atol=2e-3)
+
+
+@pytest.mark.parametrize("dtype_name", ["fp16", "bf16", "fp32"])
+def test_single_odd_shapes_all_dtypes(dtype_name):
+    """tests/test_gpu.py:69-86."""
+    torch = _torch()
+    from kernels import last_matmul_config, launch_matmul, select_config
+
+    gen = torch.Generator(device="cuda").manual_seed(7)
+    for m, k, n in ((1, 5, 3), (17, 13, 31), (33, 70, 65), (64, 128, 256), (200, 320, 136)):
+        a = _randn((m, k), _dtype(dtype_name), gen)
+        b = _randn((k, n), _dtype(dtype_name), gen)
+        c = torch.full((m, n), float("nan"), device="cuda", dtype=_dtype(dtype_name))
+        fallback = select_config(m, n, k)
+        launch_matmul(a, b, c, fallback)
+        torch.cuda.synchronize()
+        selected = last_matmul_config(fallback)
+        assert selected.block_m in (16, 32, 64, 128, 256)
+        assert selected.block_n in (32, 64, 128, 256)
+        assert selected.block_k in (32, 64, 128)
+        _oracle_check(c, a, b, dtype_name)
+
+
+def test_single_strided_fp32_tf32():
+    """tests/test_gpu.py:88-97: strided views, TF32 requested."""
+    torch = _torch()
+    from kernels import launch_matmul
+
+    gen = torch.Generator(device="cuda").manual_seed(8)
+    m, k, n = 17, 70, 65
+    a = _randn((m, k * 2), torch.float32, gen)[:, ::2]
+    b = _randn((k, n * 2), torch.float32, gen)[:, ::2]
+    storage = torch.full((m, n * 2), float("nan"), device="cuda")
+    c = storage[:, ::2]
+    launch_matmul(a, b, c, input_precision="tf32")
+    torch.cuda.synchronize()
+    _oracle_check(c, a, b, "fp32", "tf32")
+    assert torch.isnan(storage[:, 1::2]).all()
+
+
+def test_fp32_tf32_tensor_core_path():
+    """TMA-aligned fp32 with TF32 runs tcgen05 kind::tf32, both orientations."""
+    torch = _torch()
+    from kernels import KernelConfig, launch_grouped
+
+    ws = _workspace([(40, 256, 384), (40, 256, 384), (40, 256, 384)], "fp32", seed=9)
+    for cfg in (KernelConfig(32, 128, 32, 4, 4, 3), KernelConfig(128, 256, 64, 8, 8, 4)):
+        _poison(ws)
+        launch_grouped(ws, "tf32", cfg, autotune=False)
+        torch.cuda.synchronize()
+        assert ws.launch_info["path"] == "tcgen05_tma"
+        for a, b, c in ws.problem_tensors():
+            _oracle_check(c, a, b, "fp32", "tf32")
+
+
+@pytest.mark.parametrize("dtype_name", ["fp16", "bf16", "fp32"])
+def test_grouped_distinct_pointers_shapes_and_dtypes(dtype_name):
+    """tests/test_gpu.py:99-115: heterogeneous problems -> generic scheduler."""
+    torch = _torch()
+    from kernels import build_grouped_workspace, launch_grouped, select_config
+
+    shapes = [(1, 5, 3), (17, 13, 31), (9, 70, 65)]
+    ws = build_grouped_workspace(shapes, _dtype(dtype_name), seed=99, config=select_config(17, 65, 70))
+    assert len({x.data_ptr() for x in ws.a}) == len(shapes)
+    launch_grouped(ws)
+    torch.cuda.synchronize()
+    assert ws.scheduler == "generic_persistent"
+    assert ws.config.block_k in (32, 64, 128)
+    assert ws.config.num_warps in (2, 4, 8)
+    for a, b, c in ws.problem_tensors():
+        _oracle_check(c, a, b, dtype_name)
+
+
+@pytest.mark.parametrize("dtype_name", ["fp16", "bf16"])
+def test_grouped_heterogeneous_tma_aligned(dtype_name):
+    """Heterogeneous but TMA-legal problems: per-problem tensor maps rebuilt on the device."""
+    torch = _torch()
+    from kernels import KernelConfig, launch_grouped
+
+    shapes = [(16, 128, 128), (40, 192, 256), (130, 64, 384), (1, 320, 64), (77, 256, 128)]
+    ws = _workspace(shapes, dtype_name, seed=5)
+    assert not ws.homogeneous
+    for cfg in (KernelConfig(16, 128, 64, 4, 4, 3), KernelConfig(32, 256, 64, 4, 8, 4),
+                KernelConfig(64, 128, 64, 8, 4, 4), KernelConfig(128, 64, 64, 8, 4, 3),
+                KernelConfig(128, 256, 64, 8, 8, 4), KernelConfig(256, 128, 64, 8, 8, 4)):
+        _poison(ws)
+        launch_grouped(ws, config=cfg, autotune=False)
+        torch.cuda.synchronize()
+        assert ws.launch_info["path"] == "tcgen05_tma", ws.launch_info
+        assert ws.scheduler == "generic_persistent"
+        for a, b, c in ws.problem_tensors():
+            _oracle_check(c, a, b, dtype_name)
+
+
+def test_grouped_homogeneous_persistent_fast_path():
+    """tests/test_gpu.py:117-125."""
+    torch = _torch()
+    from kernels import build_grouped_workspace, launch_grouped
+
+    ws = build_grouped_workspace([(17, 13, 31)] * 3, torch.float16, seed=101)
+    assert ws.homogeneous
+    launch_grouped(ws)
+    torch.cuda.synchronize()
+    assert ws.scheduler == "homogeneous_persistent"
+    for a, b, c in ws.problem_tensors():
+        _oracle_check(c, a, b, "fp16")
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1), (17, 33, 65), (33, 64, 136), (130, 128, 256)])
+def test_homogeneous_tail_candidates_write_every_output(shape):
+    """tests/test_gpu.py:127-154: exact integers for every candidate config."""
+    torch = _torch()
+    from kernels import build_grouped_workspace, grouped_candidate_configs, launch_grouped
+
+    for dtype in (torch.float16, torch.bfloat16, torch.float32):
+        ws = build_grouped_workspace([shape] * 3, dtype)
+        for index, (a, b, _) in enumerate(ws.problem_tensors()):
+            a.fill_(1)
+            b.fill_(index + 1)
+        m, k, n = shape
+        candidates = grouped_candidate_configs(m, n, k, problem_count=3, sm_count=ws.sm_count)
+        assert candidates
+        for config in candidates:
+            _poison(ws)
+            launch_grouped(ws, config=config, autotune=False)
+            torch.cuda.synchronize()
+            for index, output in enumerate(ws.c):
+                torch.testing.assert_close(output, torch.full_like(output, k * (index + 1)), rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("dtype_name,k,n", [("fp32", 33, 65), ("bf16", 64, 136), ("fp16", 192, 64)])
+def test_homogeneous_multiple_rounds_and_guard_storage(dtype_name, k, n):
+    """tests/test_gpu.py:156-174: > one persistent round, C swapped after build
+    (including c_ptrs), NaN guard bands around every C must survive."""
+    torch = _torch()
+    from kernels import KernelConfig, build_grouped_workspace, launch_grouped
+
+    config = KernelConfig(16, 32, 32, 4, 4, 2)
+    sm_count = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    m = (sm_count + 1) * config.block_m + 1
+    ws = build_grouped_workspace([(m, k, n)] * 2, _dtype(dtype_name))
+    guards = []
+    for index in range(ws.problem_count):
+        storage = torch.full((m * n + 32,), float("nan"), device="cuda", dtype=_dtype(dtype_name))
+        output = storage[16:-16].view(m, n)
+        guards.append(storage)
+        ws.c[index] = output
+        ws.c_ptrs[index] = output.data_ptr()
+    for cfg in (config, KernelConfig(128, 128, 64, 8, 8, 4)):
+        launch_grouped(ws, config=cfg, autotune=False)
+        torch.cuda.synchronize()
+        for (a, b, c), storage in zip(ws.problem_tensors(), guards):
+            if dtype_name == "fp32":
+                reference = (a.double() @ b.double()).float()
+                torch.testing.assert_close(c, reference, rtol=1e-4, atol=1e-6)
+            else:
+                _oracle_check(c, a, b, dtype_name)
+            assert torch.isnan(storage[:16]).all()
+            assert torch.isnan(storage[-16:]).all()
+
+
+def test_fused_gate_up_packed_output_in_one_grouped_launch():
+    """tests/test_gpu.py:176-188 (plus a TMA-aligned bf16 W13 miniature)."""
+    torch = _torch()
+    from kernels import build_fused_gate_up_workspace, launch_grouped
+
+    for dtype_name, shapes in (("fp16", [(17, 13, 62)] * 3), ("bf16", [(24, 256, 512)] * 3)):
+        ws = build_fused_gate_up_workspace(shapes, _dtype(dtype_name), seed=102)
+        assert ws.operation == "gate_up"
+        launch_grouped(ws)
+        torch.cuda.synchronize()
+        assert ws.scheduler == "homogeneous_persistent"
+        for a, packed_weight, packed_output in ws.problem_tensors():
+            _oracle_check(packed_output, a, packed_weight, dtype_name, gate_up=True)
+
+
+def test_one_problem_group_dispatches_standard_matmul():
+    """tests/test_gpu.py:190-195."""
+    torch = _torch()
+    from kernels import build_grouped_workspace, launch_grouped
+
+    for dtype, shape in ((torch.float16, (17, 70, 65)), (torch.bfloat16, (96, 256, 384))):
+        ws = build_grouped_workspace([shape], dtype, seed=103)
+        launch_grouped(ws)
+        torch.cuda.synchronize()
+        assert ws.scheduler == "single_problem_matmul"
+        _oracle_check(ws.c[0], ws.a[0], ws.b[0], "fp16" if dtype == torch.float16 else "bf16")
+
+
+def test_graph_capture_and_replay_reads_tables_on_device():
+    """Launches record into a CUDA graph (utils/benchmark.py:123-151); a replay
+    after the inputs change computes the new product (tables and data are
+    read on the device at run time)."""
+    torch = _torch()
+    from kernels import KernelConfig, launch_grouped
+
+    ws = _workspace([(32, 512, 256)] * 4, "bf16", seed=11)
+    cfg = KernelConfig(32, 128, 64, 4, 4, 3)
+    launch_grouped(ws, config=cfg, autotune=False)  # eager warm-up outside capture
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        launch_grouped(ws, config=cfg, autotune=False)
+    for a in ws.a:
+        a.mul_(-1.5)
+    _poison(ws)
+    graph.replay()
+    torch.cuda.synchronize()
+    for a, b, c in ws.problem_tensors():
+        _oracle_check(c, a, b, "bf16")
+
+
+def test_autotune_selects_a_candidate_and_caches_it():
+    torch = _torch()
+    from kernels import build_fused_gate_up_workspace, grouped_candidate_configs, launch_grouped
+
+    ws = build_fused_gate_up_workspace([(16, 1024, 1024)] * 8, torch.bfloat16, seed=3)
+    launch_grouped(ws)
+    torch.cuda.synchronize()
+    first = ws.config
+    candidates = grouped_candidate_configs(16, 1024, 1024, problem_count=8, sm_count=ws.sm_count)
+    assert first in candidates
+    _poison(ws)
+    launch_grouped(ws)
+    torch.cuda.synchronize()
+    assert ws.config == first
+    for a, b, c in ws.problem_tensors():
+        _oracle_check(c, a, b, "bf16", gate_up=True)
+
+
+# --------------------------------------------------- DeepSeek-V3 shapes
+def _sampled_rows_check(ws, dtype_name, rows_per_problem=24, seed=0, gate_up=False):
+    """Oracle on a sample of output rows (full K reduction, all N columns)."""
+    torch = _torch()
+    rng = np.random.default_rng(seed)
+    for a, b, c in ws.problem_tensors():
+        m = a.shape[0]
+        rows = np.unique(np.concatenate([[0, m - 1], rng.integers(0, m, size=rows_per_problem)]))
+        idx = torch.as_tensor(rows, device=a.device)
+        _oracle_check(c.index_select(0, idx), a.index_select(0, idx), b, dtype_name, gate_up=gate_up)
+
+
+@pytest.mark.parametrize("m_e", [16, 64, 128, 256, 1024])
+@pytest.mark.parametrize("proj,k,n", [("W13_EP", 7168, 4096), ("W13_TP", 7168, 512), ("W2_EP", 2048, 7168),
+                                      ("W2_TP", 256, 7168)])
+def test_deepseek_v3_rank_shapes(m_e, proj, k, n):
+    """DeepSeek-V3 P=8 rank shapes with 3 experts, the autotuned
+    launch, A ~ N(0,1), B ~ N(0, 1/sqrt(K)); oracle on sampled rows."""
+    torch = _torch()
+    from kernels import check_device_errors, launch_grouped
+
+    ws = _workspace([(m_e, k, n)] * 3, "bf16", seed=m_e + k, b_scale=1.0 / math.sqrt(k))
+    launch_grouped(ws)
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert ws.launch_info["path"] == "tcgen05_tma"
+    _sampled_rows_check(ws, "bf16", gate_up=proj.startswith("W13"))
+
+
+def test_full_size_w13_ep_column_checksums():
+    """Full DeepSeek-V3 W13 EP rank (32 x [1024, 7168] @ [7168, 4096]):
+    size-independent linearity check 1^T C = (1^T A) B per expert, in fp64."""
+    torch = _torch()
+    from kernels import check_device_errors, launch_grouped
+
+    ws = _workspace([(1024, 7168, 4096)] * 32, "bf16", seed=77, b_scale=1.0 / math.sqrt(7168))
+    launch_grouped(ws)
+    torch.cuda.synchronize()
+    check_device_errors()
+    for a, b, c in ws.problem_tensors():
+        expected = a.double().sum(0) @ b.double()
+        got = c.double().sum(0)
+        err = float((got - expected).norm() / expected.norm())
+        assert err < 1e-2, err
+
+
+def test_bounded_wait_reports_and_context_survives():
+    """Failure detection without a fault: the test hook makes the epilogue
+    wait on a barrier nothing arrives on; the wait gives up after its budget,
+    the error word reports it, and the context keeps working."""
+    torch = _torch()
+    from kernels import KernelConfig, _native, check_device_errors, launch_grouped
+
+    ws = _workspace([(16, 256, 256)] * 2, "bf16", seed=12)
+    check_device_errors()
+    _native.set_debug(wait_budget_cycles=2_000_000, test_flags=1)
+    try:
+        launch_grouped(ws, config=KernelConfig(16, 128, 64, 4, 4, 3), autotune=False)
+        torch.cuda.synchronize()
+    finally:
+        _native.set_debug(0, 0)
+    word = _native.read_and_clear_error_word(torch.cuda.current_device())
+    assert word == _native.TEST_WAIT_BIT, _native.describe_error_word(word)
+    _poison(ws)
+    launch_grouped(ws, config=KernelConfig(16, 128, 64, 4, 4, 3), autotune=False)
+    torch.cuda.synchronize()
+    check_device_errors()
+    for a, b, c in ws.problem_tensors():
+        _oracle_check(c, a, b, "bf16")
+
+
+def test_table_entry_breaking_alignment_is_skipped_not_faulted():
+    """A device table entry changed to an address that breaks the TMA
+    promise is skipped on the device and reported; nothing is dereferenced."""
+    torch = _torch()
+    from kernels import KernelConfig, _native, launch_grouped
+
+    ws = _workspace([(16, 256, 256)] * 3, "bf16", seed=13)
+    check_ok = _native.read_and_clear_error_word(torch.cuda.current_device())
+    del check_ok
+    good = int(ws.a_ptrs[1].item())
+    ws.a_ptrs[1] = good + 2  # misaligned by 2 bytes, still inside the allocation
+    _poison(ws)
+    launch_grouped(ws, config=KernelConfig(16, 128, 64, 4, 4, 3), autotune=False)
+    torch.cuda.synchronize()
+    word = _native.read_and_clear_error_word(torch.cuda.current_device())
+    assert word & (1 << 5)
+    assert torch.isnan(ws.c[1]).all()
+    for e in (0, 2):
+        _oracle_check(ws.c[e], ws.a[e], ws.b[e], "bf16")
+    ws.a_ptrs[1] = good
