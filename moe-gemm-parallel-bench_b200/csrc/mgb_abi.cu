@@ -76,6 +76,13 @@ int device_state(DeviceState* out) {
 
 int elem_size(int dtype) { return dtype == MGB_FP32 ? 4 : 2; }
 
+// Activations (K-major) always use the 128-byte swizzle.  Weights are the
+// MN-major operand: MN-major TF32 needs the 32-byte-granule 128-byte swizzle.
+constexpr CUtensorMapSwizzle kActSwizzle = CU_TENSOR_MAP_SWIZZLE_128B;
+CUtensorMapSwizzle wgt_swizzle(int dtype) {
+  return dtype == MGB_FP32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+}
+
 CUtensorMapDataType map_type(int dtype) {
   return dtype == MGB_FP32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
          : dtype == MGB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
@@ -83,15 +90,15 @@ CUtensorMapDataType map_type(int dtype) {
 }
 
 // 2-D row-major map: `inner` contiguous elements per row, `outer` rows,
-// `pitch` bytes between rows; 128-byte swizzled boxes of box_inner x box_outer.
+// `pitch` bytes between rows; swizzled boxes of box_inner x box_outer.
 bool encode_2d(CUtensorMap* map, int dtype, const void* base, uint64_t inner, uint64_t outer, uint64_t pitch,
-               uint32_t box_inner, uint32_t box_outer) {
+               uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {pitch};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1, 1};
   const CUresult r = g_encode(map, map_type(dtype), 2, const_cast<void*>(base), dims, strides, box, estr,
-                              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
@@ -220,8 +227,8 @@ int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
     const uint64_t act_pitch = ((static_cast<uint64_t>(k) * es + 15) / 16) * 16;
     const uint64_t wgt_pitch = ((static_cast<uint64_t>(n) * es + 15) / 16) * 16;
     CUtensorMap act, wgt;
-    if (!encode_2d(&act, dtype, scratch, k, m, act_pitch, vi.bk, v.tm) ||
-        !encode_2d(&wgt, dtype, scratch, n, k, wgt_pitch, vi.bk, vi.bk)) {
+    if (!encode_2d(&act, dtype, scratch, k, m, act_pitch, vi.bk, v.tm, kActSwizzle) ||
+        !encode_2d(&wgt, dtype, scratch, n, k, wgt_pitch, vi.bk, vi.bk, wgt_swizzle(dtype))) {
       return MGB_ERR_CUDA;
     }
     const int e = tc_launch_typed(dtype, v, act, wgt, p, grid, s);
@@ -281,8 +288,8 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
     TcVariantInfo vi;
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
     CUtensorMap act, wgt;
-    if (!encode_2d(&act, dtype, a, k, m, static_cast<uint64_t>(stride_am) * es, vi.bk, v.tm) ||
-        !encode_2d(&wgt, dtype, b, n, k, static_cast<uint64_t>(stride_bk) * es, vi.bk, vi.bk)) {
+    if (!encode_2d(&act, dtype, a, k, m, static_cast<uint64_t>(stride_am) * es, vi.bk, v.tm, kActSwizzle) ||
+        !encode_2d(&wgt, dtype, b, n, k, static_cast<uint64_t>(stride_bk) * es, vi.bk, vi.bk, wgt_swizzle(dtype))) {
       return MGB_ERR_CUDA;
     }
     const int grid = grid_for(1, m, n, v.tm, v.tn, ds.sm_count);

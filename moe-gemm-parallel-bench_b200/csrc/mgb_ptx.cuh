@@ -210,16 +210,21 @@ __device__ __forceinline__ void tmem_ld_wait() {
 }
 
 // ------------------------------------------------------ UMMA descriptors
-// Shared-memory matrix descriptor for the 128-byte-swizzled canonical layouts
-// (start address, leading/stride byte offsets, descriptor version 1, swizzle
-// mode 2 = 128B).  Tiles must sit on 1024-byte boundaries.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+// Shared-memory matrix descriptor layout types used here.
+constexpr uint32_t kLayoutSw128 = 2;        // 128-byte swizzle, 16-byte granules, 8-row atoms
+constexpr uint32_t kLayoutSw128Base32 = 1;  // 128-byte swizzle, 32-byte granules, 4-row atoms (MN-major TF32)
+
+// Shared-memory matrix descriptor (start address, leading/stride byte
+// offsets, descriptor version 1, layout type).  Tiles sit on 1024-byte
+// boundaries.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                                              uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= 1ull << 46;
-  d |= 2ull << 61;
+  d |= static_cast<uint64_t>(layout) << 61;
   return d;
 }
 

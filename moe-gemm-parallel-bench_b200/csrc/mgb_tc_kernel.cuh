@@ -63,6 +63,12 @@ struct TcCfg {
                                                                             : 0u;
   static constexpr uint32_t kIdesc = SWAP ? instr_desc(kFmt, 1, 0, 128, TM) : instr_desc(kFmt, 0, 1, TM, TN);
   static constexpr int kSmemBytes = kStages * kStageBytes + 2048 + 1024;
+  // The weight operand is MN-major.  For 16-bit types it uses the plain
+  // 128-byte swizzle (8-row K atoms, SBO 1024); MN-major TF32 admits only the
+  // 32-byte-granule variant (4-row K atoms, SBO 512), loaded by TMA with the
+  // matching 128B_ATOM_32B swizzle.
+  static constexpr uint32_t kWgtLayout = kElem == 4 ? kLayoutSw128Base32 : kLayoutSw128;
+  static constexpr uint32_t kWgtSbo = kElem == 4 ? 512u : 1024u;
 
   static_assert(kStages >= 2, "operand ring needs at least two stages");
   static_assert(TM % 16 == 0 && TM >= 16 && TM <= 256, "token tile");
@@ -329,12 +335,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int ks = 0; ks < Cfg::kKSteps; ++ks) {
             const uint32_t acc = (kb > 0 || ks > 0) ? 1u : 0u;
-            const uint64_t act_desc = smem_desc_sw128(a_base + ks * 32, 16, 1024);
+            const uint64_t act_desc = smem_desc(a_base + ks * 32, 16, 1024, kLayoutSw128);
             if constexpr (SWAP) {
 #pragma unroll
               for (int c = 0; c < TN / 128; ++c) {
-                const uint64_t wgt_desc =
-                    smem_desc_sw128(w_base + c * 16384 + ks * Cfg::kKStep * 128, Cfg::kBoxBytes, 1024);
+                const uint64_t wgt_desc = smem_desc(w_base + c * 16384 + ks * Cfg::kKStep * 128, Cfg::kBoxBytes,
+                                                    Cfg::kWgtSbo, Cfg::kWgtLayout);
                 if constexpr (std::is_same<T, float>::value) {
                   mma_tf32(d_tmem + c * TM, wgt_desc, act_desc, Cfg::kIdesc, acc);
                 } else {
@@ -342,7 +348,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
               }
             } else {
-              const uint64_t wgt_desc = smem_desc_sw128(w_base + ks * Cfg::kKStep * 128, Cfg::kBoxBytes, 1024);
+              const uint64_t wgt_desc =
+                  smem_desc(w_base + ks * Cfg::kKStep * 128, Cfg::kBoxBytes, Cfg::kWgtSbo, Cfg::kWgtLayout);
               if constexpr (std::is_same<T, float>::value) {
                 mma_tf32(d_tmem, act_desc, wgt_desc, Cfg::kIdesc, acc);
               } else {
