@@ -88,6 +88,10 @@ class GroupedWorkspace:
     scheduler: str = "not_launched"
     scratch: object = None
     launch_info: dict | None = field(default=None)
+    # Host-side TMA verdict for the A / B lists, computed once (see
+    # operands_tma_aligned).  The device re-checks every table entry, so an
+    # entry swapped later for a misaligned one is skipped, never dereferenced.
+    tma_aligned: bool | None = None
 
     @property
     def problem_count(self) -> int:
@@ -373,7 +377,9 @@ def launch_grouped(
         workspace.launch_info = last_launch_info()
         workspace.scheduler = SCHEDULER_SINGLE
         return
-    aligned = operands_tma_aligned(workspace)
+    if workspace.tma_aligned is None:
+        workspace.tma_aligned = operands_tma_aligned(workspace)
+    aligned = workspace.tma_aligned
     scheduler = SCHEDULER_HOMOGENEOUS if workspace.homogeneous else SCHEDULER_GENERIC
     if not autotune:
         _launch_native(workspace, cfg, input_precision, aligned)

@@ -1,0 +1,112 @@
+"""The oracle, pinned against outputs of the reference itself.
+
+tests/golden/gemm_cases.npz holds inputs and outputs of the reference's Triton
+kernels (kernels/grouped_gemm.py:321-482, kernels/matmul.py:223-273) executed
+by the Triton CPU interpreter (tests/golden/make_golden.py).  The oracle must
+reproduce them within the output type's rounding: the reference accumulates
+in fp32 and casts once, the oracle sums in float64 and casts once.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import gemm as oracle
+from tests.golden_data import load_gemm_cases
+
+CASES = load_gemm_cases()
+
+
+def _tolerance(dtype: str) -> tuple[float, float]:
+    # fp16: one output ulp at |C| ~ 1 plus fp32-vs-fp64 accumulation order;
+    # fp32: accumulation-order differences only.
+    return (2e-3, 2e-3) if dtype == "fp16" else (1e-5, 1e-6)
+
+
+@pytest.mark.parametrize("case", CASES, ids=[c["name"] for c in CASES])
+def test_oracle_reproduces_reference_outputs(case):
+    if case["kind"] == "single_strided":
+        a = case["a_base"][:, ::2].astype(np.float64)
+        b = case["b_base"][:, ::2].astype(np.float64)
+        expected = oracle.matmul(a, b, "fp32")
+        got = case["c_base"][:, ::2].astype(np.float64)
+        # The reference ran with input_precision="tf32"; the interpreter's dot
+        # keeps fp32 products, so the fp32 oracle agrees to TF32's tolerance.
+        np.testing.assert_allclose(got, expected, rtol=2e-3, atol=2e-3)
+        assert np.isnan(case["c_base"][:, 1::2]).all(), "reference wrote outside the strided view"
+        return
+    rtol, atol = _tolerance(case["dtype"])
+    for e, (a, b, c) in enumerate(zip(case["a"], case["b"], case["c"])):
+        if case["kind"] == "gate_up":
+            expected = oracle.gate_up(a.astype(np.float64), b.astype(np.float64), case["dtype"])
+        else:
+            expected = oracle.matmul(a.astype(np.float64), b.astype(np.float64), case["dtype"])
+        got = c.astype(np.float64)
+        assert np.isfinite(got).all(), f"{case['name']}: reference left unwritten outputs"
+        np.testing.assert_allclose(got, expected, rtol=rtol, atol=atol, err_msg=f"{case['name']} problem {e}")
+        assert oracle.relative_frobenius(got, expected) < (1e-3 if case["dtype"] == "fp16" else 1e-6)
+
+
+def test_golden_cases_cover_the_reference_test_shapes():
+    names = {c["name"] for c in CASES}
+    for required in ("grouped_generic_fp32", "grouped_generic_fp16", "grouped_homog_fp32", "grouped_homog_fp16",
+                     "gate_up_fp16", "tutorial_homog_fp16", "moe_narrow_fp16", "moe_tail_fp16", "moe_hetero_fp16",
+                     "single_fp32_strided_tf32"):
+        assert required in names
+    singles = {c["name"] for c in CASES if c["kind"] == "single"}
+    assert {"single_fp16_1x5x3", "single_fp32_17x13x31", "single_fp32_33x70x65"} <= singles
+
+
+@pytest.mark.parametrize("shape", [(1, 1, 1), (17, 33, 65)])
+def test_exact_integer_known_answer(shape):
+    """tests/test_gpu.py:127-154 of the reference: A = 1, B_e = e + 1."""
+    m, k, n = shape
+    for dtype in ("fp16", "bf16", "fp32"):
+        outs = oracle.grouped_gemm([np.ones((m, k))] * 3, [np.full((k, n), e + 1.0) for e in range(3)], dtype)
+        for got, expected in zip(outs, oracle.exact_integer_outputs(shape, 3)):
+            np.testing.assert_array_equal(got, expected)
+
+
+def test_gate_up_is_two_halves():
+    rng = np.random.default_rng(0)
+    a = rng.standard_normal((5, 7))
+    b = rng.standard_normal((7, 6))
+    packed = oracle.gate_up(a, b, "fp32")
+    np.testing.assert_array_equal(packed, oracle.matmul(a, b, "fp32"))
+    with pytest.raises(ValueError):
+        oracle.gate_up(a, rng.standard_normal((7, 5)), "fp32")
+
+
+def test_bf16_rounding_matches_torch():
+    torch = pytest.importorskip("torch")
+    rng = np.random.default_rng(1)
+    values = np.concatenate([
+        rng.standard_normal(10000).astype(np.float32) * 10,
+        # exact ties between two bf16 neighbours (round half to even)
+        (np.arange(1, 200, dtype=np.float32) * 2.0**-7 + 2.0**-15).astype(np.float32),
+        np.array([0.0, -0.0, 1e-40, 3.4e38, -3.4e38, np.inf, -np.inf], dtype=np.float32),
+    ])
+    ours = oracle.bf16_round(values)
+    theirs = torch.from_numpy(values).to(torch.bfloat16).float().numpy()
+    np.testing.assert_array_equal(ours, theirs)
+    assert np.isnan(oracle.bf16_round(np.array([np.nan], dtype=np.float32))).all()
+
+
+def test_rounding_is_idempotent_and_rejects_unknown():
+    rng = np.random.default_rng(2)
+    x = rng.standard_normal(1000)
+    for dtype in oracle.DTYPES:
+        once = oracle.round_to_dtype(x, dtype)
+        np.testing.assert_array_equal(oracle.round_to_dtype(once, dtype), once)
+    with pytest.raises(ValueError):
+        oracle.round_to_dtype(x, "fp8")
+    with pytest.raises(ValueError):
+        oracle.matmul(np.ones((2, 3)), np.ones((4, 2)), "fp32")
+
+
+def test_relative_frobenius():
+    a = np.array([[3.0, 4.0]])
+    assert oracle.relative_frobenius(a, a) == 0.0
+    assert oracle.relative_frobenius(np.zeros((1, 2)), a) == pytest.approx(1.0)
+    assert oracle.relative_frobenius(np.ones((2, 2)), np.zeros((2, 2))) == pytest.approx(2.0)
