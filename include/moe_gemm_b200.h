@@ -94,6 +94,35 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
                   int32_t dtype, int32_t precision, const mgb_tile_config* config, void* stream,
                   mgb_launch_info* info);
 
+/* Size of the scratch array compiled into the library for
+ * grouped_gemm_launch_noalloc (bytes, per GPU that loads the library). */
+#define MGB_NOALLOC_SCRATCH_BYTES (1u << 20)
+
+/* grouped_gemm_launch for callers that cannot allocate device memory.  No
+ * counterpart in the reference (its Triton launches need no scratch).
+ *
+ * Same arguments and result as grouped_gemm_launch, minus the scratch buffer:
+ * the tensor-map slots come from a fixed MGB_NOALLOC_SCRATCH_BYTES array inside
+ * this library, so the call allocates and frees nothing.  It serves callers
+ * with no device allocator of their own -- a plugin in a process whose
+ * framework owns all device memory, a launch made while a CUDA graph is being
+ * captured (cudaMalloc is not permitted there), a launch path that must never
+ * block in the driver's allocator.
+ *   - The first call on a device looks up the array's device address (once per
+ *     device, with that device current); make that first call before any
+ *     stream capture.
+ *   - A device whose launches could need more than MGB_NOALLOC_SCRATCH_BYTES
+ *     (more than 256 SMs) is refused with MGB_ERR_SCRATCH.
+ *   - Every call shares the one array and leaves its last contents behind;
+ *     nothing in it has to start at zero (each launch writes every slot before
+ *     reading it), but calls that overlap on the GPU -- other streams, other
+ *     threads -- race on it and must be serialised by the caller. */
+int grouped_gemm_launch_noalloc(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs,
+                                const int32_t* dims, const int64_t* strides, int32_t problem_count,
+                                int32_t homogeneous, int64_t m, int64_t n, int64_t k, int32_t dtype,
+                                int32_t precision, int32_t operands_tma_aligned, const mgb_tile_config* config,
+                                void* stream, mgb_launch_info* info);
+
 /* Reads and clears the device's error word: OR of the bits the kernels raised
  * since the last call (bounded waits that gave up, table entries that broke
  * the TMA promise).  Synchronous.  The reference has no counterpart: Triton

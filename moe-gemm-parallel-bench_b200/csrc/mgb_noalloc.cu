@@ -1,0 +1,73 @@
+// grouped_gemm_launch_noalloc: the grouped GEMM launch for callers that cannot
+// allocate device memory.
+//
+// Some callers have no way to obtain a device buffer for the launch's scratch
+// (the per-CTA tensor-map slots of the tensor-core path): a plugin inside a
+// host process whose framework owns every byte of device memory, code that
+// launches while a CUDA graph is being captured (cudaMalloc is not permitted
+// there), or a real-time launch path that must never block in the driver's
+// allocator.  This entry point takes its scratch from a fixed array compiled
+// into the library instead, so it allocates nothing and frees nothing.
+//
+// The array is a file-scope __device__ object: every GPU that loads this
+// library holds kNoAllocScratchBytes of it until the process exits.  In host
+// code its name is only a host-side stand-in, never a device address, so the
+// device address is looked up once per device (cudaGetSymbolAddress, with that
+// device current) and that address is what the kernels receive.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+
+#include "../../include/moe_gemm_b200.h"
+
+namespace {
+
+// Largest scratch one launch may use: grid x tensor-map slots x 256 bytes.
+// 1 MiB covers a 148-SM B200 (at most 148 x 13 x 256 = 492,544 bytes) with
+// room for devices of up to 256 SMs.
+constexpr size_t kNoAllocScratchBytes = MGB_NOALLOC_SCRATCH_BYTES;
+
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 128;
+std::mutex g_setup_mutex;
+void* g_scratch_address[kMaxDevices] = {};
+
+// Resolves the device address of g_noalloc_scratch for the current device,
+// once per device.  Returns nullptr when the lookup fails.
+void* scratch_address(int* device_out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  *device_out = dev;
+  std::lock_guard<std::mutex> lock(g_setup_mutex);
+  if (g_scratch_address[dev] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (err != cudaSuccess || ptr == nullptr) return nullptr;
+    g_scratch_address[dev] = ptr;
+  }
+  return g_scratch_address[dev];
+}
+
+}  // namespace
+
+extern "C" {
+
+int grouped_gemm_launch_noalloc(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs,
+                                const int32_t* dims, const int64_t* strides, int32_t problem_count,
+                                int32_t homogeneous, int64_t m, int64_t n, int64_t k, int32_t dtype,
+                                int32_t precision, int32_t operands_tma_aligned, const mgb_tile_config* config,
+                                void* stream, mgb_launch_info* info) {
+  int sm_count = 0, dev = -1;
+  void* scratch = scratch_address(&dev);
+  if (scratch == nullptr) return MGB_ERR_CUDA;
+  if (cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return MGB_ERR_CUDA;
+  // The launch never needs more than grouped_gemm_scratch_bytes() for this
+  // device; refuse a device whose need exceeds the fixed array.
+  if (grouped_gemm_scratch_bytes(problem_count, sm_count) > kNoAllocScratchBytes) return MGB_ERR_SCRATCH;
+  return grouped_gemm_launch(a_ptrs, b_ptrs, c_ptrs, dims, strides, problem_count, homogeneous, m, n, k, dtype,
+                             precision, operands_tma_aligned, config, scratch, kNoAllocScratchBytes, stream, info);
+}
+
+}  // extern "C"

@@ -29,6 +29,7 @@ STATUS_SCRATCH = 4
 EXPORTED_SYMBOLS = (
     "grouped_gemm_scratch_bytes",
     "grouped_gemm_launch",
+    "grouped_gemm_launch_noalloc",
     "matmul_launch",
     "read_and_clear_error_word",
     "mgb_set_debug",
@@ -103,6 +104,12 @@ def _declare(lib) -> None:
         ctypes.POINTER(TileConfig), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
     ]
     lib.grouped_gemm_launch.restype = ctypes.c_int
+    lib.grouped_gemm_launch_noalloc.argtypes = [
+        c_i64p, c_i64p, c_i64p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+        ctypes.POINTER(TileConfig), ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
+    ]
+    lib.grouped_gemm_launch_noalloc.restype = ctypes.c_int
     lib.matmul_launch.argtypes = [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
@@ -183,6 +190,29 @@ def grouped_launch(
         int(scratch_nbytes), stream, ctypes.byref(info),
     )
     _check(status, "grouped_gemm_launch")
+    return info
+
+
+# Size of the library's fixed scratch array (MGB_NOALLOC_SCRATCH_BYTES in the header).
+NOALLOC_SCRATCH_BYTES = 1 << 20
+
+
+def grouped_launch_noalloc(
+    a_ptrs: int, b_ptrs: int, c_ptrs: int, dims: int, strides: int, problem_count: int, homogeneous: bool,
+    m: int, n: int, k: int, dtype: str, precision: str, tma_aligned: bool, config, stream: int,
+) -> LaunchInfo:
+    """grouped_gemm_launch_noalloc: the grouped launch for callers that cannot
+    allocate device memory (its scratch is a fixed array inside the library).
+    The first call on a device must come before any stream capture; calls that
+    overlap on the GPU race on the shared array."""
+    info = LaunchInfo()
+    cfg = tile_config(config)
+    status = load().grouped_gemm_launch_noalloc(
+        a_ptrs, b_ptrs, c_ptrs, dims, strides, int(problem_count), int(bool(homogeneous)), int(m), int(n), int(k),
+        DTYPE_CODES[dtype], PRECISION_CODES[precision], int(bool(tma_aligned)), ctypes.byref(cfg), stream,
+        ctypes.byref(info),
+    )
+    _check(status, "grouped_gemm_launch_noalloc")
     return info
 
 
