@@ -56,6 +56,12 @@ def parse_args(argv=None):
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--skip-cpu-baseline", action="store_true")
     p.add_argument("--m-values", type=str, default=",".join(map(str, M_VALUES)))
+    # Profiling / diagnosis knobs (defaults give the benchmark workload).
+    p.add_argument("--parallel", type=str, default="EP,TP", help="subset of EP,TP to build and launch")
+    p.add_argument("--config", type=str, default=None,
+                   help="block_m,block_n: fixed KernelConfig instead of autotuning (profiling)")
+    p.add_argument("--expert-limit", type=int, default=None,
+                   help="at most this many experts per workspace (smaller cases for ncu captures)")
     return p.parse_args(argv)
 
 
@@ -151,8 +157,8 @@ def expert_weight(expert: int, device):
     return w.mul_(1.0 / math.sqrt(HIDDEN)).to(torch.bfloat16)
 
 
-def build_rank(rank: int, m_values, device):
-    """Per-rank tensors and the 14 grouped workspaces of one step."""
+def build_rank(rank: int, m_values, device, parallel=("EP", "TP"), expert_limit=None):
+    """Per-rank tensors and the grouped workspaces of one step (14 by default)."""
     import torch
 
     from kernels import workspace_from_tensors
@@ -160,37 +166,53 @@ def build_rank(rank: int, m_values, device):
 
     ep = rank_plan("W1", "EP", rank, PARALLEL, EXPERTS, FFN, HIDDEN)
     tp = rank_plan("W1", "TP", rank, PARALLEL, EXPERTS, FFN, HIDDEN)
+    ep_experts = ep.experts[:expert_limit] if expert_limit else ep.experts
+    tp_experts = tp.experts[:expert_limit] if expert_limit else tp.experts
     ep_w, tp_w = [], []
     for e in range(EXPERTS):
+        if not ((e in ep_experts and "EP" in parallel) or (e in tp_experts and "TP" in parallel)):
+            continue
         w = expert_weight(e, device)
-        if e in ep.experts:
+        if e in ep_experts and "EP" in parallel:
             ep_w.append(w)
-        tp_w.append(shard_weight(w, tp))
-        if e not in ep.experts:
-            del w
+        if e in tp_experts and "TP" in parallel:
+            tp_w.append(shard_weight(w, tp))
+        del w
     activations, outputs, workspaces = {}, {}, []
     for m in m_values:
         gen = torch.Generator(device=device).manual_seed(7919 * m)
         a_all = torch.randn((EXPERTS, m, HIDDEN), device=device, generator=gen).to(torch.bfloat16)
         activations[m] = a_all
-        c_ep = torch.empty((len(ep.experts), m, 2 * FFN), device=device, dtype=torch.bfloat16)
-        c_tp = torch.empty((EXPERTS, m, tp.local_ffn * 2), device=device, dtype=torch.bfloat16)
+        c_ep = torch.empty((len(ep_experts), m, 2 * FFN), device=device, dtype=torch.bfloat16)
+        c_tp = torch.empty((len(tp_experts), m, tp.local_ffn * 2), device=device, dtype=torch.bfloat16)
         outputs[m] = (c_ep, c_tp)
-        ws_ep = workspace_from_tensors([a_all[e] for e in ep.experts], ep_w, list(c_ep))
-        ws_tp = workspace_from_tensors([a_all[e] for e in tp.experts], tp_w, list(c_tp))
-        for ws in (ws_ep, ws_tp):
-            ws.operation = "gate_up"
-        workspaces.append(("EP", m, ws_ep))
-        workspaces.append(("TP", m, ws_tp))
+        if "EP" in parallel:
+            ws_ep = workspace_from_tensors([a_all[e] for e in ep_experts], ep_w, list(c_ep))
+            ws_ep.operation = "gate_up"
+            workspaces.append(("EP", m, ws_ep))
+        if "TP" in parallel:
+            ws_tp = workspace_from_tensors([a_all[e] for e in tp_experts], tp_w, list(c_tp))
+            ws_tp.operation = "gate_up"
+            workspaces.append(("TP", m, ws_tp))
     return ep, tp, activations, outputs, workspaces
 
 
-def graph_of_steps(workspaces, steps: int, stream):
-    """One CUDA graph holding `steps` passes of the 14 launches, with an event
-    pair around every launch (read after the timed replay)."""
-    import torch
+FIXED_CONFIG = None  # set by --config: launches use it instead of the autotuned winner
 
+
+def launch(ws) -> None:
     from kernels import launch_grouped
+
+    if FIXED_CONFIG is None:
+        launch_grouped(ws)
+    else:
+        launch_grouped(ws, config=FIXED_CONFIG, autotune=False)
+
+
+def graph_of_steps(workspaces, steps: int, stream):
+    """One CUDA graph holding `steps` passes of the step's launches, with an
+    event pair around every launch (read after the timed replay)."""
+    import torch
 
     events = []
     graph = torch.cuda.CUDAGraph()
@@ -200,7 +222,7 @@ def graph_of_steps(workspaces, steps: int, stream):
                 start = torch.cuda.Event(enable_timing=True, external=True)
                 end = torch.cuda.Event(enable_timing=True, external=True)
                 start.record()
-                launch_grouped(ws)
+                launch(ws)
                 end.record()
                 events.append((par, m, start, end))
     return graph, events
@@ -355,11 +377,16 @@ def main(argv=None) -> int:
     m_values = [int(v) for v in args.m_values.split(",")]
     peaks, peak_source = load_peaks()
 
-    from kernels import check_device_errors, launch_grouped
+    from kernels import KernelConfig, check_device_errors
     from moe_parallel import gemm_flops
 
+    global FIXED_CONFIG
+    if args.config:
+        bm, bn = (int(v) for v in args.config.split(","))
+        FIXED_CONFIG = KernelConfig(bm, bn, 64, 8, 4, 4)
+    parallel = tuple(p for p in ("EP", "TP") if p in args.parallel.split(","))
     progress("building rank tensors")
-    ep, tp, activations, outputs, workspaces = build_rank(rank, m_values, device)
+    ep, tp, activations, outputs, workspaces = build_rank(rank, m_values, device, parallel, args.expert_limit)
     progress("autotuning the first launch of each workspace")
     rank_flops = sum(gemm_flops(*ws.shapes[0]) * ws.problem_count for _, _, ws in workspaces)
     stream = torch.cuda.Stream(device)
@@ -367,7 +394,7 @@ def main(argv=None) -> int:
     with torch.cuda.stream(stream):
         for par, m, ws in workspaces:  # first call: autotune (eager, untimed)
             progress(f"autotune {par} M_e={m}")
-            launch_grouped(ws)
+            launch(ws)
             progress(f"  -> {ws.config} {ws.launch_info}")
     stream.synchronize()
     check_device_errors(local_rank)
@@ -464,7 +491,7 @@ def main(argv=None) -> int:
             for m in m_values:
                 activations[m].copy_(host_a[m], non_blocking=True)
                 for ws in by_m[m]:
-                    launch_grouped(ws)
+                    launch(ws)
                 host_c[m][0].copy_(outputs[m][0], non_blocking=True)
                 host_c[m][1].copy_(outputs[m][1], non_blocking=True)
         e_end.record(stream)
@@ -476,7 +503,10 @@ def main(argv=None) -> int:
     check_device_errors(local_rank)
 
     progress("verification")
-    verification = verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_values)
+    if parallel == ("EP", "TP") and not args.expert_limit:
+        verification = verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_values)
+    else:
+        verification = {"skipped": "partial workload (--parallel / --expert-limit)"}
     launches = torch.tensor([len(workspaces) * args.steps], device=device, dtype=torch.int64)
     if world > 1:
         dist.all_reduce(launches)

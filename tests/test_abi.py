@@ -1,0 +1,94 @@
+"""The C-ABI library loads and exports every symbol include/*.h declares.
+
+No compute calls here: these run without a GPU.  Only the pure host entry
+points (status strings, scratch sizing, ABI version, debug knobs) are called.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from kernels import _native
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+
+
+def declared_functions() -> set[str]:
+    names = set()
+    for header in HEADERS:
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        for match in re.finditer(r"^\s*(?:const\s+)?[A-Za-z_][\w\s\*]*?\b([A-Za-z_]\w*)\s*\(", text, flags=re.M):
+            name = match.group(1)
+            if name not in {"if", "while", "for", "switch", "return", "sizeof"}:
+                names.add(name)
+    return names
+
+
+def test_header_exists_and_declares_the_boundary():
+    assert HEADERS, "include/*.h missing"
+    names = declared_functions()
+    assert {"grouped_gemm_launch", "matmul_launch", "read_and_clear_error_word"} <= names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _native.load()
+    names = declared_functions()
+    assert names == set(_native.EXPORTED_SYMBOLS)
+    for name in sorted(names):
+        assert hasattr(lib, name), f"{name} not exported"
+    exported = subprocess.run(["nm", "-D", "--defined-only", str(_native.LIBRARY_PATH)], capture_output=True,
+                              text=True, check=True).stdout
+    for name in names:
+        assert re.search(rf"\sT\s{name}$", exported, flags=re.M), f"{name} is not a defined text symbol"
+
+
+def test_library_is_built_for_sm_100a():
+    out = subprocess.run(["cuobjdump", "--list-elf", str(_native.LIBRARY_PATH)], capture_output=True, text=True)
+    if out.returncode != 0:
+        pytest.skip("cuobjdump unavailable")
+    assert "sm_100a" in out.stdout
+
+
+def test_host_only_entry_points():
+    lib = _native.load()
+    assert lib.mgb_abi_version() == 1
+    assert _native.status_text(_native.STATUS_OK) == "ok"
+    assert "scratch" in _native.status_text(_native.STATUS_SCRATCH)
+    assert _native.status_text(99) == "unknown status"
+    # 16 tensor-map slots x 2 maps x 128 bytes per CTA, one CTA per SM.
+    assert _native.scratch_bytes(256, 148) == 148 * 16 * 256
+    assert _native.scratch_bytes(1, 0) == 16 * 256
+    assert _native.scratch_bytes(256, 256) <= _native.NOALLOC_SCRATCH_BYTES
+    _native.set_debug(1000, 1)
+    _native.set_debug(0, 0)
+
+
+def test_invalid_arguments_are_rejected_before_any_device_call():
+    lib = _native.load()
+    cfg = _native.TileConfig(16, 128, 64, 4, 4, 3, 1)
+    info = _native.LaunchInfo()
+    # null tables / non-positive problem count / bad dtype: MGB_ERR_INVALID without touching CUDA
+    status = lib.grouped_gemm_launch(None, None, None, None, None, 0, 1, 1, 1, 1, 1, 0, 1, ctypes.byref(cfg), None,
+                                     0, None, ctypes.byref(info))
+    assert status == _native.STATUS_INVALID
+    status = lib.grouped_gemm_launch(None, None, None, None, None, 4, 1, 1, 1, 1, 7, 0, 1, ctypes.byref(cfg), None,
+                                     0, None, ctypes.byref(info))
+    assert status == _native.STATUS_INVALID
+    status = lib.matmul_launch(None, None, None, -1, 1, 1, 1, 1, 1, 1, 1, 1, 1, 0, ctypes.byref(cfg), None,
+                               ctypes.byref(info))
+    assert status == _native.STATUS_INVALID
+
+
+def test_missing_library_fails_loudly(tmp_path, monkeypatch):
+    monkeypatch.setattr(_native, "LIBRARY_PATH", tmp_path / "absent.so")
+    monkeypatch.setattr(_native, "_lib", None)
+    monkeypatch.setattr(_native, "_load_error", None)
+    with pytest.raises(RuntimeError, match="missing"):
+        _native.load()
+    assert not _native.available()

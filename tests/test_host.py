@@ -1,0 +1,122 @@
+"""Host-side logic of the kernels package that needs no GPU.
+
+Argument validation mirrors the reference's errors (ValueError for shapes,
+devices and dtypes, kernels/matmul.py:318-329; RuntimeError when no CUDA
+runtime is present, kernels/grouped_gemm.py:626-627), the TMA alignment
+verdict, and the EP/TP shard plans with their reassembly.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+from kernels import KernelConfig, launch_grouped, launch_matmul  # noqa: E402
+from kernels.grouped_gemm import GroupedWorkspace, _shape_signature, operands_tma_aligned  # noqa: E402
+from kernels.matmul import _validate_matrices, dtype_name  # noqa: E402
+from moe_parallel import (  # noqa: E402
+    assemble_w2_tp,
+    assemble_w13_tp,
+    ep_owner,
+    moe_shapes,
+    rank_plan,
+    shard_weight,
+)
+
+NO_CUDA = not torch.cuda.is_available()
+
+
+def test_validate_matrices_errors():
+    a, b, c = torch.zeros(2, 3), torch.zeros(3, 4), torch.zeros(2, 4)
+    with pytest.raises(ValueError, match="matrices"):
+        _validate_matrices(a[0], b, c)
+    with pytest.raises(ValueError, match="shape mismatch"):
+        _validate_matrices(a, torch.zeros(4, 4), c)
+    with pytest.raises(ValueError, match="CUDA"):
+        _validate_matrices(a, b, c)
+    with pytest.raises(ValueError):
+        dtype_name(torch.int8)
+
+
+@pytest.mark.skipif(not NO_CUDA, reason="checks the CPU-only error path")
+def test_launches_need_cuda():
+    a, b, c = torch.zeros(2, 3), torch.zeros(3, 4), torch.zeros(2, 4)
+    with pytest.raises(RuntimeError):
+        launch_matmul(a, b, c)
+    ws = _cpu_workspace([(2, 8, 8), (2, 8, 8)])
+    with pytest.raises(RuntimeError):
+        launch_grouped(ws)
+
+
+def _cpu_workspace(shapes, a=None, b=None):
+    a = a or [torch.zeros(m, k, dtype=torch.bfloat16) for m, k, _ in shapes]
+    b = b or [torch.zeros(k, n, dtype=torch.bfloat16) for _, k, n in shapes]
+    c = [torch.zeros(m, n, dtype=torch.bfloat16) for m, _, n in shapes]
+    return GroupedWorkspace(a, b, c, None, None, None, None, None, tuple(shapes), KernelConfig(16, 64, 32, 4, 2, 2),
+                            _shape_signature(shapes), 0, 148, 0, True)
+
+
+def test_tma_alignment_verdict():
+    ok = _cpu_workspace([(16, 64, 128)] * 2)
+    assert operands_tma_aligned(ok)
+    odd_pitch = _cpu_workspace([(17, 13, 31)])  # 26-byte rows
+    assert not operands_tma_aligned(odd_pitch)
+    base = torch.zeros(16, 129, dtype=torch.bfloat16)
+    shifted = _cpu_workspace([(16, 64, 128)], a=[base[:, 1:65]])  # base + 2 bytes
+    assert not operands_tma_aligned(shifted)
+    strided = _cpu_workspace([(16, 64, 64)], b=[torch.zeros(64, 128, dtype=torch.bfloat16)[:, ::2]])
+    assert not operands_tma_aligned(strided)
+
+
+def test_shape_signature_is_stable_and_discriminates():
+    assert _shape_signature([(1, 2, 3)]) == _shape_signature([(1, 2, 3)])
+    assert _shape_signature([(1, 2, 3)]) != _shape_signature([(1, 3, 2)])
+    assert 0 <= _shape_signature([(7, 7, 7)] * 100) < 2**31
+
+
+def test_rank_plans_cover_the_layer():
+    e, f, h, p = 8, 12, 5, 4
+    ep_experts = [x for r in range(p) for x in rank_plan("W1", "EP", r, p, e, f, h).experts]
+    assert ep_experts == list(range(e))
+    assert all(ep_owner(x, p, e) == x // 2 for x in range(e))
+    tp_slices = [rank_plan("W2", "TP", r, p, e, f, h).ffn_slice for r in range(p)]
+    assert tp_slices == [(0, 3), (3, 6), (6, 9), (9, 12)]
+    with pytest.raises(ValueError):
+        rank_plan("W1", "EP", 4, p, e, f, h)
+
+
+@pytest.mark.parametrize("p", [1, 2, 4])
+def test_tp_shards_reassemble_the_global_product(p):
+    """[gate_r | up_r] slices and W2 partial sums rebuild the full-layer product
+    exactly (integer-valued inputs keep float64 sums exact)."""
+    rng = np.random.default_rng(p)
+    e, f, h, m = 4, 8, 6, 5
+    a = rng.integers(-3, 4, size=(m, h)).astype(np.float64)
+    w13 = rng.integers(-3, 4, size=(h, 2 * f)).astype(np.float64)
+    act = rng.integers(-3, 4, size=(m, f)).astype(np.float64)
+    w2 = rng.integers(-3, 4, size=(f, h)).astype(np.float64)
+    w13_outs, w2_parts = [], []
+    for r in range(p):
+        plan13 = rank_plan("W1", "TP", r, p, e, f, h)
+        plan2 = rank_plan("W2", "TP", r, p, e, f, h)
+        local13 = shard_weight(w13, plan13)
+        local2 = shard_weight(w2, plan2)
+        assert local13.shape == (h, 2 * f // p) and local2.shape == (f // p, h)
+        assert [(m,) + local13.shape] == [moe_shapes("W1", "TP", m, h, f, e, p)[0]]
+        w13_outs.append(a @ local13)
+        start, stop = plan2.ffn_slice
+        w2_parts.append(act[:, start:stop] @ local2)
+    np.testing.assert_array_equal(assemble_w13_tp(w13_outs, p), a @ w13)
+    np.testing.assert_array_equal(assemble_w2_tp(w2_parts), act @ w2)
+    ep = rank_plan("W1", "EP", 0, p, e, f, h)
+    assert shard_weight(w13, ep) is w13
+
+
+def test_torch_tensors_shard_too():
+    w = torch.arange(24.0).reshape(3, 8)
+    plan = rank_plan("W1", "TP", 1, 2, 2, 4, 3)
+    local = shard_weight(w, plan)
+    assert torch.equal(local, torch.cat((w[:, 2:4], w[:, 6:8]), 1))
+    assert local.is_contiguous()
