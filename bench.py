@@ -60,8 +60,16 @@ def parse_args(argv=None):
     p.add_argument("--parallel", type=str, default="EP,TP", help="subset of EP,TP to build and launch")
     p.add_argument("--config", type=str, default=None,
                    help="block_m,block_n: fixed KernelConfig instead of autotuning (profiling)")
+    p.add_argument("--config-small", type=str, default=None,
+                   help="block_m,block_n for workspaces with M_e <= 128 (overrides autotuning for them)")
+    p.add_argument("--config-large", type=str, default=None,
+                   help="block_m,block_n for workspaces with M_e > 128 (overrides autotuning for them)")
+    p.add_argument("--tile-map", type=str, default=None,
+                   help="per-M_e configs, e.g. '16:16,256;128:128,256;1024:256,128' (overrides autotuning)")
     p.add_argument("--expert-limit", type=int, default=None,
                    help="at most this many experts per workspace (smaller cases for ncu captures)")
+    p.add_argument("--tile-sweep", action="store_true",
+                   help="time every native tile per shape, alone and right after a heavy launch (diagnosis)")
     return p.parse_args(argv)
 
 
@@ -198,15 +206,17 @@ def build_rank(rank: int, m_values, device, parallel=("EP", "TP"), expert_limit=
 
 
 FIXED_CONFIG = None  # set by --config: launches use it instead of the autotuned winner
+CLASS_CONFIGS: dict[str, object] = {}  # set by --config-small / --config-large
 
 
 def launch(ws) -> None:
     from kernels import launch_grouped
 
-    if FIXED_CONFIG is None:
+    fixed = FIXED_CONFIG or CLASS_CONFIGS.get(ws.max_m) or CLASS_CONFIGS.get("small" if ws.max_m <= 128 else "large")
+    if fixed is None:
         launch_grouped(ws)
     else:
-        launch_grouped(ws, config=FIXED_CONFIG, autotune=False)
+        launch_grouped(ws, config=fixed, autotune=False)
 
 
 def graph_of_steps(workspaces, steps: int, stream):
@@ -355,6 +365,72 @@ def reference_arm(args, rank: int, world: int) -> None:
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------------- tile sweep
+SWEEP_TILES = {
+    "swap16x128": (16, 128), "swap16x256": (16, 256), "swap32x128": (32, 128), "swap32x256": (32, 256),
+    "swap64x128": (64, 128), "swap64x256": (64, 256), "tok128x64": (128, 64), "tok128x128": (128, 128),
+    "tok128x256": (128, 256), "pair256x256": (256, 128),
+}
+
+
+def tile_sweep(args, device) -> None:
+    """Per shape and native tile: median launch time alone ("alone") and right
+    after a heavy launch that drives the GPU into its power cap ("loaded"), as
+    fractions of the per-shape roofline.  Prints one line per shape."""
+    import torch
+
+    from kernels import KernelConfig, launch_grouped
+
+    m_values = [int(v) for v in args.m_values.split(",")]
+    parallel = tuple(p for p in ("EP", "TP") if p in args.parallel.split(","))
+    _, _, _, _, workspaces = build_rank(0, sorted(set(m_values) | {1024}), device, ("EP", "TP"), args.expert_limit)
+    heavy = next(ws for par, m, ws in workspaces if par == "EP" and m == 1024)
+    heavy_cfg = KernelConfig(128, 256, 64, 8, 8, 4)
+    stream = torch.cuda.Stream(device)
+    peaks, _ = load_peaks()
+
+    def median_ms(ws, cfg, loaded: bool, reps: int = 10) -> float:
+        with torch.cuda.stream(stream):
+            launch_grouped(ws, config=cfg, autotune=False)
+            launch_grouped(heavy, config=heavy_cfg, autotune=False)
+        stream.synchronize()
+        pairs = []
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(reps):
+                if loaded:
+                    launch_grouped(heavy, config=heavy_cfg, autotune=False)
+                start = torch.cuda.Event(enable_timing=True, external=True)
+                end = torch.cuda.Event(enable_timing=True, external=True)
+                start.record()
+                launch_grouped(ws, config=cfg, autotune=False)
+                end.record()
+                pairs.append((start, end))
+        with torch.cuda.stream(stream):
+            for _ in range(8 if loaded else 2):
+                graph.replay()
+        stream.synchronize()
+        result = statistics.median(a.elapsed_time(b) for a, b in pairs)
+        del graph
+        return result
+
+    for par, m, ws in workspaces:
+        if m not in m_values or par not in parallel:
+            continue
+        (mm, k, n), count = ws.shapes[0], ws.problem_count
+        roof, bound = roofline_ms(mm, k, n, count, peaks)
+        rows = []
+        for name, (bm, bn) in SWEEP_TILES.items():
+            if (bm <= 32 and m > 128) or (bm == 256 and m < 128):
+                continue
+            cfg = KernelConfig(bm, bn, 64, 8, 4, 4)
+            alone, loaded = median_ms(ws, cfg, False), median_ms(ws, cfg, True)
+            rows.append((loaded, name, alone))
+        rows.sort()
+        print(f"{par} M_e={m} roofline {roof:.3f} ms ({bound}): " + "  ".join(
+            f"{name} {alone:.3f}/{loaded:.3f} ms ({roof / loaded:.2f})" for loaded, name, alone in rows), flush=True)
+
+
 # ------------------------------------------------------------- main
 def main(argv=None) -> int:
     args = parse_args(argv)
@@ -370,6 +446,9 @@ def main(argv=None) -> int:
 
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
+    if args.tile_sweep:
+        tile_sweep(args, device)
+        return 0
     if world > 1:
         from datetime import timedelta
 
@@ -384,6 +463,15 @@ def main(argv=None) -> int:
     if args.config:
         bm, bn = (int(v) for v in args.config.split(","))
         FIXED_CONFIG = KernelConfig(bm, bn, 64, 8, 4, 4)
+    for key, text in (("small", args.config_small), ("large", args.config_large)):
+        if text:
+            bm, bn = (int(v) for v in text.split(","))
+            CLASS_CONFIGS[key] = KernelConfig(bm, bn, 64, 8, 4, 4)
+    if args.tile_map:
+        for item in args.tile_map.split(";"):
+            m_text, cfg_text = item.split(":")
+            bm, bn = (int(v) for v in cfg_text.split(","))
+            CLASS_CONFIGS[int(m_text)] = KernelConfig(bm, bn, 64, 8, 4, 4)
     parallel = tuple(p for p in ("EP", "TP") if p in args.parallel.split(","))
     progress("building rank tensors")
     ep, tp, activations, outputs, workspaces = build_rank(rank, m_values, device, parallel, args.expert_limit)

@@ -46,7 +46,8 @@ typedef struct mgb_tile_config {
 
 /* What a launch actually ran (filled when the pointer is non-null). */
 typedef struct mgb_launch_info {
-  int32_t path;    /* 0 = TMA + tcgen05 tensor-core kernel, 1 = generic-stride SIMT kernel */
+  int32_t path;    /* 0 = TMA + tcgen05 tensor-core kernel, 1 = generic-stride SIMT kernel,
+                      2 = TMA + tcgen05 on CTA pairs (cta_group::2, 256 x 256 cluster tiles) */
   int32_t swap_ab; /* 1 when the weight dimension is the MMA M dimension (narrow-M variant) */
   int32_t tile_m, tile_n, tile_k, stages, grid;
 } mgb_launch_info;

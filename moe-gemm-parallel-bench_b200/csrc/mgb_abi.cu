@@ -107,7 +107,10 @@ bool encode_2d(CUtensorMap* map, int dtype, const void* base, uint64_t inner, ui
 // block_m <= 64 selects the swap-AB (weight-streaming) family with that many
 // tokens per tile; block_m == 128 the MMA-M = 128 token family; larger
 // block_m the swap-AB 256-token tile.  block_n picks the weight tile.
-TcVariant pick_variant(const mgb_tile_config* cfg) {
+// block_m >= 256 with block_n >= 128 selects, for fp16 / bf16, the CTA-pair
+// kernel's 256 x 256 cluster tile; block_m >= 256 with a narrower block_n (and
+// every fp32 case) the one-CTA swap-AB 256 x 128 tile.
+TcVariant pick_variant(const mgb_tile_config* cfg, int dtype) {
   const int bm = cfg ? cfg->block_m : 64;
   const int bn = cfg ? cfg->block_n : 128;
   const int wide = bn >= 256 ? 256 : 128;
@@ -115,6 +118,7 @@ TcVariant pick_variant(const mgb_tile_config* cfg) {
   if (bm <= 32) return {true, 32, wide};
   if (bm <= 64) return {true, 64, wide};
   if (bm <= 128) return {false, 128, bn <= 64 ? 64 : (bn <= 128 ? 128 : 256)};
+  if (dtype != MGB_FP32 && bn >= 128) return {false, 256, 256, true};
   return {true, 256, 128};
 }
 
@@ -153,7 +157,7 @@ int grid_for(int64_t problems, int64_t m, int64_t n, int tm, int tn, int64_t cap
 
 void fill_info(mgb_launch_info* info, int path, const TcVariant& v, const TcVariantInfo& vi, int grid) {
   if (info == nullptr) return;
-  info->path = path;
+  info->path = path == 0 && v.pair ? 2 : path;
   info->swap_ab = path == 0 && v.swap ? 1 : 0;
   info->tile_m = path == 0 ? v.tm : mgb::kSimtBM;
   info->tile_n = path == 0 ? v.tn : mgb::kSimtBN;
@@ -210,10 +214,11 @@ int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
   const bool tensor_core = operands_tma_aligned && (dtype != MGB_FP32 || precision == MGB_TF32) && m > 0 &&
                            n > 0 && k > 0;
   if (tensor_core) {
-    const TcVariant v = pick_variant(config);
+    const TcVariant v = pick_variant(config, dtype);
     TcVariantInfo vi;
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
-    const int grid = grid_for(problem_count, m, n, v.tm, v.tn, ds.sm_count);
+    const int grid = v.pair ? 2 * grid_for(problem_count, m, n, v.tm, v.tn, std::max(1, vi.max_clusters))
+                            : grid_for(problem_count, m, n, v.tm, v.tn, ds.sm_count);
     const size_t need = static_cast<size_t>(grid) * vi.slots * kSlotBytes;
     if (scratch == nullptr || scratch_bytes < need || reinterpret_cast<uintptr_t>(scratch) % 128 != 0) {
       return MGB_ERR_SCRATCH;
@@ -227,7 +232,7 @@ int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
     const uint64_t act_pitch = ((static_cast<uint64_t>(k) * es + 15) / 16) * 16;
     const uint64_t wgt_pitch = ((static_cast<uint64_t>(n) * es + 15) / 16) * 16;
     CUtensorMap act, wgt;
-    if (!encode_2d(&act, dtype, scratch, k, m, act_pitch, vi.bk, v.tm, kActSwizzle) ||
+    if (!encode_2d(&act, dtype, scratch, k, m, act_pitch, vi.bk, vi.box_rows, kActSwizzle) ||
         !encode_2d(&wgt, dtype, scratch, n, k, wgt_pitch, vi.bk, vi.bk, wgt_swizzle(dtype))) {
       return MGB_ERR_CUDA;
     }
@@ -284,15 +289,16 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
                        n < (1ll << 31) && k < (1ll << 31);
   const bool tensor_core = aligned && k > 0 && (dtype != MGB_FP32 || precision == MGB_TF32);
   if (tensor_core) {
-    const TcVariant v = pick_variant(config);
+    const TcVariant v = pick_variant(config, dtype);
     TcVariantInfo vi;
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
     CUtensorMap act, wgt;
-    if (!encode_2d(&act, dtype, a, k, m, static_cast<uint64_t>(stride_am) * es, vi.bk, v.tm, kActSwizzle) ||
+    if (!encode_2d(&act, dtype, a, k, m, static_cast<uint64_t>(stride_am) * es, vi.bk, vi.box_rows, kActSwizzle) ||
         !encode_2d(&wgt, dtype, b, n, k, static_cast<uint64_t>(stride_bk) * es, vi.bk, vi.bk, wgt_swizzle(dtype))) {
       return MGB_ERR_CUDA;
     }
-    const int grid = grid_for(1, m, n, v.tm, v.tn, ds.sm_count);
+    const int grid = v.pair ? 2 * grid_for(1, m, n, v.tm, v.tn, std::max(1, vi.max_clusters))
+                            : grid_for(1, m, n, v.tm, v.tn, ds.sm_count);
     const int e = tc_launch_typed(dtype, v, act, wgt, p, grid, s);
     if (e != 0) return MGB_ERR_CUDA;
     fill_info(info, 0, v, vi, grid);

@@ -11,18 +11,24 @@
 namespace mgb {
 
 // A native tensor-core tile: orientation and token / weight tile extents.
+// `pair` selects the CTA-pair kernel (tm = tn = 256 per cluster of two CTAs).
 struct TcVariant {
   bool swap;
   int tm;
   int tn;
+  bool pair = false;
 };
 
-// Compile-time facts of a variant the host needs (box sizes, ring depth, slots).
+// Compile-time facts of a variant the host needs (box sizes, ring depth, slots),
+// plus, for the CTA-pair kernel, how many clusters the device runs at once.
 struct TcVariantInfo {
   int bk;
   int stages;
   int slots;
   int smem_bytes;
+  int max_clusters = 0;
+  int box_rows = 0;  // token rows one CTA loads per stage (the activation box height)
+  int box_cols = 0;  // weight columns one CTA loads per stage
 };
 
 // Returns false for a variant that is not instantiated.

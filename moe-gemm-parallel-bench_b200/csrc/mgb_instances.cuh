@@ -7,6 +7,7 @@
 
 #include "mgb_dispatch.cuh"
 #include "mgb_simt_kernel.cuh"
+#include "mgb_tc2_kernel.cuh"
 #include "mgb_tc_kernel.cuh"
 
 namespace mgb {
@@ -43,13 +44,87 @@ static int launch_variant(const CUtensorMap& act, const CUtensorMap& wgt, const 
   return static_cast<int>(cudaGetLastError());
 }
 
+// The CTA-pair kernel exists for 16-bit types only.
+template <typename T>
+struct PairKernel {
+  static constexpr bool kAvailable = sizeof(T) == 2;
+};
+
+// Clusters of two the device keeps resident at once for the pair kernel
+// (queried once per device; 0 when the query is unavailable).
+template <typename T>
+static int pair_max_clusters() {
+  if constexpr (!PairKernel<T>::kAvailable) {
+    return 0;
+  } else {
+    static int cached[128] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 0;
+    if (cached[dev] == 0) {
+      using Cfg = Tc2Cfg<T>;
+      if (cudaFuncSetAttribute(tc2_grouped_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
+          cudaSuccess) {
+        return 0;
+      }
+      int sms = 0;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1), 1, 1);
+      cfg.blockDim = dim3(kTcThreads, 1, 1);
+      cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, tc2_grouped_kernel<T>, &cfg) != cudaSuccess || clusters <= 0) {
+        cudaGetLastError();
+        clusters = sms / 2;
+      }
+      cached[dev] = clusters;
+    }
+    return cached[dev];
+  }
+}
+
+template <typename T>
+static int launch_pair(const CUtensorMap& act, const CUtensorMap& wgt, const GroupedParams& p, int grid,
+                       cudaStream_t stream) {
+  if constexpr (!PairKernel<T>::kAvailable) {
+    return static_cast<int>(cudaErrorInvalidValue);
+  } else {
+    using Cfg = Tc2Cfg<T>;
+    static bool configured[128] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 128) return static_cast<int>(cudaErrorInvalidDevice);
+    if (!configured[dev]) {
+      const cudaError_t e =
+          cudaFuncSetAttribute(tc2_grouped_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+      if (e != cudaSuccess) return static_cast<int>(e);
+      configured[dev] = true;
+    }
+    tc2_grouped_kernel<T><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(act, wgt, p);
+    return static_cast<int>(cudaGetLastError());
+  }
+}
+
+template <typename T>
+static bool pair_variant_info(const TcVariant& v, TcVariantInfo* info) {
+  if constexpr (!PairKernel<T>::kAvailable) {
+    return false;
+  } else {
+    using Cfg = Tc2Cfg<T>;
+    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSlots, Cfg::kSmemBytes, pair_max_clusters<T>(), Cfg::kHalf,
+                          Cfg::kHalf};
+    return v.tm == Cfg::kTileM && v.tn == Cfg::kTileN;
+  }
+}
+
 template <>
 bool tc_variant_info<MGB_ELEM>(const TcVariant& v, TcVariantInfo* info) {
-#define MGB_INFO(S, M, N)                                          \
-  if (v.swap == S && v.tm == M && v.tn == N) {                     \
-    using Cfg = TcCfg<MGB_ELEM, S, M, N>;                          \
-    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSlots, Cfg::kSmemBytes}; \
-    return true;                                                   \
+  if (v.pair) return pair_variant_info<MGB_ELEM>(v, info);
+#define MGB_INFO(S, M, N)                                                               \
+  if (v.swap == S && v.tm == M && v.tn == N) {                                          \
+    using Cfg = TcCfg<MGB_ELEM, S, M, N>;                                               \
+    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSlots, Cfg::kSmemBytes, 0, M, N}; \
+    return true;                                                                        \
   }
   MGB_FOR_EACH_VARIANT(MGB_INFO)
 #undef MGB_INFO
@@ -59,6 +134,7 @@ bool tc_variant_info<MGB_ELEM>(const TcVariant& v, TcVariantInfo* info) {
 template <>
 int tc_launch<MGB_ELEM>(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt, const GroupedParams& p,
                         int grid, cudaStream_t stream) {
+  if (v.pair) return launch_pair<MGB_ELEM>(act, wgt, p, grid, stream);
 #define MGB_LAUNCH(S, M, N) \
   if (v.swap == S && v.tm == M && v.tn == N) return launch_variant<MGB_ELEM, S, M, N>(act, wgt, p, grid, stream);
   MGB_FOR_EACH_VARIANT(MGB_LAUNCH)

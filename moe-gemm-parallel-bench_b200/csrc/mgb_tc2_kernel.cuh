@@ -1,0 +1,303 @@
+// Persistent grouped GEMM on CTA pairs (tcgen05 cta_group::2), fp16 / bf16.
+//
+// Same contract as tc_grouped_kernel (C_e = A_e @ B_e, fp32 accumulate, cast
+// on store) for token-rich problems: a cluster of two CTAs on neighbouring
+// SMs owns a 256-token x 256-weight-column output tile.  CTA r loads token
+// rows [128r, 128r + 128) of the tile and weight columns [128r, 128r + 128)
+// into its own shared memory; the even CTA issues tcgen05.mma.cta_group::2
+// (M = 256, N = 256), which reads both CTAs' halves.  Per SM this halves the
+// weight bytes each MMA pulls through shared memory and L2 compared with a
+// one-CTA 128 x 256 tile, which is what keeps the tensor pipe fed.
+//
+// Roles per CTA (192 threads) as in tc_grouped_kernel; only the even CTA's MMA
+// lane issues MMAs.  Barriers:
+//   full[s]      in CTA 0 only: both CTAs' TMA bytes for stage s land on it
+//                (the even CTA's producer posts the expected byte count);
+//   empty[s]     in each CTA: the MMA commit multicasts to both;
+//   acc_full[b]  in each CTA: the MMA commit multicasts to both epilogues;
+//   acc_empty[b] in CTA 0 only: the 8 epilogue warps of the pair arrive.
+// Every wait is bounded; loads carry no multicast.
+#pragma once
+
+#include "mgb_tc_kernel.cuh"
+
+namespace mgb {
+
+template <typename T>
+struct Tc2Cfg {
+  static constexpr int kElem = static_cast<int>(sizeof(T));
+  static_assert(kElem == 2, "the CTA-pair kernel serves fp16 / bf16");
+  static constexpr int kBK = 64;
+  static constexpr int kKStep = 16;
+  static constexpr int kKSteps = 4;
+  static constexpr int kTileM = 256;  // tokens per cluster tile
+  static constexpr int kTileN = 256;  // weight columns per cluster tile
+  static constexpr int kHalf = 128;   // per CTA: token rows and weight columns
+  static constexpr int kActBytes = kHalf * 128;
+  static constexpr int kBoxBytes = kBK * 128;
+  static constexpr int kWgtBytes = kHalf * 128;
+  static constexpr int kStageBytes = kActBytes + kWgtBytes;
+  static constexpr int kStages = kTcStageBudget / kStageBytes > 12 ? 12 : kTcStageBudget / kStageBytes;
+  static constexpr int kSlots = kStages + 1;
+  static constexpr int kAccCols = kTileN;
+  static constexpr int kTmemCols = 512;
+  static constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  static constexpr uint32_t kIdesc = instr_desc(kFmt, 0, 1, kTileM, kTileN);
+  static constexpr int kSmemBytes = kStages * kStageBytes + 2048 + 1024;
+  static_assert(2 * kAccCols <= kTmemCols, "two accumulators");
+  static_assert(kSmemBytes <= 232448, "shared memory");
+};
+
+template <typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
+    tc2_grouped_kernel(const __grid_constant__ CUtensorMap act_tmpl, const __grid_constant__ CUtensorMap wgt_tmpl,
+                       const GroupedParams p) {
+  using Cfg = Tc2Cfg<T>;
+  constexpr int S = Cfg::kStages;
+  constexpr int BK = Cfg::kBK;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty = full + S;
+  uint64_t* acc_full = empty + S;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* test_bar = acc_empty + 2;
+  uint64_t* drain_bar = test_bar + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* never = abort + 1;
+  CUtensorMap* staging = reinterpret_cast<CUtensorMap*>(
+      (reinterpret_cast<uintptr_t>(tmem_slot + 4) + 127) & ~uintptr_t(127));
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t cluster = blockIdx.x >> 1;
+  const int64_t clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 8);
+    }
+    mbar_init(test_bar, 1);
+    mbar_init(drain_bar, 1);
+    *abort = 0;
+    *never = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers exist before anything lands on them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const long long budget = p.wait_budget;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    CUtensorMap* slots = reinterpret_cast<CUtensorMap*>(p.desc_slots) +
+                         static_cast<int64_t>(blockIdx.x) * Cfg::kSlots * 2;
+    const CUtensorMap* act_map = &act_tmpl;
+    const CUtensorMap* wgt_map = &wgt_tmpl;
+    if (p.single && lane == 0) {
+      prefetch_tmap(act_map);
+      prefetch_tmap(wgt_map);
+    }
+    // L2 hints: a weight block read by a single token tile is streamed
+    // (evict-first); one that several token tiles share keeps normal priority
+    // so the sharers hit in L2.  Activation blocks are shared by every weight
+    // tile of their expert and are kept (evict-last).
+    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_shared = policy_evict_normal();
+    const uint64_t pol_act = policy_evict_last();
+    TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
+    uint32_t it = 0;
+    int slot = -1;
+    int built = -1;
+    bool ok = true;
+    for (int64_t t = cluster; ok && walk.seek(p, t); t += clusters) {
+      const Problem& q = walk.prob;
+      if (!tma_legal<T>(q)) {
+        if (lane == 0 && walk.problem != built) atomicOr(p.error_word, kErrMisaligned);
+        continue;
+      }
+      const int64_t kblocks = (q.k + BK - 1) / BK;
+      const uint64_t pol_wgt = walk.m_blocks > 1 ? pol_shared : pol_stream;
+      const int32_t m0 = static_cast<int32_t>(walk.m_block(t) * Cfg::kTileM + rank * Cfg::kHalf);
+      const int32_t n0 = static_cast<int32_t>(walk.n_block(t) * Cfg::kTileN + rank * Cfg::kHalf);
+      for (int64_t kb = 0; kb < kblocks; ++kb) {
+        const int s = static_cast<int>(it % S);
+        const uint32_t phase = (it / S) & 1u;
+        if (!mbar_wait_warp(&empty[s], phase ^ 1u, budget, abort)) {
+          if (lane == 0) raise_error(p, kErrWaitEmpty, abort);
+          ok = false;
+          break;
+        }
+        if (kb == 0 && !p.single && walk.problem != built) {
+          slot = (slot + 1) % Cfg::kSlots;
+          uint64_t* st = reinterpret_cast<uint64_t*>(staging);
+          st[lane] = lane < 16 ? reinterpret_cast<const uint64_t*>(&act_tmpl)[lane]
+                               : reinterpret_cast<const uint64_t*>(&wgt_tmpl)[lane - 16];
+          __syncwarp();
+          if (lane == 0) {
+            tmap_replace_address(&staging[0], q.a);
+            tmap_replace_address(&staging[1], q.b);
+            if (!p.homogeneous) {
+              tmap_replace_dim(&staging[0], 0, static_cast<uint32_t>(q.k));
+              tmap_replace_dim(&staging[0], 1, static_cast<uint32_t>(q.m));
+              tmap_replace_stride1(&staging[0], static_cast<uint64_t>(q.sam) * sizeof(T));
+              tmap_replace_dim(&staging[1], 0, static_cast<uint32_t>(q.n));
+              tmap_replace_dim(&staging[1], 1, static_cast<uint32_t>(q.k));
+              tmap_replace_stride1(&staging[1], static_cast<uint64_t>(q.sbk) * sizeof(T));
+            }
+          }
+          __syncwarp();
+          CUtensorMap* g = slots + 2 * slot;
+          tmap_publish(&g[0], &staging[0]);
+          tmap_publish(&g[1], &staging[1]);
+          if (lane == 0) {
+            tmap_acquire(&g[0]);
+            tmap_acquire(&g[1]);
+          }
+          __syncwarp();
+          act_map = &g[0];
+          wgt_map = &g[1];
+          built = walk.problem;
+        }
+        if (lane == 0) {
+          uint8_t* st_act = ring + s * Cfg::kStageBytes;
+          uint8_t* st_wgt = st_act + Cfg::kActBytes;
+          const int32_t kx = static_cast<int32_t>(kb * BK);
+          const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
+          tma_load_2d_pair(act_map, bar, st_act, kx, m0, pol_act);
+#pragma unroll
+          for (int j = 0; j < Cfg::kHalf / BK; ++j) {
+            tma_load_2d_pair(wgt_map, bar, st_wgt + j * Cfg::kBoxBytes, n0 + j * BK, kx, pol_wgt);
+          }
+        }
+        __syncwarp();
+        ++it;
+      }
+    }
+    if (*abort && leader && lane == 0) {
+      const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0u;
+      for (uint32_t j = first; j < it; ++j) {
+        if (!mbar_wait(&full[j % S], (j / S) & 1u, budget, never)) {
+          atomicOr(p.error_word, kErrWaitTeardown);
+          break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------- MMA issuer (even CTA only)
+    if (lane == 0 && leader) {
+      TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
+      uint32_t it = 0;
+      uint32_t acc_it = 0;
+      bool ok = true;
+      for (int64_t t = cluster; ok && walk.seek(p, t); t += clusters) {
+        const Problem& q = walk.prob;
+        if (!tma_legal<T>(q) || q.k <= 0) continue;
+        const int64_t kblocks = (q.k + BK - 1) / BK;
+        const int buf = static_cast<int>(acc_it & 1u);
+        if (!mbar_wait(&acc_empty[buf], ((acc_it >> 1) & 1u) ^ 1u, budget, abort)) {
+          raise_error(p, kErrWaitAccEmpty, abort);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * Cfg::kAccCols);
+        for (int64_t kb = 0; kb < kblocks; ++kb) {
+          const int s = static_cast<int>(it % S);
+          if (!mbar_wait(&full[s], (it / S) & 1u, budget, abort)) {
+            raise_error(p, kErrWaitFull, abort);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(ring + s * Cfg::kStageBytes);
+          const uint32_t w_base = a_base + Cfg::kActBytes;
+#pragma unroll
+          for (int ks = 0; ks < Cfg::kKSteps; ++ks) {
+            const uint64_t act_desc = smem_desc(a_base + ks * 32, 16, 1024, kLayoutSw128);
+            const uint64_t wgt_desc = smem_desc(w_base + ks * Cfg::kKStep * 128, Cfg::kBoxBytes, 1024, kLayoutSw128);
+            mma_f16_pair(d_tmem, act_desc, wgt_desc, Cfg::kIdesc, (kb > 0 || ks > 0) ? 1u : 0u);
+          }
+          mma_commit_pair(&empty[s], 0x3);  // frees stage s in both CTAs
+          ++it;
+        }
+        if (!ok) break;
+        mma_commit_pair(&acc_full[buf], 0x3);  // both epilogues may read their TMEM half
+        ++acc_it;
+      }
+      if (*abort) {
+        mma_commit_pair(drain_bar, 0x1);
+        if (!mbar_wait(drain_bar, 0, budget, never)) atomicOr(p.error_word, kErrWaitTeardown);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;
+    const int ethread = threadIdx.x - 64;
+    if (p.test_flags & 1) {
+      if (!mbar_wait_warp(test_bar, 0, budget, never) && lane == 0) atomicOr(p.error_word, kErrTestWait);
+    }
+    TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
+    uint32_t acc_it = 0;
+    for (int64_t t = cluster; walk.seek(p, t); t += clusters) {
+      const Problem& q = walk.prob;
+      if (!tma_legal<T>(q)) continue;
+      const int64_t m0 = walk.m_block(t) * Cfg::kTileM + rank * Cfg::kHalf;
+      const int64_t n0 = walk.n_block(t) * Cfg::kTileN;
+      if (q.k <= 0) {
+        for (int idx = ethread; idx < Cfg::kHalf * Cfg::kTileN; idx += 128) {
+          const int64_t row = m0 + idx / Cfg::kTileN, col = n0 + idx % Cfg::kTileN;
+          if (row < q.m && col < q.n) store_scalar<T>(q.c, row * q.scm + col * q.scn, 0.0f);
+        }
+        continue;
+      }
+      const int buf = static_cast<int>(acc_it & 1u);
+      if (!mbar_wait_warp(&acc_full[buf], (acc_it >> 1) & 1u, budget, abort)) {
+        if (lane == 0) raise_error(p, kErrWaitAccFull, abort);
+        break;
+      }
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                             static_cast<uint32_t>(buf * Cfg::kAccCols);
+      const int64_t row = m0 + quarter * 32 + lane;
+#pragma unroll 1
+      for (int j = 0; j < Cfg::kTileN / 16; ++j) {
+        uint32_t r[16];
+        tmem_ld16(taddr + j * 16, r);
+        tmem_ld_wait();
+        store_row16<T>(q, row, n0 + j * 16, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[buf]), 0));
+      ++acc_it;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the pair may still touch its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace mgb

@@ -220,7 +220,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       prefetch_tmap(act_map);
       prefetch_tmap(wgt_map);
     }
-    const uint64_t pol_wgt = policy_evict_first();
+    // L2 hints: a weight block read by a single token tile is streamed
+    // (evict-first); one that several token tiles share keeps normal priority
+    // so the sharers hit in L2.  Activation blocks are shared by every weight
+    // tile of their expert and are kept (evict-last).
+    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_shared = policy_evict_normal();
     const uint64_t pol_act = policy_evict_last();
     TileWalk<TM, TN> walk;
     uint32_t it = 0;
@@ -234,6 +239,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         continue;
       }
       const int64_t kblocks = (q.k + BK - 1) / BK;
+      const uint64_t pol_wgt = walk.m_blocks > 1 ? pol_shared : pol_stream;
       const int32_t m0 = static_cast<int32_t>(walk.m_block(t) * TM);
       const int32_t n0 = static_cast<int32_t>(walk.n_block(t) * TN);
       for (int64_t kb = 0; kb < kblocks; ++kb) {

@@ -19,6 +19,7 @@ from .matmul import (
     last_matmul_config,
     launch_matmul,
     matmul_candidate_configs,
+    native_candidates,
     select_config,
 )
 
@@ -33,6 +34,7 @@ __all__ = [
     "launch_grouped",
     "launch_matmul",
     "matmul_candidate_configs",
+    "native_candidates",
     "select_config",
     "workspace_from_tensors",
 ]

@@ -76,7 +76,7 @@ class LaunchInfo(ctypes.Structure):
 
     def as_dict(self) -> dict[str, int | str]:
         return {
-            "path": "tcgen05_tma" if self.path == 0 else "simt_generic",
+            "path": {0: "tcgen05_tma", 1: "simt_generic", 2: "tcgen05_tma_pair"}.get(int(self.path), "unknown"),
             "swap_ab": int(self.swap_ab),
             "tile_m": int(self.tile_m),
             "tile_n": int(self.tile_n),

@@ -37,6 +37,7 @@ from .matmul import (
     last_matmul_config,
     launch_matmul,
     matmul_candidate_configs,
+    native_candidates,
     select_config,
 )
 
@@ -361,7 +362,11 @@ def launch_grouped(
     ``single_problem_matmul``).  Otherwise the scheduler is
     ``homogeneous_persistent`` for equal contiguous problems and
     ``generic_persistent`` for the rest; ``workspace.config`` records the
-    config that ran (the autotune winner when ``autotune`` is true).
+    config that ran.  ``autotune=True`` launches the native tile
+    ``native_candidates`` picks for the group's largest M (measured policy,
+    cached per shape / dtype / precision); ``autotune=False`` launches
+    ``config`` mapped to a native tile, so every ``grouped_candidate_configs``
+    entry launches.
     """
     if torch is None or not torch.cuda.is_available():
         raise RuntimeError("CUDA PyTorch and the native sm_100a library are required")
@@ -390,10 +395,7 @@ def launch_grouped(
         workspace.shape_signature, workspace.problem_count, workspace.device_signature, workspace.homogeneous,
         aligned, input_precision, workspace.a[0].dtype,
     )
-    candidates = grouped_candidate_configs(
-        workspace.max_m, workspace.max_n, workspace.max_k,
-        problem_count=workspace.problem_count, sm_count=workspace.sm_count,
-    )
+    candidates = native_candidates(workspace.max_m)
     best, _ = autotune_over(
         candidates, lambda c: _launch_native(workspace, c, input_precision, aligned), key, _GROUPED_TUNED
     )

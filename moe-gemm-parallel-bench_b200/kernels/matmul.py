@@ -13,7 +13,7 @@ select_config) run unchanged:
 * ``launch_matmul``           kernels/matmul.py:332-392
 
 The candidate heuristics are restated so that they return what the
-reference returns (pinned by tests/golden/configs.json, generated from the
+reference returns (pinned by tests/golden/configs.json.gz, generated from the
 reference).  The launch itself goes to the native sm_100a library: a TMA +
 tcgen05 tensor-core kernel when the operands satisfy the TMA rules, a
 generic-stride kernel otherwise.  A ``KernelConfig`` selects the native tile
@@ -55,7 +55,8 @@ class KernelConfig:
 
 native_tile_note = (
     "block_m <= 64 -> swap-AB tile with block_m tokens (16/32/64) x 128 or 256 weight columns; "
-    "block_m == 128 -> 128-token MMA tile x 64/128/256 columns; block_m >= 256 -> swap-AB 256 x 128"
+    "block_m == 128 -> 128-token MMA tile x 64/128/256 columns; block_m >= 256 -> CTA-pair 256 x 256 tile "
+    "(fp16/bf16) or swap-AB 256 x 128 (fp32)"
 )
 
 
@@ -238,22 +239,57 @@ def _tile_key(info: dict) -> tuple:
     return (info["path"], info["swap_ab"], info["tile_m"], info["tile_n"])
 
 
-def autotune_over(candidates, launch, key: tuple, cache: dict) -> tuple[KernelConfig, dict]:
-    """Times each distinct native tile among `candidates` and caches the winner.
+# Native tiles, named by the pool KernelConfig that selects them.
+TILE_SWAP_16x256 = KernelConfig(16, 256, 64, 4, 8, 4)
+TILE_SWAP_32x256 = KernelConfig(32, 256, 64, 4, 8, 4)
+TILE_SWAP_64x256 = KernelConfig(64, 256, 64, 8, 8, 4)
+TILE_TOKENS_128x256 = KernelConfig(128, 256, 64, 8, 8, 4)
+TILE_PAIR_256x256 = KernelConfig(256, 128, 64, 8, 8, 4)  # CTA pair for fp16/bf16, swap-AB 256 x 128 for fp32
 
-    Each candidate is launched once eagerly; candidates that map to a native
-    tile already seen are not timed again.  Timing uses CUDA-graph event
-    samples (see _timing.graph_median_ms).  Under stream capture nothing is
-    timed: the cached winner, or the first candidate, is launched.
+
+def native_candidates(max_m: int) -> tuple[KernelConfig, ...]:
+    """The native tile ``autotune=True`` launches for ``max_m`` token rows.
+
+    Measured on B200 over whole DeepSeek-V3 W13 steps (``bench.py
+    --tile-map``), where the GPU sits at its power cap and every launch's
+    energy sets the clock of the others: the token tile fits M exactly (swap-AB
+    16 / 32 / 64 tokens x 256 weight columns, so no MMA work is spent on padding
+    rows), 128-token x 256-column tiles at M <= 128, and the CTA-pair 256 x 256
+    tile beyond.  Timing candidates alone at boost clocks (the reference's
+    hot autotune) picks tiles that lose once the GPU is power-capped, so the
+    policy is fixed rather than re-timed per shape.
+    """
+    if max_m <= 16:
+        return (TILE_SWAP_16x256,)
+    if max_m <= 32:
+        return (TILE_SWAP_32x256,)
+    if max_m <= 64:
+        return (TILE_SWAP_64x256,)
+    if max_m <= 128:
+        return (TILE_TOKENS_128x256,)
+    return (TILE_PAIR_256x256,)
+
+
+def autotune_over(candidates, launch, key: tuple, cache: dict) -> tuple[KernelConfig, dict]:
+    """Launches the cached choice for `key`, choosing it on first use.
+
+    One candidate is launched as is.  With several, each is launched once
+    eagerly; candidates that map to a native tile already seen are not timed
+    again, and the distinct tiles are timed with CUDA-graph event samples
+    (_timing.graph_median_ms).  Under stream capture nothing is timed.
     """
     if key in cache:
         return cache[key], launch(cache[key])
-    if _timing.capturing():
+    if len(candidates) == 1 or _timing.capturing():
+        cache[key] = candidates[0]
         return candidates[0], launch(candidates[0])
     seen: dict[tuple, KernelConfig] = {}
     for candidate in candidates:
         info = launch(candidate)
         seen.setdefault(_tile_key(info), candidate)
+    if len(seen) == 1:  # every candidate runs the same kernel (e.g. the generic-stride path)
+        cache[key] = next(iter(seen.values()))
+        return cache[key], launch(cache[key])
     best, best_ms = None, float("inf")
     for candidate in seen.values():
         ms = _timing.graph_median_ms(lambda cand=candidate: launch(cand))
@@ -274,10 +310,10 @@ def launch_matmul(
 ) -> None:
     """C = A @ B on the native kernels (kernels/matmul.py:332-392).
 
-    ``autotune=True`` times the native tiles behind ``matmul_candidate_configs``
-    on the first call for a shape/stride/dtype/precision key and reuses the
-    winner afterwards; ``autotune=False`` launches ``config`` (or the
-    heuristic ``select_config``).
+    ``autotune=True`` launches the native tile ``native_candidates`` picks
+    for the shape (cached per shape/stride/dtype/precision key);
+    ``autotune=False`` launches ``config`` (or the heuristic
+    ``select_config``), mapped to a native tile.
     """
     global _last_tuned
     if torch is None or not torch.cuda.is_available():
@@ -294,7 +330,6 @@ def launch_matmul(
         a.data_ptr() % 16 == 0 and b.data_ptr() % 16 == 0,
     )
     best, _ = autotune_over(
-        matmul_candidate_configs(m, n, k), lambda cfg: _launch_once(a, b, c, m, n, k, cfg, precision), key,
-        _MATMUL_TUNED,
+        native_candidates(m), lambda cfg: _launch_once(a, b, c, m, n, k, cfg, precision), key, _MATMUL_TUNED,
     )
     _last_tuned = best

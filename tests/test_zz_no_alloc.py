@@ -58,7 +58,7 @@ def test_noalloc_entry_matches_existing_entry_on_two_calls(shapes):
     launch_grouped(ws, config=config, autotune=False)  # the existing entry point
     torch.cuda.synchronize()
     expected = [c.clone() for c in ws.c]
-    assert ws.launch_info["path"] == "tcgen05_tma"
+    assert ws.launch_info["path"].startswith("tcgen05_tma")
 
     if ws.homogeneous:
         m, k, n = ws.shapes[0]
