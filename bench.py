@@ -50,7 +50,7 @@ WORKLOAD = ("DeepSeek-V3 W13 gate+up bf16, P=8 rank shapes: EP 32 x [M_e,7168]@[
 def parse_args(argv=None):
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=100)
+    p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
     p.add_argument("--impl", choices=("native", "reference"), default="native")
     p.add_argument("--e2e-steps", type=int, default=3)
@@ -117,14 +117,14 @@ def roofline_ms(m: int, k: int, n: int, count: int, peaks: dict, sustained: bool
 class ClockSampler:
     """nvidia-smi SM clocks and throttle reasons sampled during the timed region."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: str):
         self.gpu_index = gpu_index
         self.proc = None
-        self.lines: list[str] = []
+        self.window: tuple[float, float] | None = None
 
     def start(self):
         try:
@@ -135,7 +135,13 @@ class ClockSampler:
         except (OSError, ValueError):
             self.proc = None
 
+    def mark(self, begin: float, end: float) -> None:
+        """Wall-clock bounds of the timed region; only samples inside count."""
+        self.window = (begin, end)
+
     def stop(self) -> dict | None:
+        from datetime import datetime
+
         if self.proc is None:
             return None
         self.proc.terminate()
@@ -144,15 +150,26 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        rows = [line.split(", ") for line in out.strip().splitlines() if line.count(",") >= 8]
+        rows = [line.split(", ") for line in out.strip().splitlines() if line.count(",") >= 9]
+        inside = []
+        for r in rows:
+            try:
+                stamp = datetime.strptime(r[0].strip(), "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                continue
+            if self.window is None or self.window[0] <= stamp <= self.window[1]:
+                inside.append(r)
+        rows = inside or rows
         if not rows:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        max_sm = max(float(r[2]) for r in rows if r[2].replace(".", "").isdigit())
+        sm = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        max_sm = max(float(r[3]) for r in rows if r[3].replace(".", "").isdigit())
+        power = [float(r[4]) for r in rows if r[4].replace(".", "").isdigit()]
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        reasons = sorted({name for r in rows for name, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        reasons = sorted({name for r in rows for name, v in zip(names, r[6:10]) if v.strip() == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max_sm, "reasons": reasons,
-                "samples": len(rows)}
+                "power_w_median": statistics.median(power) if power else None, "samples": len(rows),
+                "samples_in_timed_region": len(inside)}
 
 
 # ------------------------------------------------------------- workload
@@ -508,12 +525,14 @@ def main(argv=None) -> int:
     torch.cuda.synchronize(device)
     sampler.start()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall_begin = time.time()
     with torch.cuda.stream(stream):
         start.record(stream)
         for _ in range(args.steps // chunk):
             timed_graph.replay()
         end.record(stream)
     torch.cuda.synchronize(device)
+    sampler.mark(wall_begin, time.time())
     clocks = sampler.stop()
     if world > 1:
         dist.barrier()
