@@ -95,6 +95,15 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
                   int32_t dtype, int32_t precision, const mgb_tile_config* config, void* stream,
                   mgb_launch_info* info);
 
+/* Copies a rows x cols matrix with arbitrary element strides into `dst`, a
+ * row-major buffer with a row pitch of `dst_pitch` elements (elements past
+ * `cols` in each row are left untouched).  The masked single GEMM uses it to
+ * give the tensor-core path operands whose row pitch the TMA cannot address
+ * (e.g. fp32 rows of 127 or 8191 elements).  No counterpart in the reference:
+ * its Triton kernel reads every element through masked loads. */
+int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r, int64_t stride_c, void* dst,
+                  int64_t dst_pitch, int32_t elem_bytes, void* stream);
+
 /* Size of the scratch array compiled into the library for
  * grouped_gemm_launch_noalloc (bytes, per GPU that loads the library). */
 #define MGB_NOALLOC_SCRATCH_BYTES (1u << 20)

@@ -171,9 +171,50 @@ bool valid_dtype(int dtype, int precision) {
          (precision == MGB_IEEE || precision == MGB_TF32);
 }
 
+// dst[r, c] = src[r * stride_r + c * stride_c], one 32-column x 8-row block
+// per CTA iteration (grid-stride); dst writes are coalesced along rows.
+template <typename E>
+__global__ void __launch_bounds__(256) repack_kernel(const E* __restrict__ src, int64_t rows, int64_t cols,
+                                                     int64_t stride_r, int64_t stride_c, E* __restrict__ dst,
+                                                     int64_t pitch) {
+  const int64_t col_blocks = (cols + 31) / 32;
+  const int64_t blocks = ((rows + 7) / 8) * col_blocks;
+  for (int64_t b = blockIdx.x; b < blocks; b += gridDim.x) {
+    const int64_t r = (b / col_blocks) * 8 + threadIdx.y;
+    const int64_t c = (b % col_blocks) * 32 + threadIdx.x;
+    if (r < rows && c < cols) dst[r * pitch + c] = src[r * stride_r + c * stride_c];
+  }
+}
+
 }  // namespace
 
 extern "C" {
+
+int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r, int64_t stride_c, void* dst,
+                  int64_t dst_pitch, int32_t elem_bytes, void* stream) {
+  if (rows < 0 || cols < 0 || dst_pitch < cols || (rows > 0 && cols > 0 && (src == nullptr || dst == nullptr))) {
+    return MGB_ERR_INVALID;
+  }
+  if (elem_bytes != 2 && elem_bytes != 4) return MGB_ERR_INVALID;
+  if (rows == 0 || cols == 0) return MGB_OK;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    return MGB_ERR_CUDA;
+  }
+  const int64_t blocks = ((rows + 7) / 8) * ((cols + 31) / 32);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, 16ll * sms)));
+  const dim3 block(32, 8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (elem_bytes == 2) {
+    repack_kernel<uint16_t><<<grid, block, 0, s>>>(static_cast<const uint16_t*>(src), rows, cols, stride_r, stride_c,
+                                                    static_cast<uint16_t*>(dst), dst_pitch);
+  } else {
+    repack_kernel<uint32_t><<<grid, block, 0, s>>>(static_cast<const uint32_t*>(src), rows, cols, stride_r, stride_c,
+                                                    static_cast<uint32_t*>(dst), dst_pitch);
+  }
+  return cudaGetLastError() == cudaSuccess ? MGB_OK : MGB_ERR_CUDA;
+}
 
 size_t grouped_gemm_scratch_bytes(int32_t problem_count, int32_t sm_count) {
   (void)problem_count;

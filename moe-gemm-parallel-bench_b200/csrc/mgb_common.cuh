@@ -82,8 +82,8 @@ __device__ __forceinline__ int64_t ceil_div64(int64_t a, int64_t b) { return (a 
 // tiles in increasing order, so the walk only ever moves forward: the whole
 // launch costs one pass over the problem table per CTA (the reference scans it
 // the same way, kernels/grouped_gemm.py:426-436).  Tiles inside a problem are
-// ordered M-block fastest, so CTAs that run at the same time share a weight
-// column block in L2.
+// ordered M-block fastest (in bands of 8 M-blocks, see m_block), so CTAs that
+// run at the same time share a weight column block in L2.
 template <int TM, int TN>
 struct TileWalk {
   int problem = -1;
@@ -127,8 +127,27 @@ struct TileWalk {
     return true;
   }
 
-  __device__ __forceinline__ int64_t m_block(int64_t t) const { return (t - first) % m_blocks; }
-  __device__ __forceinline__ int64_t n_block(int64_t t) const { return (t - first) / m_blocks; }
+  // Tiles are rastered in bands of kBand M-blocks: inside a band the M-block
+  // runs fastest, then the N-block.  With at most kBand M-blocks (every MoE
+  // expert here) that is plain M-fastest order; for one large GEMM it keeps
+  // the tiles in flight on a kBand x (grid / kBand) patch whose A rows and B
+  // columns both fit in L2, instead of sweeping every A row per B column.
+  static constexpr int64_t kBand = 8;
+
+  __device__ __forceinline__ int64_t m_block(int64_t t) const {
+    const int64_t local = t - first;
+    const int64_t band_tiles = kBand * (count / m_blocks);
+    const int64_t band = local / band_tiles;
+    const int64_t rows = m_blocks - band * kBand < kBand ? m_blocks - band * kBand : kBand;
+    return band * kBand + (local - band * band_tiles) % rows;
+  }
+  __device__ __forceinline__ int64_t n_block(int64_t t) const {
+    const int64_t local = t - first;
+    const int64_t band_tiles = kBand * (count / m_blocks);
+    const int64_t band = local / band_tiles;
+    const int64_t rows = m_blocks - band * kBand < kBand ? m_blocks - band * kBand : kBand;
+    return (local - band * band_tiles) / rows;
+  }
 };
 
 }  // namespace mgb

@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "grouped_gemm_launch",
     "grouped_gemm_launch_noalloc",
     "matmul_launch",
+    "matrix_repack",
     "read_and_clear_error_word",
     "mgb_set_debug",
     "mgb_status_string",
@@ -116,6 +117,11 @@ def _declare(lib) -> None:
         ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(TileConfig), ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
     ]
     lib.matmul_launch.restype = ctypes.c_int
+    lib.matrix_repack.argtypes = [
+        ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+        ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
+    ]
+    lib.matrix_repack.restype = ctypes.c_int
     lib.read_and_clear_error_word.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32)]
     lib.read_and_clear_error_word.restype = ctypes.c_int
     lib.mgb_set_debug.argtypes = [ctypes.c_int64, ctypes.c_int32]
@@ -228,6 +234,13 @@ def matmul_launch(
     )
     _check(status, "matmul_launch")
     return info
+
+
+def repack(src: int, rows: int, cols: int, stride_r: int, stride_c: int, dst: int, dst_pitch: int,
+           elem_bytes: int, stream: int) -> None:
+    """matrix_repack: copy a strided matrix into a row-pitched buffer."""
+    _check(load().matrix_repack(src, int(rows), int(cols), int(stride_r), int(stride_c), dst, int(dst_pitch),
+                                int(elem_bytes), stream), "matrix_repack")
 
 
 def read_and_clear_error_word(device: int) -> int:

@@ -222,16 +222,47 @@ def _check_precision(input_precision: str) -> str:
     return input_precision
 
 
+# Single GEMMs at least this large repack operands the TMA cannot address
+# (row pitch not a multiple of 16 bytes, unit-stride violations) so they run
+# on the tensor cores; smaller ones use the generic-stride kernel directly.
+REPACK_MIN_FLOPS = 1 << 28
+
+
+def _tma_addressable(x) -> bool:
+    return (x.data_ptr() % 16 == 0 and x.stride(1) == 1 and x.stride(0) > 0
+            and (x.stride(0) * x.element_size()) % 16 == 0)
+
+
+def _repacked(x, stream: int):
+    """Copy of ``x`` in a buffer whose row pitch is a multiple of 16 bytes
+    (a view of its first ``cols`` columns), made by the native repack kernel
+    on ``stream``."""
+    rows, cols = x.shape
+    step = 16 // x.element_size()
+    pitch = -(-cols // step) * step
+    buffer = torch.empty((rows, pitch), dtype=x.dtype, device=x.device)
+    _native.repack(x.data_ptr(), rows, cols, x.stride(0), x.stride(1), buffer.data_ptr(), pitch,
+                   x.element_size(), stream)
+    return buffer[:, :cols]
+
+
 def _launch_once(a, b, c, m: int, n: int, k: int, config: KernelConfig, precision: str) -> dict:
     global _last_launch_info
     stream = torch.cuda.current_stream(a.device).cuda_stream
+    tensor_core = a.dtype != torch.float32 or precision == "tf32"
+    repacked = False
     with torch.cuda.device(a.device):
+        if tensor_core and 2 * m * n * k >= REPACK_MIN_FLOPS and k > 0:
+            if not _tma_addressable(a):
+                a, repacked = _repacked(a, stream), True
+            if not _tma_addressable(b):
+                b, repacked = _repacked(b, stream), True
         info = _native.matmul_launch(
             a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k,
             (a.stride(0), a.stride(1), b.stride(0), b.stride(1), c.stride(0), c.stride(1)),
             dtype_name(a.dtype), precision, config, stream,
         )
-    _last_launch_info = info.as_dict()
+    _last_launch_info = {**info.as_dict(), "repacked": repacked}
     return _last_launch_info
 
 
@@ -313,7 +344,10 @@ def launch_matmul(
     ``autotune=True`` launches the native tile ``native_candidates`` picks
     for the shape (cached per shape/stride/dtype/precision key);
     ``autotune=False`` launches ``config`` (or the heuristic
-    ``select_config``), mapped to a native tile.
+    ``select_config``), mapped to a native tile.  Large GEMMs whose A or B the
+    TMA cannot address (masked shapes such as fp32 rows of 127 or 8191
+    elements) are first copied into 16-byte-pitched buffers by the native
+    repack kernel; C is always written in place through its own strides.
     """
     global _last_tuned
     if torch is None or not torch.cuda.is_available():

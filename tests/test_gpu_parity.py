@@ -492,3 +492,29 @@ def test_table_entry_breaking_alignment_is_skipped_not_faulted():
     for e in (0, 2):
         _oracle_check(ws.c[e], ws.a[e], ws.b[e], "bf16")
     ws.a_ptrs[1] = good
+
+
+@pytest.mark.parametrize("dtype_name,precision,shape", [
+    ("fp32", "tf32", (1000, 4095, 127)),
+    ("fp32", "tf32", (127, 1000, 4095)),
+    ("bf16", "ieee", (1000, 4095, 1000)),
+    ("fp16", "ieee", (333, 2047, 515)),
+])
+def test_masked_large_shapes_repack_onto_tensor_cores(dtype_name, precision, shape):
+    """The Qwen3 masked sweep's non-tile-multiple sizes:
+    rows the TMA cannot address are repacked and run on the tensor cores."""
+    torch = _torch()
+    from kernels import launch_matmul
+    from kernels.matmul import last_launch_info
+
+    m, k, n = shape
+    gen = torch.Generator(device="cuda").manual_seed(m + k + n)
+    a = _randn((m, k), _dtype(dtype_name), gen)
+    b = _randn((k, n), _dtype(dtype_name), gen)
+    c = torch.full((m, n), float("nan"), device="cuda", dtype=_dtype(dtype_name))
+    launch_matmul(a, b, c, input_precision=precision)
+    torch.cuda.synchronize()
+    info = last_launch_info()
+    assert info["path"].startswith("tcgen05_tma"), info
+    assert info["repacked"], info
+    _oracle_check(c, a, b, dtype_name, precision)
