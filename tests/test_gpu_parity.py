@@ -518,3 +518,32 @@ def test_masked_large_shapes_repack_onto_tensor_cores(dtype_name, precision, sha
     assert info["path"].startswith("tcgen05_tma"), info
     assert info["repacked"], info
     _oracle_check(c, a, b, dtype_name, precision)
+
+
+@pytest.mark.parametrize("case", [
+    # Mixtral-8x7B (E=8, H=4096, F=14336), M_e = 1024: EP P=8 is one expert per rank
+    ("mixtral W13 EP P=8", [(1024, 4096, 2 * 14336)], True),
+    ("mixtral W2 EP P=8", [(1024, 14336, 4096)], False),
+    ("mixtral W13 TP P=4", [(1024, 4096, 2 * 14336 // 4)] * 3, True),
+    ("mixtral W2 TP P=2", [(1024, 14336 // 2, 4096)] * 2, False),
+    # Qwen3-235B-A22B (E=128, H=4096, F=1536), P=8, T=256 -> M_e=16, T=16384 -> M_e=1024
+    ("qwen3 W13 EP M16", [(16, 4096, 3072)] * 4, True),
+    ("qwen3 W13 TP M1024", [(1024, 4096, 384)] * 4, True),
+    ("qwen3 W2 EP M256", [(256, 1536, 4096)] * 4, False),
+    ("qwen3 W2 TP M64", [(64, 192, 4096)] * 4, False),
+], ids=lambda c: c[0])
+def test_mixtral_and_qwen3_rank_shapes(case):
+    """Mixtral and Qwen3 rank shapes (a few
+    experts each), autotuned launch, oracle on sampled rows."""
+    torch = _torch()
+    from kernels import check_device_errors, launch_grouped
+
+    _, shapes, gate_up = case
+    k = shapes[0][1]
+    ws = _workspace(shapes, "bf16", seed=k + len(shapes), b_scale=1.0 / math.sqrt(k))
+    launch_grouped(ws)
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert ws.launch_info["path"].startswith("tcgen05_tma"), ws.launch_info
+    assert ws.scheduler == ("single_problem_matmul" if len(shapes) == 1 else "homogeneous_persistent")
+    _sampled_rows_check(ws, "bf16", rows_per_problem=8, gate_up=gate_up)
