@@ -45,6 +45,15 @@ METRIC = "grouped-GEMM TFLOP/s per B200 (EP vs TP, W13 & W2) and % of roofline"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 WORKLOAD = ("DeepSeek-V3 W13 gate+up bf16, P=8 rank shapes: EP 32 x [M_e,7168]@[7168,4096] and "
             "TP 256 x [M_e,7168]@[7168,512], M_e in {16,32,64,128,256,512,1024}; one step = 14 grouped launches")
+WORKLOAD_W2 = ("DeepSeek-V3 W2 down bf16, P=8 rank shapes: EP 32 x [M_e,2048]@[2048,7168] and "
+               "TP 256 x [M_e,256]@[256,7168] (partial sums), M_e in {16,...,1024}; one step = 14 grouped launches")
+
+
+def projection_dims(projection: str) -> dict:
+    """(K, N) of one expert GEMM per parallel type for a projection."""
+    if projection == "W1":
+        return {"EP": (HIDDEN, 2 * FFN), "TP": (HIDDEN, 2 * FFN // PARALLEL)}
+    return {"EP": (FFN, HIDDEN), "TP": (FFN // PARALLEL, HIDDEN)}
 
 
 def parse_args(argv=None):
@@ -56,6 +65,10 @@ def parse_args(argv=None):
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--skip-cpu-baseline", action="store_true")
     p.add_argument("--m-values", type=str, default=",".join(map(str, M_VALUES)))
+    p.add_argument("--projection", choices=("W1", "W2"), default="W1",
+                   help="W1: packed W13 gate+up (the benchmark line); W2: down projection (BASELINE configs[2])")
+    p.add_argument("--cache-mode", choices=("hot", "cold"), default="hot",
+                   help="cold: two resident workspace sets, alternated step by step (rotating-cold)")
     # Profiling / diagnosis knobs (defaults give the benchmark workload).
     p.add_argument("--parallel", type=str, default="EP,TP", help="subset of EP,TP to build and launch")
     p.add_argument("--config", type=str, default=None,
@@ -91,14 +104,14 @@ def dist_env() -> tuple[int, int, int]:
     return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
 
 
-def step_shapes(m_values) -> list[tuple[str, int, tuple[int, int, int], int]]:
+def step_shapes(m_values, projection: str = "W1") -> list[tuple[str, int, tuple[int, int, int], int]]:
     """(parallel_type, M_e, (M, K, N), experts) for the 14 launches of one step."""
     from moe_parallel import moe_shapes
 
     out = []
     for m in m_values:
         for par in ("EP", "TP"):
-            shapes = moe_shapes("W1", par, m, HIDDEN, FFN, EXPERTS, PARALLEL)
+            shapes = moe_shapes(projection, par, m, HIDDEN, FFN, EXPERTS, PARALLEL)
             out.append((par, m, shapes[0], len(shapes)))
     return out
 
@@ -222,6 +235,119 @@ def build_rank(rank: int, m_values, device, parallel=("EP", "TP"), expert_limit=
     return ep, tp, activations, outputs, workspaces
 
 
+def expert_down_weight(expert: int, device, seed: int = 0):
+    """Global W2 (down) weight of one expert, [F, H], B ~ N(0, 1/sqrt(F))."""
+    import torch
+
+    gen = torch.Generator(device=device).manual_seed(2_000_029 * (expert + 1) + seed)
+    w = torch.randn((FFN, HIDDEN), device=device, generator=gen, dtype=torch.float32)
+    return w.mul_(1.0 / math.sqrt(FFN)).to(torch.bfloat16)
+
+
+def expert_intermediate(expert: int, m: int, device, seed: int = 0):
+    """Global W2 input of one expert (the SiLU(gate) * up activations), [M, F]."""
+    import torch
+
+    gen = torch.Generator(device=device).manual_seed(7919 * m + 104_729 * (expert + 1) + seed)
+    return torch.randn((m, FFN), device=device, generator=gen).to(torch.bfloat16)
+
+
+def build_rank_w2(rank: int, m_values, device, parallel=("EP", "TP"), expert_limit=None, seed: int = 0):
+    """W2 (down projection) rank tensors: EP experts with the full F, TP every
+    expert with the rank's F/P slice (rows of W2, columns of the input), whose
+    [M, 7168] outputs are partial sums."""
+    import torch
+
+    from kernels import workspace_from_tensors
+    from moe_parallel import rank_plan, shard_weight
+
+    ep = rank_plan("W2", "EP", rank, PARALLEL, EXPERTS, FFN, HIDDEN)
+    tp = rank_plan("W2", "TP", rank, PARALLEL, EXPERTS, FFN, HIDDEN)
+    ep_experts = ep.experts[:expert_limit] if expert_limit else ep.experts
+    tp_experts = tp.experts[:expert_limit] if expert_limit else tp.experts
+    lo, hi = tp.ffn_slice
+    ep_w, tp_w = [], []
+    for e in range(EXPERTS):
+        use_ep = e in ep_experts and "EP" in parallel
+        use_tp = e in tp_experts and "TP" in parallel
+        if not (use_ep or use_tp):
+            continue
+        w = expert_down_weight(e, device, seed)
+        if use_ep:
+            ep_w.append(w)
+        if use_tp:
+            tp_w.append(shard_weight(w, tp).contiguous())
+        del w
+    activations, outputs, workspaces = {}, {}, []
+    for m in m_values:
+        a_ep = torch.empty((len(ep_experts), m, FFN), device=device, dtype=torch.bfloat16)
+        a_tp = torch.empty((len(tp_experts), m, hi - lo), device=device, dtype=torch.bfloat16)
+        for i, e in enumerate(tp_experts if "TP" in parallel else ()):
+            full = expert_intermediate(e, m, device, seed)
+            a_tp[i].copy_(full[:, lo:hi])
+        for i, e in enumerate(ep_experts if "EP" in parallel else ()):
+            a_ep[i].copy_(expert_intermediate(e, m, device, seed))
+        activations[m] = [a_ep, a_tp]
+        c_ep = torch.empty((len(ep_experts), m, HIDDEN), device=device, dtype=torch.bfloat16)
+        c_tp = torch.empty((len(tp_experts), m, HIDDEN), device=device, dtype=torch.bfloat16)
+        outputs[m] = (c_ep, c_tp)
+        if "EP" in parallel:
+            ws_ep = workspace_from_tensors(list(a_ep), ep_w, list(c_ep))
+            ws_ep.operation = "down"
+            workspaces.append(("EP", m, ws_ep))
+        if "TP" in parallel:
+            ws_tp = workspace_from_tensors(list(a_tp), tp_w, list(c_tp))
+            ws_tp.operation = "down"
+            workspaces.append(("TP", m, ws_tp))
+    return ep, tp, activations, outputs, workspaces
+
+
+def verify_w2_outputs(rank, world, ep, tp, outputs, device, m_values, seed: int = 0) -> dict:
+    """W2 after timing: sampled rows of every rank's EP outputs and TP partial
+    sums are all-gathered over NCCL; rank 0 checks EP rows against the full
+    float64 product and rank r's TP partial against its F/P slice of it (with
+    all 8 ranks present, the partials' sum against the full product too)."""
+    import torch
+    import torch.distributed as dist
+
+    from moe_parallel import ep_owner
+
+    per = EXPERTS // PARALLEL
+    sampled = sorted({0, per - 1} | {r * per + (r % per) for r in range(world)})
+    checks = [m_values[0], m_values[-1]]
+    width = FFN // PARALLEL
+    worst = 0.0
+    for m in checks:
+        rows = torch.tensor(sorted({0, m - 1, m // 2}), device=device)
+        c_ep, c_tp = outputs[m]
+        payload = torch.zeros((len(sampled), len(rows), 2 * HIDDEN), device=device, dtype=torch.float32)
+        for i, e in enumerate(sampled):
+            if ep_owner(e, PARALLEL, EXPERTS) == rank:
+                payload[i, :, :HIDDEN] = c_ep[ep.experts.index(e)].index_select(0, rows).float()
+            payload[i, :, HIDDEN:] = c_tp[e].index_select(0, rows).float()
+        gathered = [torch.empty_like(payload) for _ in range(world)] if world > 1 else [payload]
+        if world > 1:
+            dist.all_gather(gathered, payload)
+        if rank != 0:
+            continue
+        for i, e in enumerate(sampled):
+            a = expert_intermediate(e, m, device, seed).index_select(0, rows).double()
+            w = expert_down_weight(e, device, seed).double()
+            full = a @ w
+            owner = ep_owner(e, PARALLEL, EXPERTS)
+            if owner < world:
+                got = gathered[owner][i, :, :HIDDEN].double()
+                worst = max(worst, float((got - full).norm() / full.norm()))
+            for r in range(world):
+                part = a[:, r * width:(r + 1) * width] @ w[r * width:(r + 1) * width]
+                got = gathered[r][i, :, HIDDEN:].double()
+                worst = max(worst, float((got - part).norm() / part.norm()))
+            if world == PARALLEL:
+                summed = sum(gathered[r][i, :, HIDDEN:].double() for r in range(world))
+                worst = max(worst, float((summed - full).norm() / full.norm()))
+    return {"checked_experts": sampled, "checked_m": checks, "max_rel_frobenius": worst, "passed": worst <= 1e-2}
+
+
 FIXED_CONFIG = None  # set by --config: launches use it instead of the autotuned winner
 CLASS_CONFIGS: dict[str, object] = {}  # set by --config-small / --config-large
 
@@ -236,16 +362,17 @@ def launch(ws) -> None:
         launch_grouped(ws, config=fixed, autotune=False)
 
 
-def graph_of_steps(workspaces, steps: int, stream):
+def graph_of_steps(workspaces, steps: int, stream, rings=None):
     """One CUDA graph holding `steps` passes of the step's launches, with an
-    event pair around every launch (read after the timed replay)."""
+    event pair around every launch (read after the timed replay).  With
+    `rings` (rotating-cold), step s launches the workspace set s % len(rings)."""
     import torch
 
     events = []
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        for _ in range(steps):
-            for par, m, ws in workspaces:
+        for step in range(steps):
+            for par, m, ws in (rings[step % len(rings)] if rings else workspaces):
                 start = torch.cuda.Event(enable_timing=True, external=True)
                 end = torch.cuda.Event(enable_timing=True, external=True)
                 start.record()
@@ -299,33 +426,31 @@ def verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_val
 
 
 # ------------------------------------------------------------- CPU leg
-def cpu_problems(m_values, experts_per_launch: int, seed: int):
+def cpu_problems(m_values, experts_per_launch: int, seed: int, projection: str = "W1"):
     """Host bf16 problems for a sample of the step: `experts_per_launch`
     experts of every launch shape; weights are shared across the M_e values."""
     import torch
 
     gen = torch.Generator().manual_seed(seed)
-    scale = 1.0 / math.sqrt(HIDDEN)
-    w_ep = [(torch.randn((HIDDEN, 2 * FFN), generator=gen) * scale).to(torch.bfloat16)
-            for _ in range(experts_per_launch)]
-    w_tp = [(torch.randn((HIDDEN, 2 * FFN // PARALLEL), generator=gen) * scale).to(torch.bfloat16)
-            for _ in range(experts_per_launch)]
+    dims = projection_dims(projection)
+    weights = {par: [(torch.randn((k, n), generator=gen) / math.sqrt(k)).to(torch.bfloat16)
+                     for _ in range(experts_per_launch)] for par, (k, n) in dims.items()}
     a_list, b_list = [], []
     for m in m_values:
-        acts = torch.randn((experts_per_launch, m, HIDDEN), generator=gen).to(torch.bfloat16)
-        for weights in (w_ep, w_tp):
+        for par, (k, _n) in dims.items():
+            acts = torch.randn((experts_per_launch, m, k), generator=gen).to(torch.bfloat16)
             for j in range(experts_per_launch):
                 a_list.append(acts[j])
-                b_list.append(weights[j])
+                b_list.append(weights[par][j])
     return a_list, b_list
 
 
-def time_cpu(m_values, experts_per_launch: int, passes: int, budget_s: float) -> dict:
+def time_cpu(m_values, experts_per_launch: int, passes: int, budget_s: float, projection: str = "W1") -> dict:
     import torch
 
     from oracle.cpu_baseline import host_threads, per_expert_mm
 
-    a_list, b_list = cpu_problems(m_values, experts_per_launch, seed=5)
+    a_list, b_list = cpu_problems(m_values, experts_per_launch, seed=5, projection=projection)
     threads = host_threads()
     torch.set_num_threads(threads)
     per_expert_mm(a_list, b_list)  # warm-up pass
@@ -358,7 +483,7 @@ def reference_arm(args, rank: int, world: int) -> None:
     m_values = [int(v) for v in args.m_values.split(",")]
     threads = host_threads()
     torch.set_num_threads(threads)
-    a_list, b_list = cpu_problems(m_values, 1, seed=11)
+    a_list, b_list = cpu_problems(m_values, 1, seed=11, projection=args.projection)
     flops = sum(2 * a.shape[0] * a.shape[1] * b.shape[1] for a, b in zip(a_list, b_list))
     for _ in range(args.warmup):
         per_expert_mm(a_list, b_list)
@@ -373,7 +498,8 @@ def reference_arm(args, rank: int, world: int) -> None:
         "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": sample, "parallelism": "host CPU, rank 0 only"},
+        "config": {"workload": WORKLOAD if args.projection == "W1" else WORKLOAD_W2, "sample": sample,
+                   "parallelism": "host CPU, rank 0 only"},
         "impl": "reference",
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
                          "sample": sample},
@@ -386,7 +512,7 @@ def reference_arm(args, rank: int, world: int) -> None:
 SWEEP_TILES = {
     "swap16x128": (16, 128), "swap16x256": (16, 256), "swap32x128": (32, 128), "swap32x256": (32, 256),
     "swap64x128": (64, 128), "swap64x256": (64, 256), "tok128x64": (128, 64), "tok128x128": (128, 128),
-    "tok128x256": (128, 256), "pair256x256": (256, 128),
+    "tok128x256": (128, 256), "pair256x256": (256, 128), "pair256x512": (256, 256),
 }
 
 
@@ -491,14 +617,24 @@ def main(argv=None) -> int:
             CLASS_CONFIGS[int(m_text)] = KernelConfig(bm, bn, 64, 8, 4, 4)
     parallel = tuple(p for p in ("EP", "TP") if p in args.parallel.split(","))
     progress("building rank tensors")
-    ep, tp, activations, outputs, workspaces = build_rank(rank, m_values, device, parallel, args.expert_limit)
-    progress("autotuning the first launch of each workspace")
+    builder = build_rank if args.projection == "W1" else build_rank_w2
+    ep, tp, activations, outputs, workspaces = builder(rank, m_values, device, parallel, args.expert_limit)
+    rings = None
+    if args.cache_mode == "cold":
+        if args.steps % 2:
+            raise SystemExit("--cache-mode cold alternates two workspace sets: --steps must be even")
+        if args.projection == "W1":
+            second = build_rank(rank, m_values, device, parallel, args.expert_limit)[4]
+        else:
+            second = build_rank_w2(rank, m_values, device, parallel, args.expert_limit, seed=1)[4]
+        rings = [workspaces, second]
+    progress("first launch of each workspace (tile policy, untimed)")
     rank_flops = sum(gemm_flops(*ws.shapes[0]) * ws.problem_count for _, _, ws in workspaces)
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(stream):
-        for par, m, ws in workspaces:  # first call: autotune (eager, untimed)
-            progress(f"autotune {par} M_e={m}")
+        for par, m, ws in [entry for ring in (rings or [workspaces]) for entry in ring]:
+            progress(f"first launch {par} M_e={m}")
             launch(ws)
             progress(f"  -> {ws.config} {ws.launch_info}")
     stream.synchronize()
@@ -508,9 +644,9 @@ def main(argv=None) -> int:
     with torch.cuda.stream(stream):
         # Keep every graph's events alive as long as the graph: the graph
         # records into them on each replay.
-        warm_graph, warm_events = graph_of_steps(workspaces, 1, stream)
-        chunk = max(d for d in range(1, 11) if args.steps % d == 0)
-        timed_graph, events = graph_of_steps(workspaces, chunk, stream)
+        warm_graph, warm_events = graph_of_steps(workspaces, 2 if rings else 1, stream, rings)
+        chunk = max(d for d in range(1, 11) if args.steps % d == 0 and (not rings or d % 2 == 0))
+        timed_graph, events = graph_of_steps(workspaces, chunk, stream, rings)
         for _ in range(args.warmup):
             warm_graph.replay()
         timed_graph.replay()  # warms the timed graph's instantiation
@@ -579,11 +715,12 @@ def main(argv=None) -> int:
     # runs, and every output comes back device -> host.
     progress("end-to-end pass")
     e2e_steps = max(1, args.e2e_steps)
-    host_a = {m: torch.empty(a.shape, dtype=a.dtype, pin_memory=True).copy_(a, non_blocking=False)
-              for m, a in activations.items()}
+    act_lists = {m: (a if isinstance(a, list) else [a]) for m, a in activations.items()}
+    host_a = {m: [torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t) for t in ts]
+              for m, ts in act_lists.items()}
     host_c = {m: (torch.empty(c[0].shape, dtype=c[0].dtype, pin_memory=True),
                   torch.empty(c[1].shape, dtype=c[1].dtype, pin_memory=True)) for m, c in outputs.items()}
-    h2d = sum(t.numel() * t.element_size() for t in host_a.values())
+    h2d = sum(t.numel() * t.element_size() for ts in host_a.values() for t in ts)
     d2h = sum(t.numel() * t.element_size() for pair in host_c.values() for t in pair)
     by_m = {}
     for par, m, ws in workspaces:
@@ -596,7 +733,8 @@ def main(argv=None) -> int:
         e_start.record(stream)
         for _ in range(e2e_steps):
             for m in m_values:
-                activations[m].copy_(host_a[m], non_blocking=True)
+                for dev_t, host_t in zip(act_lists[m], host_a[m]):
+                    dev_t.copy_(host_t, non_blocking=True)
                 for ws in by_m[m]:
                     launch(ws)
                 host_c[m][0].copy_(outputs[m][0], non_blocking=True)
@@ -610,7 +748,9 @@ def main(argv=None) -> int:
     check_device_errors(local_rank)
 
     progress("verification")
-    if parallel == ("EP", "TP") and not args.expert_limit:
+    if parallel == ("EP", "TP") and not args.expert_limit and args.projection == "W2":
+        verification = verify_w2_outputs(rank, world, ep, tp, outputs, device, m_values)
+    elif parallel == ("EP", "TP") and not args.expert_limit:
         verification = verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_values)
     else:
         verification = {"skipped": "partial workload (--parallel / --expert-limit)"}
@@ -620,7 +760,7 @@ def main(argv=None) -> int:
     cpu = None
     if rank == 0 and world == 1 and not args.skip_cpu_baseline:
         progress("cpu baseline")
-        cpu = time_cpu(m_values, experts_per_launch=8, passes=10, budget_s=25.0)
+        cpu = time_cpu(m_values, experts_per_launch=8, passes=10, budget_s=25.0, projection=args.projection)
 
     if rank == 0:
         total_flops = rank_flops * world
@@ -629,8 +769,11 @@ def main(argv=None) -> int:
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "parallelism": f"GPU r runs rank r of P=8 (EP and TP), {world} rank(s)",
-                       "cache": "hot; inputs larger than L2 (1.88 GB of weights per projection), no flush",
+            "config": {"workload": WORKLOAD if args.projection == "W1" else WORKLOAD_W2,
+                       "parallelism": f"GPU r runs rank r of P=8 (EP and TP), {world} rank(s)",
+                       "cache": ("hot; inputs larger than L2 (0.94-1.88 GB of weights per projection), no flush"
+                                 if args.cache_mode == "hot" else
+                                 "rotating-cold: two resident workspace sets alternated step by step"),
                        "timing": "CUDA events around graph replays of whole steps, max over ranks"},
             "roofline": roofline,
             "roofline_step_frac": round(step_roof_ms / total_ms, 3),

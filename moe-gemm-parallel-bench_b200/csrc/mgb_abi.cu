@@ -26,8 +26,8 @@ using mgb::TcVariantInfo;
 __device__ uint32_t g_error_word;
 
 constexpr int kMaxDevices = 128;
-constexpr int kMaxSlotsPerCta = 16;              // >= every variant's kSlots
-constexpr size_t kSlotBytes = 2 * sizeof(CUtensorMap);  // act + wgt maps
+constexpr size_t kMapsPerCta = 32;  // >= every variant's kMapsPerCta (operand slots + output maps)
+constexpr size_t kMapBytes = sizeof(CUtensorMap);
 constexpr long long kDefaultWaitBudget = 2000000000ll;  // ~1 s of SM clock
 
 std::mutex g_mutex;
@@ -107,9 +107,10 @@ bool encode_2d(CUtensorMap* map, int dtype, const void* base, uint64_t inner, ui
 // block_m <= 64 selects the swap-AB (weight-streaming) family with that many
 // tokens per tile; block_m == 128 the MMA-M = 128 token family; larger
 // block_m the swap-AB 256-token tile.  block_n picks the weight tile.
-// block_m >= 256 with block_n >= 128 selects, for fp16 / bf16, the CTA-pair
-// kernel's 256 x 256 cluster tile; block_m >= 256 with a narrower block_n (and
-// every fp32 case) the one-CTA swap-AB 256 x 128 tile.
+// block_m >= 256 with block_n == 128 selects, for fp16 / bf16, the CTA-pair
+// kernel's 256 x 256 cluster tile, and block_n >= 256 its 256 x 512 tile (the
+// reference's configs keep block_n <= 256); block_m >= 256 with a narrower
+// block_n (and every fp32 case) the one-CTA swap-AB 256 x 128 tile.
 TcVariant pick_variant(const mgb_tile_config* cfg, int dtype) {
   const int bm = cfg ? cfg->block_m : 64;
   const int bn = cfg ? cfg->block_n : 128;
@@ -118,6 +119,7 @@ TcVariant pick_variant(const mgb_tile_config* cfg, int dtype) {
   if (bm <= 32) return {true, 32, wide};
   if (bm <= 64) return {true, 64, wide};
   if (bm <= 128) return {false, 128, bn <= 64 ? 64 : (bn <= 128 ? 128 : 256)};
+  if (dtype != MGB_FP32 && bn >= 256) return {false, 256, 512, true};
   if (dtype != MGB_FP32 && bn >= 128) return {false, 256, 256, true};
   return {true, 256, 128};
 }
@@ -131,12 +133,19 @@ bool variant_info(int dtype, const TcVariant& v, TcVariantInfo* info) {
 }
 
 int tc_launch_typed(int dtype, const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt,
-                    const GroupedParams& p, int grid, cudaStream_t s) {
+                    const CUtensorMap& out, const GroupedParams& p, int grid, cudaStream_t s) {
   switch (dtype) {
-    case MGB_FP16: return mgb::tc_launch<__half>(v, act, wgt, p, grid, s);
-    case MGB_BF16: return mgb::tc_launch<__nv_bfloat16>(v, act, wgt, p, grid, s);
-    default: return mgb::tc_launch<float>(v, act, wgt, p, grid, s);
+    case MGB_FP16: return mgb::tc_launch<__half>(v, act, wgt, out, p, grid, s);
+    case MGB_BF16: return mgb::tc_launch<__nv_bfloat16>(v, act, wgt, out, p, grid, s);
+    default: return mgb::tc_launch<float>(v, act, wgt, out, p, grid, s);
   }
+}
+
+// Output map: boxes of 32 rows x 128 bytes with the 128-byte swizzle, the
+// layout the row-tile epilogues stage each chunk in.
+bool encode_out(CUtensorMap* map, int dtype, const void* base, uint64_t cols, uint64_t rows, uint64_t pitch) {
+  return encode_2d(map, dtype, base, cols, rows, pitch, static_cast<uint32_t>(128 / elem_size(dtype)), 32,
+                   CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 int simt_launch_typed(int dtype, const GroupedParams& p, int grid, cudaStream_t s) {
@@ -153,6 +162,17 @@ int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 int grid_for(int64_t problems, int64_t m, int64_t n, int tm, int tn, int64_t cap) {
   const int64_t tiles = problems * cdiv(std::max<int64_t>(m, 1), tm) * cdiv(std::max<int64_t>(n, 1), tn);
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, cap)));
+}
+
+// Tiles per schedule unit for a grouped tensor-core launch (see TileWalk):
+// enough tiles that a unit holds about 16 k-blocks of MMA work, so the
+// per-problem tensor-map rebuild is amortised, but no more than keeps 16
+// units per scheduler (CTA or CTA pair) for a short last round.
+int unit_tiles_for(int64_t tiles, int64_t k, int bk, int schedulers) {
+  const int64_t kblocks = std::max<int64_t>(1, cdiv(k, bk));
+  int64_t unit = std::min<int64_t>(8, cdiv(16, kblocks));
+  while (unit > 1 && tiles / unit < 16ll * schedulers) unit >>= 1;
+  return static_cast<int>(std::max<int64_t>(1, unit));
 }
 
 void fill_info(mgb_launch_info* info, int path, const TcVariant& v, const TcVariantInfo& vi, int grid) {
@@ -219,7 +239,7 @@ int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r,
 size_t grouped_gemm_scratch_bytes(int32_t problem_count, int32_t sm_count) {
   (void)problem_count;
   const size_t ctas = sm_count > 0 ? static_cast<size_t>(sm_count) : 1;
-  return ctas * kMaxSlotsPerCta * kSlotBytes;
+  return ctas * kMapsPerCta * kMapBytes;
 }
 
 int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs, const int32_t* dims,
@@ -260,24 +280,29 @@ int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
     const int grid = v.pair ? 2 * grid_for(problem_count, m, n, v.tm, v.tn, std::max(1, vi.max_clusters))
                             : grid_for(problem_count, m, n, v.tm, v.tn, ds.sm_count);
-    const size_t need = static_cast<size_t>(grid) * vi.slots * kSlotBytes;
+    const size_t need = static_cast<size_t>(grid) * vi.maps * kMapBytes;
     if (scratch == nullptr || scratch_bytes < need || reinterpret_cast<uintptr_t>(scratch) % 128 != 0) {
       return MGB_ERR_SCRATCH;
     }
     p.desc_slots = static_cast<uint8_t*>(scratch);
+    const int64_t tiles = problem_count * cdiv(m, v.tm) * cdiv(n, v.tn);
+    p.unit_tiles = unit_tiles_for(tiles, k, vi.bk, v.pair ? grid / 2 : grid);
     // Templates: box shape, swizzle and element type are final; the device
     // rewrites the base address (and, for heterogeneous groups, the extents
     // and row pitch) of its copies per problem.  The scratch pointer stands in
     // as a 16-byte aligned placeholder address; it is never read through.
+    // (A homogeneous group whose C rows are not 16-byte multiples apart is
+    // stored without TMA; its rounded-up template pitch is then unused.)
     const int es = elem_size(dtype);
     const uint64_t act_pitch = ((static_cast<uint64_t>(k) * es + 15) / 16) * 16;
     const uint64_t wgt_pitch = ((static_cast<uint64_t>(n) * es + 15) / 16) * 16;
-    CUtensorMap act, wgt;
+    CUtensorMap act, wgt, out;
     if (!encode_2d(&act, dtype, scratch, k, m, act_pitch, vi.bk, vi.box_rows, kActSwizzle) ||
-        !encode_2d(&wgt, dtype, scratch, n, k, wgt_pitch, vi.bk, vi.bk, wgt_swizzle(dtype))) {
+        !encode_2d(&wgt, dtype, scratch, n, k, wgt_pitch, vi.bk, vi.bk, wgt_swizzle(dtype)) ||
+        !encode_out(&out, dtype, scratch, n, m, wgt_pitch)) {
       return MGB_ERR_CUDA;
     }
-    const int e = tc_launch_typed(dtype, v, act, wgt, p, grid, s);
+    const int e = tc_launch_typed(dtype, v, act, wgt, out, p, grid, s);
     if (e != 0) return MGB_ERR_CUDA;
     fill_info(info, 0, v, vi, grid);
     return MGB_OK;
@@ -302,6 +327,7 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
   GroupedParams p;
   std::memset(&p, 0, sizeof(p));
   p.single = 1;
+  p.unit_tiles = 1;
   p.problem_count = 1;
   p.m = m;
   p.n = n;
@@ -333,14 +359,20 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
     const TcVariant v = pick_variant(config, dtype);
     TcVariantInfo vi;
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
-    CUtensorMap act, wgt;
+    // C gets a real output map when TMA can address it (the kernel applies
+    // the same test); otherwise a placeholder over A that is never used.
+    const bool c_tma = reinterpret_cast<uintptr_t>(c) % 16 == 0 && stride_cn == 1 && stride_cm >= n &&
+                       (stride_cm * es) % 16 == 0;
+    CUtensorMap act, wgt, out;
     if (!encode_2d(&act, dtype, a, k, m, static_cast<uint64_t>(stride_am) * es, vi.bk, vi.box_rows, kActSwizzle) ||
-        !encode_2d(&wgt, dtype, b, n, k, static_cast<uint64_t>(stride_bk) * es, vi.bk, vi.bk, wgt_swizzle(dtype))) {
+        !encode_2d(&wgt, dtype, b, n, k, static_cast<uint64_t>(stride_bk) * es, vi.bk, vi.bk, wgt_swizzle(dtype)) ||
+        !(c_tma ? encode_out(&out, dtype, c, n, m, static_cast<uint64_t>(stride_cm) * es)
+                : encode_out(&out, dtype, a, 128 / es, 32, 128))) {
       return MGB_ERR_CUDA;
     }
     const int grid = v.pair ? 2 * grid_for(1, m, n, v.tm, v.tn, std::max(1, vi.max_clusters))
                             : grid_for(1, m, n, v.tm, v.tn, ds.sm_count);
-    const int e = tc_launch_typed(dtype, v, act, wgt, p, grid, s);
+    const int e = tc_launch_typed(dtype, v, act, wgt, out, p, grid, s);
     if (e != 0) return MGB_ERR_CUDA;
     fill_info(info, 0, v, vi, grid);
     return MGB_OK;

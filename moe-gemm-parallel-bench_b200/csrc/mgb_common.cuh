@@ -37,6 +37,7 @@ struct GroupedParams {
   int64_t sam, sak, sbk, sbn, scm, scn;
   // Scratch for the per-CTA tensor-map slots of the TMA path.
   uint8_t* desc_slots;
+  int32_t unit_tiles;     // tensor-core kernels: consecutive tiles of one problem a CTA takes at a time
   long long wait_budget;  // SM clock cycles a barrier wait may take before the launch gives up
   int32_t test_flags;     // bit 0: make the epilogue wait on a barrier nothing arrives on
   uint32_t* error_word;   // where error bits are OR-ed (a __device__ word of this library)
@@ -84,13 +85,86 @@ __device__ __forceinline__ int64_t ceil_div64(int64_t a, int64_t b) { return (a 
 // the same way, kernels/grouped_gemm.py:426-436).  Tiles inside a problem are
 // ordered M-block fastest (in bands of 8 M-blocks, see m_block), so CTAs that
 // run at the same time share a weight column block in L2.
+//
+// The tensor-core kernels hand out work in units: U consecutive tiles of one
+// problem (the last unit of a problem may be shorter), units strided over the
+// CTAs (seek_unit).  With U = 1 this is the plain strided tile schedule; a
+// larger U keeps a CTA on one problem for several short-K tiles, so the
+// per-problem tensor-map rebuilds are paid once per unit.
 template <int TM, int TN>
 struct TileWalk {
   int problem = -1;
   int64_t first = 0;   // first global tile of `problem`
   int64_t count = 0;   // tiles of `problem`
+  int64_t ufirst = 0;  // first global unit of `problem` (seek_unit)
+  int64_t ucount = 0;  // units of `problem` (seek_unit)
   int64_t m_blocks = 1;
   Problem prob;
+
+  // Moves to the problem holding global unit `u` of `unit` tiles each and
+  // returns its global tile range [t0, t1); false when `u` is past the end.
+  // The walk must only be driven by seek_unit (not mixed with seek).
+  __device__ __forceinline__ bool seek_unit(const GroupedParams& p, int64_t u, int64_t unit, int64_t& t0,
+                                            int64_t& t1) {
+    if (p.single || p.homogeneous) {
+      if (problem < 0) {
+        Problem q = load_problem(p, 0);
+        m_blocks = ceil_div64(q.m, TM);
+        count = (q.m > 0 && q.n > 0) ? m_blocks * ceil_div64(q.n, TN) : 0;
+      }
+      const int total_problems = p.single ? 1 : p.problem_count;
+      if (count == 0) return false;
+      ucount = ceil_div64(count, unit);
+      const int64_t e = u / ucount;
+      if (e >= total_problems) return false;
+      if (e != problem) {
+        problem = static_cast<int>(e);
+        first = e * count;
+        prob = load_problem(p, problem);
+      }
+      ufirst = e * ucount;
+    } else {
+      while (problem < 0 || u >= ufirst + ucount) {
+        first += count;
+        ufirst += ucount;
+        ++problem;
+        if (problem >= p.problem_count) return false;
+        prob = load_problem(p, problem);
+        if (prob.m <= 0 || prob.n <= 0 || prob.k < 0) {
+          count = 0;
+          ucount = 0;
+          m_blocks = 1;
+          continue;
+        }
+        m_blocks = ceil_div64(prob.m, TM);
+        count = m_blocks * ceil_div64(prob.n, TN);
+        ucount = ceil_div64(count, unit);
+      }
+    }
+    t0 = first + (u - ufirst) * unit;
+    t1 = t0 + unit < first + count ? t0 + unit : first + count;
+    return true;
+  }
+
+  // This CTA's next tile under the unit schedule (units first_unit,
+  // first_unit + stride, ...; U = p.unit_tiles tiles each): the next tile of
+  // the current unit, else the first tile of the next unit.  False at the end.
+  int64_t unit_index = -1;
+  int64_t unit_next = 0;  // next tile of the current unit
+  int64_t unit_end = 0;   // end of the current unit
+  __device__ __forceinline__ bool next_tile(const GroupedParams& p, int64_t first_unit, int64_t stride, int64_t& t) {
+    if (unit_next < unit_end) {
+      t = unit_next++;
+      return true;
+    }
+    unit_index = unit_index < 0 ? first_unit : unit_index + stride;
+    int64_t t0 = 0, t1 = 0;
+    if (!seek_unit(p, unit_index, p.unit_tiles > 0 ? p.unit_tiles : 1, t0, t1)) return false;
+    t = t0;
+    unit_next = t0 + 1;
+    unit_end = t1;
+    return true;
+  }
 
   // Moves to the problem holding global tile `t`; false when `t` is past the end.
   __device__ __forceinline__ bool seek(const GroupedParams& p, int64_t t) {

@@ -29,16 +29,18 @@ struct TcVariantInfo {
   int max_clusters = 0;
   int box_rows = 0;  // token rows one CTA loads per stage (the activation box height)
   int box_cols = 0;  // weight columns one CTA loads per stage
+  int maps = 0;      // tensor maps (128 bytes each) one CTA keeps in the scratch buffer
 };
 
 // Returns false for a variant that is not instantiated.
 template <typename T>
 bool tc_variant_info(const TcVariant& v, TcVariantInfo* info);
 
-// Launches tc_grouped_kernel<T, v.swap, v.tm, v.tn>; returns a cudaError_t value.
+// Launches tc_grouped_kernel<T, v.swap, v.tm, v.tn> (or the pair kernel);
+// returns a cudaError_t value.  `out` is the output map (template for groups).
 template <typename T>
-int tc_launch(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt, const GroupedParams& p,
-              int grid, cudaStream_t stream);
+int tc_launch(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
+              const GroupedParams& p, int grid, cudaStream_t stream);
 
 // Launches simt_grouped_kernel<T>; returns a cudaError_t value.
 template <typename T>

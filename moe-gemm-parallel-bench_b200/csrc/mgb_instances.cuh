@@ -27,8 +27,8 @@ namespace mgb {
   X(false, 128, 256)
 
 template <typename T, bool SWAP, int TM, int TN>
-static int launch_variant(const CUtensorMap& act, const CUtensorMap& wgt, const GroupedParams& p, int grid,
-                          cudaStream_t stream) {
+static int launch_variant(const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
+                          const GroupedParams& p, int grid, cudaStream_t stream) {
   using Cfg = TcCfg<T, SWAP, TM, TN>;
   static bool configured[128] = {};
   int dev = 0;
@@ -40,7 +40,7 @@ static int launch_variant(const CUtensorMap& act, const CUtensorMap& wgt, const 
     if (e != cudaSuccess) return static_cast<int>(e);
     configured[dev] = true;
   }
-  tc_grouped_kernel<T, SWAP, TM, TN><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(act, wgt, p);
+  tc_grouped_kernel<T, SWAP, TM, TN><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(act, wgt, out, p);
   return static_cast<int>(cudaGetLastError());
 }
 
@@ -50,9 +50,9 @@ struct PairKernel {
   static constexpr bool kAvailable = sizeof(T) == 2;
 };
 
-// Clusters of two the device keeps resident at once for the pair kernel
-// (queried once per device; 0 when the query is unavailable).
-template <typename T>
+// Clusters of two the device keeps resident at once for the pair kernel with
+// NH halves (queried once per device; 0 when the query is unavailable).
+template <typename T, int NH>
 static int pair_max_clusters() {
   if constexpr (!PairKernel<T>::kAvailable) {
     return 0;
@@ -61,9 +61,9 @@ static int pair_max_clusters() {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 0;
     if (cached[dev] == 0) {
-      using Cfg = Tc2Cfg<T>;
-      if (cudaFuncSetAttribute(tc2_grouped_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes) !=
-          cudaSuccess) {
+      using Cfg = Tc2Cfg<T, NH>;
+      if (cudaFuncSetAttribute(tc2_grouped_kernel<T, NH>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               Cfg::kSmemBytes) != cudaSuccess) {
         return 0;
       }
       int sms = 0;
@@ -73,7 +73,8 @@ static int pair_max_clusters() {
       cfg.blockDim = dim3(kTcThreads, 1, 1);
       cfg.dynamicSmemBytes = Cfg::kSmemBytes;
       int clusters = 0;
-      if (cudaOccupancyMaxActiveClusters(&clusters, tc2_grouped_kernel<T>, &cfg) != cudaSuccess || clusters <= 0) {
+      if (cudaOccupancyMaxActiveClusters(&clusters, tc2_grouped_kernel<T, NH>, &cfg) != cudaSuccess ||
+          clusters <= 0) {
         cudaGetLastError();
         clusters = sms / 2;
       }
@@ -83,47 +84,47 @@ static int pair_max_clusters() {
   }
 }
 
-template <typename T>
-static int launch_pair(const CUtensorMap& act, const CUtensorMap& wgt, const GroupedParams& p, int grid,
-                       cudaStream_t stream) {
+template <typename T, int NH>
+static int launch_pair(const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
+                       const GroupedParams& p, int grid, cudaStream_t stream) {
   if constexpr (!PairKernel<T>::kAvailable) {
     return static_cast<int>(cudaErrorInvalidValue);
   } else {
-    using Cfg = Tc2Cfg<T>;
+    using Cfg = Tc2Cfg<T, NH>;
     static bool configured[128] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= 128) return static_cast<int>(cudaErrorInvalidDevice);
     if (!configured[dev]) {
-      const cudaError_t e =
-          cudaFuncSetAttribute(tc2_grouped_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
+      const cudaError_t e = cudaFuncSetAttribute(tc2_grouped_kernel<T, NH>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
       if (e != cudaSuccess) return static_cast<int>(e);
       configured[dev] = true;
     }
-    tc2_grouped_kernel<T><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(act, wgt, p);
+    tc2_grouped_kernel<T, NH><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(act, wgt, out, p);
     return static_cast<int>(cudaGetLastError());
   }
 }
 
-template <typename T>
+template <typename T, int NH>
 static bool pair_variant_info(const TcVariant& v, TcVariantInfo* info) {
   if constexpr (!PairKernel<T>::kAvailable) {
     return false;
   } else {
-    using Cfg = Tc2Cfg<T>;
-    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSlots, Cfg::kSmemBytes, pair_max_clusters<T>(), Cfg::kHalf,
-                          Cfg::kHalf};
+    using Cfg = Tc2Cfg<T, NH>;
+    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSlots, Cfg::kSmemBytes, pair_max_clusters<T, NH>(),
+                          Cfg::kHalf, NH * Cfg::kHalf, Cfg::kMapsPerCta};
     return v.tm == Cfg::kTileM && v.tn == Cfg::kTileN;
   }
 }
 
 template <>
 bool tc_variant_info<MGB_ELEM>(const TcVariant& v, TcVariantInfo* info) {
-  if (v.pair) return pair_variant_info<MGB_ELEM>(v, info);
+  if (v.pair) return v.tn > 256 ? pair_variant_info<MGB_ELEM, 2>(v, info) : pair_variant_info<MGB_ELEM, 1>(v, info);
 #define MGB_INFO(S, M, N)                                                               \
   if (v.swap == S && v.tm == M && v.tn == N) {                                          \
     using Cfg = TcCfg<MGB_ELEM, S, M, N>;                                               \
-    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSlots, Cfg::kSmemBytes, 0, M, N}; \
+    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSlots, Cfg::kSmemBytes, 0, M, N, Cfg::kMapsPerCta}; \
     return true;                                                                        \
   }
   MGB_FOR_EACH_VARIANT(MGB_INFO)
@@ -132,11 +133,14 @@ bool tc_variant_info<MGB_ELEM>(const TcVariant& v, TcVariantInfo* info) {
 }
 
 template <>
-int tc_launch<MGB_ELEM>(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt, const GroupedParams& p,
-                        int grid, cudaStream_t stream) {
-  if (v.pair) return launch_pair<MGB_ELEM>(act, wgt, p, grid, stream);
+int tc_launch<MGB_ELEM>(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
+                        const GroupedParams& p, int grid, cudaStream_t stream) {
+  if (v.pair) {
+    return v.tn > 256 ? launch_pair<MGB_ELEM, 2>(act, wgt, out, p, grid, stream)
+                      : launch_pair<MGB_ELEM, 1>(act, wgt, out, p, grid, stream);
+  }
 #define MGB_LAUNCH(S, M, N) \
-  if (v.swap == S && v.tm == M && v.tn == N) return launch_variant<MGB_ELEM, S, M, N>(act, wgt, p, grid, stream);
+  if (v.swap == S && v.tm == M && v.tn == N) return launch_variant<MGB_ELEM, S, M, N>(act, wgt, out, p, grid, stream);
   MGB_FOR_EACH_VARIANT(MGB_LAUNCH)
 #undef MGB_LAUNCH
   return static_cast<int>(cudaErrorInvalidValue);

@@ -83,6 +83,28 @@ __device__ __forceinline__ void tma_load_2d(const void* tmap, uint64_t* bar, voi
       : "memory");
 }
 
+// Tile store shared -> global.  Box elements outside the tensor's extents are
+// not written.  Completion is tracked per thread with bulk async-groups.
+__device__ __forceinline__ void tma_store_2d(const void* tmap, const void* src, int32_t x, int32_t y,
+                                             uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group.L2::cache_hint [%0, {%2, %3}], [%1], %4;" ::"l"(
+          tmap),
+      "r"(smem_u32(src)), "r"(x), "r"(y), "l"(policy)
+      : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit_group() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most N of this thread's bulk groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_group_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+// Waits until every bulk group of this thread has completed (writes performed).
+__device__ __forceinline__ void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));

@@ -2,12 +2,13 @@
 //
 // Same contract as tc_grouped_kernel (C_e = A_e @ B_e, fp32 accumulate, cast
 // on store) for token-rich problems: a cluster of two CTAs on neighbouring
-// SMs owns a 256-token x 256-weight-column output tile.  CTA r loads token
-// rows [128r, 128r + 128) of the tile and weight columns [128r, 128r + 128)
-// into its own shared memory; the even CTA issues tcgen05.mma.cta_group::2
-// (M = 256, N = 256), which reads both CTAs' halves.  Per SM this halves the
-// weight bytes each MMA pulls through shared memory and L2 compared with a
-// one-CTA 128 x 256 tile, which is what keeps the tensor pipe fed.
+// SMs owns a 256-token x (256 NH)-weight-column output tile.  CTA r loads
+// token rows [128r, 128r + 128) of the tile and, of every 256-column half h,
+// weight columns [256h + 128r, 256h + 128r + 128) into its own shared memory;
+// the even CTA issues tcgen05.mma.cta_group::2 (M = 256, N = 256) per half,
+// which reads both CTAs' halves.  Per SM this halves the weight bytes each MMA
+// pulls through shared memory and L2 compared with a one-CTA 128 x 256 tile,
+// which is what keeps the tensor pipe fed.
 //
 // Roles per CTA (192 threads) as in tc_grouped_kernel; only the even CTA's MMA
 // lane issues MMAs.  Barriers:
@@ -23,46 +24,62 @@
 
 namespace mgb {
 
-template <typename T>
+// NH = number of 256-column MMA halves per cluster tile: 1 gives the 256 x 256
+// tile with two TMEM accumulators (the epilogue of one tile overlaps the MMAs
+// of the next); 2 gives the 256 x 512 tile, whose single 512-column
+// accumulator fills TMEM.  Per k-block a CTA of the wide tile loads 16 KB of
+// activations and 32 KB of weights for 128 x 512 x 64 MACs (171 FLOP per
+// byte from L2) instead of 16 + 16 KB for 128 x 256 x 64 (128 FLOP per byte).
+template <typename T, int NH>
 struct Tc2Cfg {
   static constexpr int kElem = static_cast<int>(sizeof(T));
   static_assert(kElem == 2, "the CTA-pair kernel serves fp16 / bf16");
+  static_assert(NH == 1 || NH == 2, "one or two 256-column halves");
   static constexpr int kBK = 64;
   static constexpr int kKStep = 16;
   static constexpr int kKSteps = 4;
-  static constexpr int kTileM = 256;  // tokens per cluster tile
-  static constexpr int kTileN = 256;  // weight columns per cluster tile
-  static constexpr int kHalf = 128;   // per CTA: token rows and weight columns
+  static constexpr int kTileM = 256;       // tokens per cluster tile
+  static constexpr int kTileN = 256 * NH;  // weight columns per cluster tile
+  static constexpr int kHalf = 128;        // per CTA: token rows, and weight columns per MMA half
   static constexpr int kActBytes = kHalf * 128;
   static constexpr int kBoxBytes = kBK * 128;
-  static constexpr int kWgtBytes = kHalf * 128;
+  static constexpr int kHalfWgtBytes = kHalf * 128;  // one CTA's weight columns of one MMA half
+  static constexpr int kWgtBytes = NH * kHalfWgtBytes;
   static constexpr int kStageBytes = kActBytes + kWgtBytes;
-  static constexpr int kStages = kTcStageBudget / kStageBytes > 12 ? 12 : kTcStageBudget / kStageBytes;
+  static constexpr int kEpiBytes = kEpiBytesRowTile;  // staging blocks of the 4 epilogue warps
+  static constexpr int kStagesRaw = (kTcSmemBudget - kEpiBytes) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
   static constexpr int kSlots = kStages + 1;
+  static constexpr int kMapsPerCta = 2 * kSlots + kOutMapsPerCta;
   static constexpr int kAccCols = kTileN;
+  static constexpr int kAccBufs = NH == 1 ? 2 : 1;
   static constexpr int kTmemCols = 512;
   static constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
-  static constexpr uint32_t kIdesc = instr_desc(kFmt, 0, 1, kTileM, kTileN);
-  static constexpr int kSmemBytes = kStages * kStageBytes + 2048 + 1024;
-  static_assert(2 * kAccCols <= kTmemCols, "two accumulators");
+  static constexpr uint32_t kIdesc = instr_desc(kFmt, 0, 1, kTileM, 256);  // one MMA: M = 256, N = 256
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 2048 + 1024;
+  static_assert(kAccBufs * kAccCols <= kTmemCols, "accumulators fit in TMEM");
+  static_assert(kStages >= 3, "operand ring depth");
   static_assert(kSmemBytes <= 232448, "shared memory");
+  static_assert(kMapsPerCta <= kMapsPerCtaLimit, "tensor maps per CTA exceed the scratch region");
 };
 
-template <typename T>
+template <typename T, int NH>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     tc2_grouped_kernel(const __grid_constant__ CUtensorMap act_tmpl, const __grid_constant__ CUtensorMap wgt_tmpl,
-                       const GroupedParams p) {
-  using Cfg = Tc2Cfg<T>;
+                       const __grid_constant__ CUtensorMap out_tmpl, const GroupedParams p) {
+  using Cfg = Tc2Cfg<T, NH>;
   constexpr int S = Cfg::kStages;
+  constexpr int NB = Cfg::kAccBufs;
   constexpr int BK = Cfg::kBK;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* epi_stage = smem + S * Cfg::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + Cfg::kEpiBytes);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
-  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* acc_empty = acc_full + 2;  // NB of the two are used
   uint64_t* test_bar = acc_empty + 2;
   uint64_t* drain_bar = test_bar + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
@@ -107,7 +124,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     CUtensorMap* slots = reinterpret_cast<CUtensorMap*>(p.desc_slots) +
-                         static_cast<int64_t>(blockIdx.x) * Cfg::kSlots * 2;
+                         static_cast<int64_t>(blockIdx.x) * Cfg::kMapsPerCta;
     const CUtensorMap* act_map = &act_tmpl;
     const CUtensorMap* wgt_map = &wgt_tmpl;
     if (p.single && lane == 0) {
@@ -126,7 +143,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     int slot = -1;
     int built = -1;
     bool ok = true;
-    for (int64_t t = cluster; ok && walk.seek(p, t); t += clusters) {
+    for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
       const Problem& q = walk.prob;
       if (!tma_legal<T>(q)) {
         if (lane == 0 && walk.problem != built) atomicOr(p.error_word, kErrMisaligned);
@@ -135,7 +152,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       const int64_t kblocks = (q.k + BK - 1) / BK;
       const uint64_t pol_wgt = walk.m_blocks > 1 ? pol_shared : pol_stream;
       const int32_t m0 = static_cast<int32_t>(walk.m_block(t) * Cfg::kTileM + rank * Cfg::kHalf);
-      const int32_t n0 = static_cast<int32_t>(walk.n_block(t) * Cfg::kTileN + rank * Cfg::kHalf);
+      const int32_t n0 = static_cast<int32_t>(walk.n_block(t) * Cfg::kTileN + rank * Cfg::kHalf);  // + 256 h
       for (int64_t kb = 0; kb < kblocks; ++kb) {
         const int s = static_cast<int>(it % S);
         const uint32_t phase = (it / S) & 1u;
@@ -183,8 +200,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
           tma_load_2d_pair(act_map, bar, st_act, kx, m0, pol_act);
 #pragma unroll
-          for (int j = 0; j < Cfg::kHalf / BK; ++j) {
-            tma_load_2d_pair(wgt_map, bar, st_wgt + j * Cfg::kBoxBytes, n0 + j * BK, kx, pol_wgt);
+          for (int h = 0; h < NH; ++h) {
+#pragma unroll
+            for (int j = 0; j < Cfg::kHalf / BK; ++j) {
+              tma_load_2d_pair(wgt_map, bar, st_wgt + h * Cfg::kHalfWgtBytes + j * Cfg::kBoxBytes,
+                               n0 + 256 * h + j * BK, kx, pol_wgt);
+            }
           }
         }
         __syncwarp();
@@ -207,13 +228,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       uint32_t it = 0;
       uint32_t acc_it = 0;
       bool ok = true;
-      for (int64_t t = cluster; ok && walk.seek(p, t); t += clusters) {
+      for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
         const Problem& q = walk.prob;
         if (!tma_legal<T>(q) || q.k <= 0) continue;
         const int64_t kblocks = (q.k + BK - 1) / BK;
-        const int buf = static_cast<int>(acc_it & 1u);
-        if (!mbar_wait(&acc_empty[buf], ((acc_it >> 1) & 1u) ^ 1u, budget, abort)) {
+        const int buf = static_cast<int>(acc_it % NB);
+        if (!mbar_wait(&acc_empty[buf], ((acc_it / NB) & 1u) ^ 1u, budget, abort)) {
           raise_error(p, kErrWaitAccEmpty, abort);
+          ok = false;
           break;
         }
         tc_fence_after();
@@ -231,8 +253,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
 #pragma unroll
           for (int ks = 0; ks < Cfg::kKSteps; ++ks) {
             const uint64_t act_desc = smem_desc(a_base + ks * 32, 16, 1024, kLayoutSw128);
-            const uint64_t wgt_desc = smem_desc(w_base + ks * Cfg::kKStep * 128, Cfg::kBoxBytes, 1024, kLayoutSw128);
-            mma_f16_pair(d_tmem, act_desc, wgt_desc, Cfg::kIdesc, (kb > 0 || ks > 0) ? 1u : 0u);
+#pragma unroll
+            for (int h = 0; h < NH; ++h) {
+              const uint64_t wgt_desc = smem_desc(w_base + h * Cfg::kHalfWgtBytes + ks * Cfg::kKStep * 128,
+                                                  Cfg::kBoxBytes, 1024, kLayoutSw128);
+              mma_f16_pair(d_tmem + h * 256, act_desc, wgt_desc, Cfg::kIdesc, (kb > 0 || ks > 0) ? 1u : 0u);
+            }
           }
           mma_commit_pair(&empty[s], 0x3);  // frees stage s in both CTAs
           ++it;
@@ -256,7 +282,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     }
     TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
     uint32_t acc_it = 0;
-    for (int64_t t = cluster; walk.seek(p, t); t += clusters) {
+    uint8_t* my_blocks = epi_stage + quarter * 2 * kEpiWarpBytes;
+    OutMapRing out_ring{nullptr, staging + 2 + quarter, -1, -1, nullptr};
+    if (!p.single) {
+      out_ring.slots = reinterpret_cast<CUtensorMap*>(p.desc_slots) +
+                       static_cast<int64_t>(blockIdx.x) * Cfg::kMapsPerCta + 2 * Cfg::kSlots + quarter * kOutSlots;
+    }
+    const uint64_t pol_out = policy_evict_first();
+    uint32_t chunk_seq = 0;
+    bool ok = true;
+    for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
       const Problem& q = walk.prob;
       if (!tma_legal<T>(q)) continue;
       const int64_t m0 = walk.m_block(t) * Cfg::kTileM + rank * Cfg::kHalf;
@@ -268,27 +303,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         }
         continue;
       }
-      const int buf = static_cast<int>(acc_it & 1u);
-      if (!mbar_wait_warp(&acc_full[buf], (acc_it >> 1) & 1u, budget, abort)) {
+      const void* cmap = c_tma_legal<T>(q) ? out_map_for<T>(out_ring, p, out_tmpl, q, walk.problem, lane) : nullptr;
+      const int buf = static_cast<int>(acc_it % NB);
+      if (!mbar_wait_warp(&acc_full[buf], (acc_it / NB) & 1u, budget, abort)) {
         if (lane == 0) raise_error(p, kErrWaitAccFull, abort);
+        ok = false;
         break;
       }
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(buf * Cfg::kAccCols);
-      const int64_t row = m0 + quarter * 32 + lane;
-#pragma unroll 1
-      for (int j = 0; j < Cfg::kTileN / 16; ++j) {
-        uint32_t r[16];
-        tmem_ld16(taddr + j * 16, r);
-        tmem_ld_wait();
-        store_row16<T>(q, row, n0 + j * 16, r);
+      if (cmap != nullptr) {
+        store_rows_tma<T, Cfg::kTileN>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
+                                       static_cast<int32_t>(n0), my_blocks, lane, chunk_seq, pol_out);
+      } else {
+        store_rows_staged<T, Cfg::kTileN>(q, taddr, m0 + quarter * 32, n0, my_blocks, lane);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[buf]), 0));
       ++acc_it;
     }
+    if (lane == 0) bulk_wait_group_all();  // tensor stores done before the CTA's shared memory goes away
+    __syncwarp();
   }
 
   tc_fence_before();

@@ -35,7 +35,17 @@
 namespace mgb {
 
 constexpr int kTcThreads = 192;
-constexpr int kTcStageBudget = 220 * 1024;  // shared memory given to the operand ring
+// Dynamic shared memory for the operand ring plus the epilogue staging blocks;
+// 3 KB of the 227 KB a CTA may use stay for barriers, staging maps and the
+// 1024-byte alignment of the ring.
+constexpr int kTcSmemBudget = 232448 - 3072;
+constexpr int kEpiWarpBytes = 32 * 128;  // one staging block: 32 rows x 128 bytes
+constexpr int kEpiBytesRowTile = 4 * 2 * kEpiWarpBytes;  // 4 epilogue warps x 2 blocks (double-buffered)
+// Output tensor maps: each epilogue warp keeps its own ring of kOutSlots maps
+// in the CTA's scratch region, after the producer's operand-map slots.
+constexpr int kOutSlots = 3;
+constexpr int kOutMapsPerCta = 4 * kOutSlots;
+constexpr int kMapsPerCtaLimit = 32;  // the scratch region per CTA: 32 maps of 128 bytes
 
 constexpr int pow2_at_least(int v) {
   int p = 32;
@@ -53,16 +63,21 @@ struct TcCfg {
   static constexpr int kBoxBytes = kBK * 128;  // one weight box: kBK columns x kBK K-rows
   static constexpr int kWgtBytes = TN * 128;   // TN / kBK boxes
   static constexpr int kStageBytes = kActBytes + kWgtBytes;
-  static constexpr int kStagesRaw = kTcStageBudget / kStageBytes;
+  // Row tiles stage their epilogue through shared memory and store it with
+  // TMA (store_rows_tma); swap-AB tiles store column-per-lane, already
+  // contiguous across the warp.
+  static constexpr int kEpiBytes = SWAP ? 0 : kEpiBytesRowTile;
+  static constexpr int kStagesRaw = (kTcSmemBudget - kEpiBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
-  static constexpr int kSlots = kStages + 1;  // tensor-map slots per CTA (see producer)
+  static constexpr int kSlots = kStages + 1;  // operand-map slots per CTA (see producer)
+  static constexpr int kMapsPerCta = 2 * kSlots + (SWAP ? 0 : kOutMapsPerCta);
   static constexpr int kAccCols = SWAP ? (TN / 128) * TM : TN;
   static constexpr int kTmemCols = pow2_at_least(2 * kAccCols);
   static constexpr uint32_t kFmt = std::is_same<T, float>::value ? 2u
                                    : std::is_same<T, __nv_bfloat16>::value ? 1u
                                                                             : 0u;
   static constexpr uint32_t kIdesc = SWAP ? instr_desc(kFmt, 1, 0, 128, TM) : instr_desc(kFmt, 0, 1, TM, TN);
-  static constexpr int kSmemBytes = kStages * kStageBytes + 2048 + 1024;
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 2048 + 1024;
   // The weight operand is MN-major.  For 16-bit types it uses the plain
   // 128-byte swizzle (8-row K atoms, SBO 1024); MN-major TF32 admits only the
   // 32-byte-granule variant (4-row K atoms, SBO 512), loaded by TMA with the
@@ -76,6 +91,7 @@ struct TcCfg {
   static_assert(TN % 128 == 0 || (!SWAP && TN == 64), "weight tile");
   static_assert(2 * kAccCols <= 512, "two accumulators must fit in TMEM");
   static_assert(kSmemBytes <= 232448, "shared memory");
+  static_assert(kMapsPerCta <= kMapsPerCtaLimit, "tensor maps per CTA exceed the scratch region");
 };
 
 // A problem is served by the TMA path when its operands satisfy the TMA rules:
@@ -88,6 +104,15 @@ __device__ __forceinline__ bool tma_legal(const Problem& q) {
   return (a % 16 == 0) && (b % 16 == 0) && q.sak == 1 && q.sbn == 1 && (q.sam * E) % 16 == 0 &&
          (q.sbk * E) % 16 == 0 && q.sam > 0 && q.sbk > 0 && q.m < (1ll << 31) && q.n < (1ll << 31) &&
          q.k < (1ll << 31);
+}
+
+// C is stored by TMA when its base is 16-byte aligned, its columns are unit
+// stride and its rows are whole multiples of 16 bytes apart (and do not overlap).
+template <typename T>
+__device__ __forceinline__ bool c_tma_legal(const Problem& q) {
+  constexpr int E = static_cast<int>(sizeof(T));
+  return (reinterpret_cast<uint64_t>(q.c) % 16 == 0) && q.scn == 1 && q.scm >= q.n && (q.scm * E) % 16 == 0 &&
+         q.m < (1ll << 31) && q.n < (1ll << 31);
 }
 
 __device__ __forceinline__ void raise_error(const GroupedParams& p, uint32_t bits, volatile int* abort) {
@@ -121,48 +146,180 @@ __device__ __forceinline__ void store_scalar(char* base, int64_t elem_offset, fl
   }
 }
 
-// 16 consecutive columns of one row: vector stores when the row segment is
-// whole, contiguous and 16-byte aligned; element stores otherwise.
 template <typename T>
-__device__ __forceinline__ void store_row16(const Problem& q, int64_t row, int64_t col0, const uint32_t (&r)[16]) {
-  if (row >= q.m) return;
-  char* dst = q.c + (row * q.scm + col0 * q.scn) * static_cast<int64_t>(sizeof(T));
-  const bool whole = (q.scn == 1) && (col0 + 16 <= q.n) && (reinterpret_cast<uint64_t>(dst) % 16 == 0);
-  if (whole) {
-    if constexpr (std::is_same<T, float>::value) {
-      uint4* d = reinterpret_cast<uint4*>(dst);
+__device__ __forceinline__ uint32_t pack_pair(uint32_t lo_bits, uint32_t hi_bits) {
+  const float lo = __uint_as_float(lo_bits), hi = __uint_as_float(hi_bits);
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+// One 128-byte-per-row chunk of a warp's 32 accumulator rows (TMEM lanes):
+// loads columns [col0, col0 + 128 / sizeof(T)), converts them and writes row
+// `lane` of the 32 x 128-byte block `block` with its 16-byte units rotated by
+// lane % 8 -- the 128-byte swizzle TMA uses, which also keeps the
+// row-per-lane writes free of bank conflicts.  Returns after the writes;
+// the caller synchronises the warp.
+template <typename T>
+__device__ __forceinline__ void load_chunk_tmem(uint32_t taddr, int col0, uint32_t (&v)[128 / sizeof(T) / 16][16]) {
+  constexpr int kLoads = 128 / static_cast<int>(sizeof(T)) / 16;
 #pragma unroll
-      for (int i = 0; i < 4; ++i) d[i] = make_uint4(r[4 * i], r[4 * i + 1], r[4 * i + 2], r[4 * i + 3]);
-    } else {
-      uint32_t packed[8];
+  for (int u = 0; u < kLoads; ++u) tmem_ld16(taddr + col0 + u * 16, v[u]);
+}
+
+template <typename T>
+__device__ __forceinline__ void write_chunk_smem(const uint32_t (&v)[128 / sizeof(T) / 16][16], uint8_t* block,
+                                                 int lane) {
+  constexpr int E = static_cast<int>(sizeof(T));
+  uint32_t w[32];
+  if constexpr (E == 4) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float lo = __uint_as_float(r[2 * i]), hi = __uint_as_float(r[2 * i + 1]);
-        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-          __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
-          packed[i] = *reinterpret_cast<uint32_t*>(&h);
+    for (int i = 0; i < 32; ++i) w[i] = v[i / 16][i % 16];
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = pack_pair<T>(v[(2 * i) / 16][(2 * i) % 16], v[(2 * i + 1) / 16][(2 * i + 1) % 16]);
+  }
+  uint8_t* my_row = block + lane * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    *reinterpret_cast<uint4*>(my_row + ((j ^ (lane & 7)) << 4)) =
+        make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+  }
+}
+
+// Row-tile epilogue of one warp through TMA: each chunk is staged in one of
+// the warp's two 4 KB blocks (double-buffered against the store still reading
+// the other) and written by one tensor store of 32 rows x 128 bytes; rows and
+// columns past C's extents are clipped by the tensor map.  `seq` counts the
+// warp's chunks across tiles and picks the block.
+template <typename T, int TN>
+__device__ __forceinline__ void store_rows_tma(const Problem& q, const void* cmap, uint32_t taddr, int32_t row0,
+                                               int32_t n0, uint8_t* blocks, int lane, uint32_t& seq,
+                                               uint64_t policy) {
+  constexpr int kChunkCols = 128 / static_cast<int>(sizeof(T));
+  static_assert(TN % kChunkCols == 0, "tile width is a whole number of chunks");
+  if (row0 >= q.m) return;  // all 32 rows of this warp lie past C (a ragged last M block)
+#pragma unroll 1
+  for (int c = 0; c < TN / kChunkCols; ++c) {
+    if (n0 + c * kChunkCols >= q.n) break;  // chunks past the last column
+    uint8_t* block = blocks + (seq & 1u) * kEpiWarpBytes;
+    uint32_t v[kChunkCols / 16][16];
+    load_chunk_tmem<T>(taddr, c * kChunkCols, v);
+    if (lane == 0) bulk_wait_group_read<1>();  // the store issued from `block` two chunks ago has read it
+    __syncwarp();
+    tmem_ld_wait();
+    write_chunk_smem<T>(v, block, lane);
+    fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA store
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(cmap, block, n0 + c * kChunkCols, row0, policy);
+      bulk_commit_group();
+    }
+    ++seq;
+  }
+}
+
+// Row-tile epilogue of one warp without TMA (C not addressable by a tensor
+// map): the chunk goes through `block` and is read back so that every global
+// store instruction writes four whole 128-byte row segments.
+template <typename T, int TN>
+__device__ __forceinline__ void store_rows_staged(const Problem& q, uint32_t taddr, int64_t row0, int64_t n0,
+                                                  uint8_t* block, int lane) {
+  constexpr int E = static_cast<int>(sizeof(T));
+  constexpr int kChunkCols = 128 / E;
+  constexpr int kUnitCols = 16 / E;  // columns per 16-byte unit
+  static_assert(TN % kChunkCols == 0, "tile width is a whole number of chunks");
+  if (lane == 0) bulk_wait_group_read<0>();  // no tensor store of this warp still reads its blocks
+  __syncwarp();
+#pragma unroll 1
+  for (int c = 0; c < TN / kChunkCols; ++c) {
+    uint32_t v[kChunkCols / 16][16];
+    load_chunk_tmem<T>(taddr, c * kChunkCols, v);
+    tmem_ld_wait();
+    write_chunk_smem<T>(v, block, lane);
+    __syncwarp();
+    const int j = lane & 7;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = 4 * i + (lane >> 3);
+      const uint4 val = *reinterpret_cast<const uint4*>(block + r * 128 + ((j ^ (r & 7)) << 4));
+      const int64_t row = row0 + r;
+      const int64_t col = n0 + c * kChunkCols + j * kUnitCols;
+      if (row < q.m) {
+        char* dst = q.c + (row * q.scm + col * q.scn) * static_cast<int64_t>(E);
+        if (q.scn == 1 && col + kUnitCols <= q.n && (reinterpret_cast<uint64_t>(dst) % 16 == 0)) {
+          *reinterpret_cast<uint4*>(dst) = val;
         } else {
-          __half2 h = __floats2half2_rn(lo, hi);
-          packed[i] = *reinterpret_cast<uint32_t*>(&h);
+          const uint32_t parts[4] = {val.x, val.y, val.z, val.w};
+#pragma unroll
+          for (int e = 0; e < kUnitCols; ++e) {
+            if (col + e >= q.n) break;
+            char* d = q.c + (row * q.scm + (col + e) * q.scn) * static_cast<int64_t>(E);
+            if constexpr (E == 4) {
+              *reinterpret_cast<uint32_t*>(d) = parts[e];
+            } else {
+              *reinterpret_cast<uint16_t*>(d) = static_cast<uint16_t>(parts[e / 2] >> (16 * (e % 2)));
+            }
+          }
         }
       }
-      uint4* d = reinterpret_cast<uint4*>(dst);
-      d[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-      d[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
     }
-    return;
+    __syncwarp();  // the block is rewritten by the next chunk
   }
-#pragma unroll
-  for (int i = 0; i < 16; ++i) {
-    const int64_t col = col0 + i;
-    if (col < q.n) store_scalar<T>(q.c, row * q.scm + col * q.scn, __uint_as_float(r[i]));
+}
+
+// One epilogue warp's output maps: a ring of kOutSlots global maps and a
+// 128-byte shared staging copy.  A map is rebuilt when the warp's walk enters
+// a new problem, before the warp waits for that tile's accumulator, so the
+// rebuild overlaps the tile's MMAs.  A slot is rewritten kOutSlots problems
+// after its last use; by then the warp has waited for every earlier store to
+// finish reading (bulk_wait_group_read<0> below), and a tensor store takes its
+// map when it starts.
+struct OutMapRing {
+  CUtensorMap* slots;
+  CUtensorMap* staging;
+  int slot;
+  int built;
+  const void* current;
+};
+
+template <typename T>
+__device__ __forceinline__ const void* out_map_for(OutMapRing& r, const GroupedParams& p, const CUtensorMap& tmpl,
+                                                   const Problem& q, int problem, int lane) {
+  if (p.single) return &tmpl;
+  if (problem != r.built) {
+    if (lane == 0) bulk_wait_group_read<0>();
+    r.slot = (r.slot + 1) % kOutSlots;
+    uint64_t* st = reinterpret_cast<uint64_t*>(r.staging);
+    if (lane < 16) st[lane] = reinterpret_cast<const uint64_t*>(&tmpl)[lane];
+    __syncwarp();
+    if (lane == 0) {
+      tmap_replace_address(r.staging, q.c);
+      if (!p.homogeneous) {
+        tmap_replace_dim(r.staging, 0, static_cast<uint32_t>(q.n));
+        tmap_replace_dim(r.staging, 1, static_cast<uint32_t>(q.m));
+        tmap_replace_stride1(r.staging, static_cast<uint64_t>(q.scm) * sizeof(T));
+      }
+    }
+    __syncwarp();
+    CUtensorMap* g = r.slots + r.slot;
+    tmap_publish(g, r.staging);
+    if (lane == 0) tmap_acquire(g);
+    __syncwarp();
+    r.built = problem;
+    r.current = g;
   }
+  return r.current;
 }
 
 template <typename T, bool SWAP, int TM, int TN>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_grouped_kernel(const __grid_constant__ CUtensorMap act_tmpl, const __grid_constant__ CUtensorMap wgt_tmpl,
-                      const GroupedParams p) {
+                      const __grid_constant__ CUtensorMap out_tmpl, const GroupedParams p) {
   using Cfg = TcCfg<T, SWAP, TM, TN>;
   constexpr int S = Cfg::kStages;
   constexpr int BK = Cfg::kBK;
@@ -170,7 +327,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* ring = smem;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint8_t* epi_stage = smem + S * Cfg::kStageBytes;  // kEpiBytes, 1024-byte aligned
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + Cfg::kEpiBytes);
   uint64_t* empty = full + S;
   uint64_t* acc_full = empty + S;
   uint64_t* acc_empty = acc_full + 2;
@@ -180,7 +338,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);  // raised by a role that gave up
   volatile int* never = abort + 1;  // stays 0: for waits no abort may cut short
   CUtensorMap* staging = reinterpret_cast<CUtensorMap*>(
-      (reinterpret_cast<uintptr_t>(tmem_slot + 4) + 127) & ~uintptr_t(127));  // [act, wgt]
+      (reinterpret_cast<uintptr_t>(tmem_slot + 4) + 127) & ~uintptr_t(127));  // [act, wgt, out x 4 warps]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -213,7 +371,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     CUtensorMap* slots = reinterpret_cast<CUtensorMap*>(p.desc_slots) +
-                         static_cast<int64_t>(blockIdx.x) * Cfg::kSlots * 2;
+                         static_cast<int64_t>(blockIdx.x) * Cfg::kMapsPerCta;
     const CUtensorMap* act_map = &act_tmpl;
     const CUtensorMap* wgt_map = &wgt_tmpl;
     if (p.single && lane == 0) {
@@ -232,7 +390,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     int slot = -1;
     int built = -1;
     bool ok = true;
-    for (int64_t t = blockIdx.x; ok && walk.seek(p, t); t += gridDim.x) {
+    for (int64_t t = 0; ok && walk.next_tile(p, blockIdx.x, gridDim.x, t);) {
       const Problem& q = walk.prob;
       if (!tma_legal<T>(q)) {
         if (lane == 0 && walk.problem != built) atomicOr(p.error_word, kErrMisaligned);
@@ -317,13 +475,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       uint32_t it = 0;
       uint32_t acc_it = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; ok && walk.seek(p, t); t += gridDim.x) {
+      for (int64_t t = 0; ok && walk.next_tile(p, blockIdx.x, gridDim.x, t);) {
         const Problem& q = walk.prob;
         if (!tma_legal<T>(q) || q.k <= 0) continue;
         const int64_t kblocks = (q.k + BK - 1) / BK;
         const int buf = static_cast<int>(acc_it & 1u);
         if (!mbar_wait(&acc_empty[buf], ((acc_it >> 1) & 1u) ^ 1u, budget, abort)) {
           raise_error(p, kErrWaitAccEmpty, abort);
+          ok = false;
           break;
         }
         tc_fence_after();
@@ -391,7 +550,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     TileWalk<TM, TN> walk;
     uint32_t acc_it = 0;
-    for (int64_t t = blockIdx.x; walk.seek(p, t); t += gridDim.x) {
+    uint8_t* my_blocks = epi_stage + quarter * 2 * kEpiWarpBytes;
+    OutMapRing out_ring{nullptr, staging + 2 + quarter, -1, -1, nullptr};
+    if constexpr (!SWAP) {
+      if (!p.single) {
+        out_ring.slots = reinterpret_cast<CUtensorMap*>(p.desc_slots) +
+                         static_cast<int64_t>(blockIdx.x) * Cfg::kMapsPerCta + 2 * Cfg::kSlots + quarter * kOutSlots;
+      }
+    }
+    const uint64_t pol_out = policy_evict_first();
+    uint32_t chunk_seq = 0;
+    bool ok = true;
+    for (int64_t t = 0; ok && walk.next_tile(p, blockIdx.x, gridDim.x, t);) {
       const Problem& q = walk.prob;
       if (!tma_legal<T>(q)) continue;
       const int64_t m0 = walk.m_block(t) * TM;
@@ -403,9 +573,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         continue;
       }
+      const void* cmap = nullptr;
+      if constexpr (!SWAP) {
+        if (c_tma_legal<T>(q)) cmap = out_map_for<T>(out_ring, p, out_tmpl, q, walk.problem, lane);
+      }
       const int buf = static_cast<int>(acc_it & 1u);
       if (!mbar_wait_warp(&acc_full[buf], (acc_it >> 1) & 1u, budget, abort)) {
         if (lane == 0) raise_error(p, kErrWaitAccFull, abort);
+        ok = false;
         break;
       }
       tc_fence_after();
@@ -430,19 +605,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       } else {
-        const int64_t row = m0 + quarter * 32 + lane;
-#pragma unroll 1
-        for (int j = 0; j < TN / 16; ++j) {
-          uint32_t r[16];
-          tmem_ld16(taddr + j * 16, r);
-          tmem_ld_wait();
-          store_row16<T>(q, row, n0 + j * 16, r);
+        if (cmap != nullptr) {
+          store_rows_tma<T, TN>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32), static_cast<int32_t>(n0),
+                                my_blocks, lane, chunk_seq, pol_out);
+        } else {
+          store_rows_staged<T, TN>(q, taddr, m0 + quarter * 32, n0, my_blocks, lane);
         }
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
       ++acc_it;
     }
+    if (lane == 0) bulk_wait_group_all();  // tensor stores done before the CTA's shared memory goes away
+    __syncwarp();
   }
 
   tc_fence_before();

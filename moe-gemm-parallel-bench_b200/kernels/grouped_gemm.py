@@ -395,7 +395,7 @@ def launch_grouped(
         workspace.shape_signature, workspace.problem_count, workspace.device_signature, workspace.homogeneous,
         aligned, input_precision, workspace.a[0].dtype,
     )
-    candidates = native_candidates(workspace.max_m)
+    candidates = native_candidates(workspace.max_m, workspace.max_k)
     best, _ = autotune_over(
         candidates, lambda c: _launch_native(workspace, c, input_precision, aligned), key, _GROUPED_TUNED
     )

@@ -56,7 +56,7 @@ class KernelConfig:
 native_tile_note = (
     "block_m <= 64 -> swap-AB tile with block_m tokens (16/32/64) x 128 or 256 weight columns; "
     "block_m == 128 -> 128-token MMA tile x 64/128/256 columns; block_m >= 256 -> CTA-pair 256 x 256 tile "
-    "(fp16/bf16) or swap-AB 256 x 128 (fp32)"
+    "(256 x 512 with block_n >= 256) for fp16/bf16, swap-AB 256 x 128 for fp32"
 )
 
 
@@ -276,18 +276,24 @@ TILE_SWAP_32x256 = KernelConfig(32, 256, 64, 4, 8, 4)
 TILE_SWAP_64x256 = KernelConfig(64, 256, 64, 8, 8, 4)
 TILE_TOKENS_128x256 = KernelConfig(128, 256, 64, 8, 8, 4)
 TILE_PAIR_256x256 = KernelConfig(256, 128, 64, 8, 8, 4)  # CTA pair for fp16/bf16, swap-AB 256 x 128 for fp32
+TILE_PAIR_256x512 = KernelConfig(256, 256, 64, 8, 8, 4)  # CTA pair, two 256-column halves (fp16/bf16)
 
 
-def native_candidates(max_m: int) -> tuple[KernelConfig, ...]:
-    """The native tile ``autotune=True`` launches for ``max_m`` token rows.
+def native_candidates(max_m: int, max_k: int | None = None) -> tuple[KernelConfig, ...]:
+    """The native tile ``autotune=True`` launches for ``max_m`` token rows
+    (and reduction depth ``max_k``).
 
-    Measured on B200 over whole DeepSeek-V3 W13 steps (``bench.py
+    Measured on B200 over whole DeepSeek-V3 W13 and W2 steps (``bench.py
     --tile-map``), where the GPU sits at its power cap and every launch's
     energy sets the clock of the others: the token tile fits M exactly (swap-AB
     16 / 32 / 64 tokens x 256 weight columns, so no MMA work is spent on padding
-    rows), 128-token x 256-column tiles at M <= 128, and the CTA-pair 256 x 256
-    tile beyond.  Timing candidates alone at boost clocks (the reference's
-    hot autotune) picks tiles that lose once the GPU is power-capped, so the
+    rows), 128-token x 256-column tiles at M <= 128, and CTA-pair tiles beyond.
+    The 256 x 512 pair tile moves 25% fewer bytes from L2 per MMA than the
+    256 x 256 one but has a single TMEM accumulator (no epilogue overlap) and
+    half as many tiles; it wins from M = 512 and, for K <= 2048, from M = 256
+    (where it also halves the per-problem tensor-map rebuilds of short-K
+    tiles).  Timing candidates alone at boost clocks (the reference's hot
+    autotune) picks tiles that lose once the GPU is power-capped, so the
     policy is fixed rather than re-timed per shape.
     """
     if max_m <= 16:
@@ -298,6 +304,8 @@ def native_candidates(max_m: int) -> tuple[KernelConfig, ...]:
         return (TILE_SWAP_64x256,)
     if max_m <= 128:
         return (TILE_TOKENS_128x256,)
+    if max_m > 256 or (max_k is not None and max_k <= 2048):
+        return (TILE_PAIR_256x512,)
     return (TILE_PAIR_256x256,)
 
 
@@ -364,6 +372,6 @@ def launch_matmul(
         a.data_ptr() % 16 == 0 and b.data_ptr() % 16 == 0,
     )
     best, _ = autotune_over(
-        native_candidates(m), lambda cfg: _launch_once(a, b, c, m, n, k, cfg, precision), key, _MATMUL_TUNED,
+        native_candidates(m, k), lambda cfg: _launch_once(a, b, c, m, n, k, cfg, precision), key, _MATMUL_TUNED,
     )
     _last_tuned = best

@@ -251,12 +251,33 @@ def test_grouped_heterogeneous_tma_aligned(dtype_name):
     assert not ws.homogeneous
     for cfg in (KernelConfig(16, 128, 64, 4, 4, 3), KernelConfig(32, 256, 64, 4, 8, 4),
                 KernelConfig(64, 128, 64, 8, 4, 4), KernelConfig(128, 64, 64, 8, 4, 3),
-                KernelConfig(128, 256, 64, 8, 8, 4), KernelConfig(256, 128, 64, 8, 8, 4)):
+                KernelConfig(128, 256, 64, 8, 8, 4), KernelConfig(256, 128, 64, 8, 8, 4),
+                KernelConfig(256, 256, 64, 8, 8, 4)):
         _poison(ws)
         launch_grouped(ws, config=cfg, autotune=False)
         torch.cuda.synchronize()
         assert ws.launch_info["path"].startswith("tcgen05_tma"), ws.launch_info
         assert ws.scheduler == "generic_persistent"
+        for a, b, c in ws.problem_tensors():
+            _oracle_check(c, a, b, dtype_name)
+
+
+@pytest.mark.parametrize("dtype_name", ["fp16", "bf16"])
+def test_pair_tiles_on_ragged_problems(dtype_name):
+    """CTA-pair tiles (256 x 256 and 256 x 512) where M, N and K end inside a
+    tile: partial M blocks, a K tail shorter than one 64-wide k-block, an N
+    block holding 8 valid columns, and a one-row problem."""
+    torch = _torch()
+    from kernels import KernelConfig, launch_grouped
+
+    shapes = [(300, 320, 520), (513, 128, 1024), (1, 64, 512), (256, 72, 264)]
+    ws = _workspace(shapes, dtype_name, seed=11)
+    for cfg in (KernelConfig(256, 128, 64, 8, 8, 4), KernelConfig(256, 256, 64, 8, 8, 4)):
+        _poison(ws)
+        launch_grouped(ws, config=cfg, autotune=False)
+        torch.cuda.synchronize()
+        assert ws.launch_info["path"] == "tcgen05_tma_pair", ws.launch_info
+        assert ws.launch_info["tile_n"] == (512 if cfg.block_n == 256 else 256)
         for a, b, c in ws.problem_tensors():
             _oracle_check(c, a, b, dtype_name)
 
@@ -315,7 +336,8 @@ def test_homogeneous_multiple_rounds_and_guard_storage(dtype_name, k, n):
         guards.append(storage)
         ws.c[index] = output
         ws.c_ptrs[index] = output.data_ptr()
-    for cfg in (config, KernelConfig(128, 128, 64, 8, 8, 4), KernelConfig(256, 128, 64, 8, 8, 4)):
+    for cfg in (config, KernelConfig(128, 128, 64, 8, 8, 4), KernelConfig(256, 128, 64, 8, 8, 4),
+                KernelConfig(256, 256, 64, 8, 8, 4)):
         for c in ws.c:
             c.fill_(float("nan"))
         launch_grouped(ws, config=cfg, autotune=False)
