@@ -526,7 +526,8 @@ def tile_sweep(args, device) -> None:
 
     m_values = [int(v) for v in args.m_values.split(",")]
     parallel = tuple(p for p in ("EP", "TP") if p in args.parallel.split(","))
-    _, _, _, _, workspaces = build_rank(0, sorted(set(m_values) | {1024}), device, ("EP", "TP"), args.expert_limit)
+    builder = build_rank if args.projection == "W1" else build_rank_w2
+    _, _, _, _, workspaces = builder(0, sorted(set(m_values) | {1024}), device, ("EP", "TP"), args.expert_limit)
     heavy = next(ws for par, m, ws in workspaces if par == "EP" and m == 1024)
     heavy_cfg = KernelConfig(128, 256, 64, 8, 8, 4)
     stream = torch.cuda.Stream(device)
@@ -705,9 +706,9 @@ def main(argv=None) -> int:
         achieved = d_bytes / (dominant["ms"] * 1e-3) / 1e9
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                     "frac": round(achieved / peaks["hbm_gbs"], 3)}
-    roofline.update({"kernel": f"W13 {dominant['parallel']} M_e={dominant['M_e']}",
+    roofline.update({"kernel": f"{'W13' if args.projection == 'W1' else 'W2'} {dominant['parallel']} M_e={dominant['M_e']}",
                      "time_share": round(dominant["ms"] / total_ms, 3), "peak_source": peak_source,
-                     "traffic": traffic_from_profiles(dominant)})
+                     "traffic": traffic_from_profiles(dominant, args.projection)})
     step_roof_ms = sum(roofline_ms(*shapes[key][0], shapes[key][1], peaks)[0] for key in shapes)
 
     # End to end through the public API with host buffers: per step, the
@@ -754,7 +755,11 @@ def main(argv=None) -> int:
         verification = verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_values)
     else:
         verification = {"skipped": "partial workload (--parallel / --expert-limit)"}
-    launches = torch.tensor([len(workspaces) * args.steps], device=device, dtype=torch.int64)
+    # A tensor-core grouped launch is two kernels (tensor-map builder + GEMM);
+    # a single-problem or generic-path launch is one.
+    kernels_per_step = sum(2 if ws.launch_info["path"].startswith("tcgen05") and ws.problem_count > 1 else 1
+                           for _, _, ws in workspaces)
+    launches = torch.tensor([kernels_per_step * args.steps], device=device, dtype=torch.int64)
     if world > 1:
         dist.all_reduce(launches)
     cpu = None
@@ -797,13 +802,13 @@ def main(argv=None) -> int:
     return 0
 
 
-def traffic_from_profiles(dominant: dict):
+def traffic_from_profiles(dominant: dict, projection: str = "W1"):
     """DRAM bytes per launch of the dominant kernel from the committed ncu summary, if any."""
     path = ROOT / "profiles" / "dram_traffic.json"
     if not path.exists():
         return None
     data = json.loads(path.read_text())
-    entry = data.get(f"W13_{dominant['parallel']}_M{dominant['M_e']}")
+    entry = data.get(f"{'W13' if projection == 'W1' else 'W2'}_{dominant['parallel']}_M{dominant['M_e']}")
     return None if entry is None else entry.get("bytes_per_launch")
 
 

@@ -52,9 +52,11 @@ typedef struct mgb_launch_info {
   int32_t tile_m, tile_n, tile_k, stages, grid;
 } mgb_launch_info;
 
-/* Bytes of scratch a grouped launch may need on a device with `sm_count` SMs
- * (per-CTA tensor-map slots of the TMA path).  Replaces nothing in the
- * reference: Triton kernels there take raw pointers and need no descriptors. */
+/* Bytes of scratch a grouped launch of `problem_count` problems needs: the
+ * A, B and C tensor maps of every problem (3 x 128 bytes each), built on the
+ * device by a small kernel that runs just before the GEMM kernel.  `sm_count`
+ * is not used.  Replaces nothing in the reference: Triton kernels there take
+ * raw pointers and need no descriptors. */
 size_t grouped_gemm_scratch_bytes(int32_t problem_count, int32_t sm_count);
 
 /* One launch of the persistent grouped GEMM: for e in [0, problem_count)
@@ -79,6 +81,8 @@ size_t grouped_gemm_scratch_bytes(int32_t problem_count, int32_t sm_count);
  *                error word (never dereferenced).  0 selects the generic path.
  *   scratch      device buffer of at least grouped_gemm_scratch_bytes() bytes,
  *                owned by the caller; not shared by launches that overlap.
+ * A tensor-core launch is two kernels on `stream`: the tensor-map builder
+ * (one warp per problem) and the GEMM kernel.
  */
 int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs,
                         const int32_t* dims, const int64_t* strides, int32_t problem_count,
@@ -112,7 +116,7 @@ int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r,
  * counterpart in the reference (its Triton launches need no scratch).
  *
  * Same arguments and result as grouped_gemm_launch, minus the scratch buffer:
- * the tensor-map slots come from a fixed MGB_NOALLOC_SCRATCH_BYTES array inside
+ * the tensor maps live in a fixed MGB_NOALLOC_SCRATCH_BYTES array inside
  * this library, so the call allocates and frees nothing.  It serves callers
  * with no device allocator of their own -- a plugin in a process whose
  * framework owns all device memory, a launch made while a CUDA graph is being
@@ -121,10 +125,10 @@ int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r,
  *   - The first call on a device looks up the array's device address (once per
  *     device, with that device current); make that first call before any
  *     stream capture.
- *   - A device whose launches could need more than MGB_NOALLOC_SCRATCH_BYTES
- *     (more than 256 SMs) is refused with MGB_ERR_SCRATCH.
+ *   - A launch that needs more than MGB_NOALLOC_SCRATCH_BYTES (more than 2730
+ *     problems) is refused with MGB_ERR_SCRATCH.
  *   - Every call shares the one array and leaves its last contents behind;
- *     nothing in it has to start at zero (each launch writes every slot before
+ *     nothing in it has to start at zero (each launch writes every map before
  *     reading it), but calls that overlap on the GPU -- other streams, other
  *     threads -- race on it and must be serialised by the caller. */
 int grouped_gemm_launch_noalloc(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs,

@@ -26,7 +26,7 @@ using mgb::TcVariantInfo;
 __device__ uint32_t g_error_word;
 
 constexpr int kMaxDevices = 128;
-constexpr size_t kMapsPerCta = 32;  // >= every variant's kMapsPerCta (operand slots + output maps)
+constexpr size_t kMapsPerProblem = 3;  // A, B and C tensor maps per problem (build_maps_kernel)
 constexpr size_t kMapBytes = sizeof(CUtensorMap);
 constexpr long long kDefaultWaitBudget = 2000000000ll;  // ~1 s of SM clock
 
@@ -129,6 +129,15 @@ bool variant_info(int dtype, const TcVariant& v, TcVariantInfo* info) {
     case MGB_FP16: return mgb::tc_variant_info<__half>(v, info);
     case MGB_BF16: return mgb::tc_variant_info<__nv_bfloat16>(v, info);
     default: return mgb::tc_variant_info<float>(v, info);
+  }
+}
+
+int maps_launch_typed(int dtype, const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
+                      const GroupedParams& p, cudaStream_t s) {
+  switch (dtype) {
+    case MGB_FP16: return mgb::maps_launch<__half>(act, wgt, out, p, s);
+    case MGB_BF16: return mgb::maps_launch<__nv_bfloat16>(act, wgt, out, p, s);
+    default: return mgb::maps_launch<float>(act, wgt, out, p, s);
   }
 }
 
@@ -237,9 +246,9 @@ int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r,
 }
 
 size_t grouped_gemm_scratch_bytes(int32_t problem_count, int32_t sm_count) {
-  (void)problem_count;
-  const size_t ctas = sm_count > 0 ? static_cast<size_t>(sm_count) : 1;
-  return ctas * kMapsPerCta * kMapBytes;
+  (void)sm_count;
+  const size_t problems = problem_count > 0 ? static_cast<size_t>(problem_count) : 1;
+  return problems * kMapsPerProblem * kMapBytes;
 }
 
 int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs, const int32_t* dims,
@@ -280,7 +289,7 @@ int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
     const int grid = v.pair ? 2 * grid_for(problem_count, m, n, v.tm, v.tn, std::max(1, vi.max_clusters))
                             : grid_for(problem_count, m, n, v.tm, v.tn, ds.sm_count);
-    const size_t need = static_cast<size_t>(grid) * vi.maps * kMapBytes;
+    const size_t need = static_cast<size_t>(problem_count) * kMapsPerProblem * kMapBytes;
     if (scratch == nullptr || scratch_bytes < need || reinterpret_cast<uintptr_t>(scratch) % 128 != 0) {
       return MGB_ERR_SCRATCH;
     }
@@ -302,6 +311,7 @@ int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
         !encode_out(&out, dtype, scratch, n, m, wgt_pitch)) {
       return MGB_ERR_CUDA;
     }
+    if (maps_launch_typed(dtype, act, wgt, out, p, s) != 0) return MGB_ERR_CUDA;
     const int e = tc_launch_typed(dtype, v, act, wgt, out, p, grid, s);
     if (e != 0) return MGB_ERR_CUDA;
     fill_info(info, 0, v, vi, grid);
@@ -310,7 +320,7 @@ int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
   const int grid = grid_for(problem_count, m, n, mgb::kSimtBM, mgb::kSimtBN, 4ll * ds.sm_count);
   const int e = simt_launch_typed(dtype, p, grid, s);
   if (e != 0) return MGB_ERR_CUDA;
-  fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0, 0}, grid);
+  fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0}, grid);
   return MGB_OK;
 }
 
@@ -345,7 +355,7 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
   p.test_flags = g_test_flags;
   p.error_word = ds.error_word;
   if (m == 0 || n == 0) {
-    fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0, 0}, 0);
+    fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0}, 0);
     return MGB_OK;
   }
 
@@ -380,7 +390,7 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
   const int grid = grid_for(1, m, n, mgb::kSimtBM, mgb::kSimtBN, 4ll * ds.sm_count);
   const int e = simt_launch_typed(dtype, p, grid, s);
   if (e != 0) return MGB_ERR_CUDA;
-  fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0, 0}, grid);
+  fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0}, grid);
   return MGB_OK;
 }
 

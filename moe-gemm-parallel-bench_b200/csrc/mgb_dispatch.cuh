@@ -24,12 +24,10 @@ struct TcVariant {
 struct TcVariantInfo {
   int bk;
   int stages;
-  int slots;
   int smem_bytes;
   int max_clusters = 0;
   int box_rows = 0;  // token rows one CTA loads per stage (the activation box height)
   int box_cols = 0;  // weight columns one CTA loads per stage
-  int maps = 0;      // tensor maps (128 bytes each) one CTA keeps in the scratch buffer
 };
 
 // Returns false for a variant that is not instantiated.
@@ -41,6 +39,12 @@ bool tc_variant_info(const TcVariant& v, TcVariantInfo* info);
 template <typename T>
 int tc_launch(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
               const GroupedParams& p, int grid, cudaStream_t stream);
+
+// Launches build_maps_kernel<T>: the A / B / C tensor maps of every problem
+// of a grouped launch into p.desc_slots; returns a cudaError_t value.
+template <typename T>
+int maps_launch(const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out, const GroupedParams& p,
+                cudaStream_t stream);
 
 // Launches simt_grouped_kernel<T>; returns a cudaError_t value.
 template <typename T>

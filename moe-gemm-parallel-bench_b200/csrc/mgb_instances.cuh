@@ -112,8 +112,8 @@ static bool pair_variant_info(const TcVariant& v, TcVariantInfo* info) {
     return false;
   } else {
     using Cfg = Tc2Cfg<T, NH>;
-    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSlots, Cfg::kSmemBytes, pair_max_clusters<T, NH>(),
-                          Cfg::kHalf, NH * Cfg::kHalf, Cfg::kMapsPerCta};
+    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSmemBytes, pair_max_clusters<T, NH>(), Cfg::kHalf,
+                          NH * Cfg::kHalf};
     return v.tm == Cfg::kTileM && v.tn == Cfg::kTileN;
   }
 }
@@ -124,7 +124,7 @@ bool tc_variant_info<MGB_ELEM>(const TcVariant& v, TcVariantInfo* info) {
 #define MGB_INFO(S, M, N)                                                               \
   if (v.swap == S && v.tm == M && v.tn == N) {                                          \
     using Cfg = TcCfg<MGB_ELEM, S, M, N>;                                               \
-    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSlots, Cfg::kSmemBytes, 0, M, N, Cfg::kMapsPerCta}; \
+    *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSmemBytes, 0, M, N};                \
     return true;                                                                        \
   }
   MGB_FOR_EACH_VARIANT(MGB_INFO)
@@ -144,6 +144,13 @@ int tc_launch<MGB_ELEM>(const TcVariant& v, const CUtensorMap& act, const CUtens
   MGB_FOR_EACH_VARIANT(MGB_LAUNCH)
 #undef MGB_LAUNCH
   return static_cast<int>(cudaErrorInvalidValue);
+}
+
+template <>
+int maps_launch<MGB_ELEM>(const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
+                          const GroupedParams& p, cudaStream_t stream) {
+  build_maps_kernel<MGB_ELEM><<<p.problem_count, 32, 0, stream>>>(act, wgt, out, p);
+  return static_cast<int>(cudaGetLastError());
 }
 
 template <>

@@ -23,9 +23,8 @@
 
 namespace {
 
-// Largest scratch one launch may use: grid x tensor-map slots x 256 bytes.
-// 1 MiB covers a 148-SM B200 (at most 148 x 13 x 256 = 492,544 bytes) with
-// room for devices of up to 256 SMs.
+// Largest scratch one launch may use: 3 tensor maps of 128 bytes per problem,
+// so 1 MiB covers groups of up to 2730 problems (DeepSeek-V3 TP ranks hold 256).
 constexpr size_t kNoAllocScratchBytes = MGB_NOALLOC_SCRATCH_BYTES;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
@@ -63,8 +62,8 @@ int grouped_gemm_launch_noalloc(const int64_t* a_ptrs, const int64_t* b_ptrs, co
   void* scratch = scratch_address(&dev);
   if (scratch == nullptr) return MGB_ERR_CUDA;
   if (cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return MGB_ERR_CUDA;
-  // The launch never needs more than grouped_gemm_scratch_bytes() for this
-  // device; refuse a device whose need exceeds the fixed array.
+  // The launch never needs more than grouped_gemm_scratch_bytes(); refuse a
+  // group whose maps would not fit the fixed array.
   if (grouped_gemm_scratch_bytes(problem_count, sm_count) > kNoAllocScratchBytes) return MGB_ERR_SCRATCH;
   return grouped_gemm_launch(a_ptrs, b_ptrs, c_ptrs, dims, strides, problem_count, homogeneous, m, n, k, dtype,
                              precision, operands_tma_aligned, config, scratch, kNoAllocScratchBytes, stream, info);

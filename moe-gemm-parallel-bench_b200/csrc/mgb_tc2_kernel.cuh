@@ -49,8 +49,6 @@ struct Tc2Cfg {
   static constexpr int kEpiBytes = kEpiBytesRowTile;  // staging blocks of the 4 epilogue warps
   static constexpr int kStagesRaw = (kTcSmemBudget - kEpiBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
-  static constexpr int kSlots = kStages + 1;
-  static constexpr int kMapsPerCta = 2 * kSlots + kOutMapsPerCta;
   static constexpr int kAccCols = kTileN;
   static constexpr int kAccBufs = NH == 1 ? 2 : 1;
   static constexpr int kTmemCols = 512;
@@ -60,7 +58,6 @@ struct Tc2Cfg {
   static_assert(kAccBufs * kAccCols <= kTmemCols, "accumulators fit in TMEM");
   static_assert(kStages >= 3, "operand ring depth");
   static_assert(kSmemBytes <= 232448, "shared memory");
-  static_assert(kMapsPerCta <= kMapsPerCtaLimit, "tensor maps per CTA exceed the scratch region");
 };
 
 template <typename T, int NH>
@@ -85,8 +82,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* never = abort + 1;
-  CUtensorMap* staging = reinterpret_cast<CUtensorMap*>(
-      (reinterpret_cast<uintptr_t>(tmem_slot + 4) + 127) & ~uintptr_t(127));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -123,8 +118,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    CUtensorMap* slots = reinterpret_cast<CUtensorMap*>(p.desc_slots) +
-                         static_cast<int64_t>(blockIdx.x) * Cfg::kMapsPerCta;
     const CUtensorMap* act_map = &act_tmpl;
     const CUtensorMap* wgt_map = &wgt_tmpl;
     if (p.single && lane == 0) {
@@ -140,7 +133,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     const uint64_t pol_act = policy_evict_last();
     TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
     uint32_t it = 0;
-    int slot = -1;
     int built = -1;
     bool ok = true;
     for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
@@ -162,27 +154,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           break;
         }
         if (kb == 0 && !p.single && walk.problem != built) {
-          slot = (slot + 1) % Cfg::kSlots;
-          uint64_t* st = reinterpret_cast<uint64_t*>(staging);
-          st[lane] = lane < 16 ? reinterpret_cast<const uint64_t*>(&act_tmpl)[lane]
-                               : reinterpret_cast<const uint64_t*>(&wgt_tmpl)[lane - 16];
-          __syncwarp();
-          if (lane == 0) {
-            tmap_replace_address(&staging[0], q.a);
-            tmap_replace_address(&staging[1], q.b);
-            if (!p.homogeneous) {
-              tmap_replace_dim(&staging[0], 0, static_cast<uint32_t>(q.k));
-              tmap_replace_dim(&staging[0], 1, static_cast<uint32_t>(q.m));
-              tmap_replace_stride1(&staging[0], static_cast<uint64_t>(q.sam) * sizeof(T));
-              tmap_replace_dim(&staging[1], 0, static_cast<uint32_t>(q.n));
-              tmap_replace_dim(&staging[1], 1, static_cast<uint32_t>(q.k));
-              tmap_replace_stride1(&staging[1], static_cast<uint64_t>(q.sbk) * sizeof(T));
-            }
-          }
-          __syncwarp();
-          CUtensorMap* g = slots + 2 * slot;
-          tmap_publish(&g[0], &staging[0]);
-          tmap_publish(&g[1], &staging[1]);
+          const CUtensorMap* g = problem_maps(p, walk.problem);  // built by build_maps_kernel
           if (lane == 0) {
             tmap_acquire(&g[0]);
             tmap_acquire(&g[1]);
@@ -283,11 +255,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
     uint32_t acc_it = 0;
     uint8_t* my_blocks = epi_stage + quarter * 2 * kEpiWarpBytes;
-    OutMapRing out_ring{nullptr, staging + 2 + quarter, -1, -1, nullptr};
-    if (!p.single) {
-      out_ring.slots = reinterpret_cast<CUtensorMap*>(p.desc_slots) +
-                       static_cast<int64_t>(blockIdx.x) * Cfg::kMapsPerCta + 2 * Cfg::kSlots + quarter * kOutSlots;
-    }
+    int c_built = -1;
     const uint64_t pol_out = policy_evict_first();
     uint32_t chunk_seq = 0;
     bool ok = true;
@@ -303,7 +271,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         }
         continue;
       }
-      const void* cmap = c_tma_legal<T>(q) ? out_map_for<T>(out_ring, p, out_tmpl, q, walk.problem, lane) : nullptr;
+      const void* cmap = c_tma_legal<T>(q) ? out_map_for(p, out_tmpl, walk.problem, c_built, lane) : nullptr;
       const int buf = static_cast<int>(acc_it % NB);
       if (!mbar_wait_warp(&acc_full[buf], (acc_it / NB) & 1u, budget, abort)) {
         if (lane == 0) raise_error(p, kErrWaitAccFull, abort);
@@ -315,7 +283,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
                              static_cast<uint32_t>(buf * Cfg::kAccCols);
       if (cmap != nullptr) {
         store_rows_tma<T, Cfg::kTileN>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
-                                       static_cast<int32_t>(n0), my_blocks, lane, chunk_seq, pol_out);
+                                       static_cast<int32_t>(n0), my_blocks, lane, chunk_seq, pol_out, p.error_word);
       } else {
         store_rows_staged<T, Cfg::kTileN>(q, taddr, m0 + quarter * 32, n0, my_blocks, lane);
       }

@@ -9,8 +9,8 @@
 // :399-482 generic) and of its single GEMM (kernels/matmul.py:223-273).
 //
 // Roles (192 threads):
-//   warp 0      TMA producer.  Rebuilds the per-problem tensor maps in a
-//               per-CTA global slot when the walk enters a new problem.
+//   warp 0      TMA producer.  Grouped launches use the per-problem tensor
+//               maps build_maps_kernel wrote just before this kernel.
 //   warp 1      TMEM allocator; lane 0 issues every tcgen05.mma.
 //   warps 2..5  epilogue (TMEM lanes 32*(warp%4) .. +31).
 //
@@ -36,16 +36,14 @@ namespace mgb {
 
 constexpr int kTcThreads = 192;
 // Dynamic shared memory for the operand ring plus the epilogue staging blocks;
-// 3 KB of the 227 KB a CTA may use stay for barriers, staging maps and the
-// 1024-byte alignment of the ring.
+// 3 KB of the 227 KB a CTA may use stay for barriers and the 1024-byte
+// alignment of the ring.
 constexpr int kTcSmemBudget = 232448 - 3072;
 constexpr int kEpiWarpBytes = 32 * 128;  // one staging block: 32 rows x 128 bytes
 constexpr int kEpiBytesRowTile = 4 * 2 * kEpiWarpBytes;  // 4 epilogue warps x 2 blocks (double-buffered)
-// Output tensor maps: each epilogue warp keeps its own ring of kOutSlots maps
-// in the CTA's scratch region, after the producer's operand-map slots.
-constexpr int kOutSlots = 3;
-constexpr int kOutMapsPerCta = 4 * kOutSlots;
-constexpr int kMapsPerCtaLimit = 32;  // the scratch region per CTA: 32 maps of 128 bytes
+// Tensor maps of a grouped launch: build_maps_kernel writes A, B and C maps of
+// every problem into the scratch buffer before the GEMM kernel runs.
+constexpr int kMapsPerProblem = 3;
 
 constexpr int pow2_at_least(int v) {
   int p = 32;
@@ -69,8 +67,7 @@ struct TcCfg {
   static constexpr int kEpiBytes = SWAP ? 0 : kEpiBytesRowTile;
   static constexpr int kStagesRaw = (kTcSmemBudget - kEpiBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
-  static constexpr int kSlots = kStages + 1;  // operand-map slots per CTA (see producer)
-  static constexpr int kMapsPerCta = 2 * kSlots + (SWAP ? 0 : kOutMapsPerCta);
+
   static constexpr int kAccCols = SWAP ? (TN / 128) * TM : TN;
   static constexpr int kTmemCols = pow2_at_least(2 * kAccCols);
   static constexpr uint32_t kFmt = std::is_same<T, float>::value ? 2u
@@ -91,7 +88,6 @@ struct TcCfg {
   static_assert(TN % 128 == 0 || (!SWAP && TN == 64), "weight tile");
   static_assert(2 * kAccCols <= 512, "two accumulators must fit in TMEM");
   static_assert(kSmemBytes <= 232448, "shared memory");
-  static_assert(kMapsPerCta <= kMapsPerCtaLimit, "tensor maps per CTA exceed the scratch region");
 };
 
 // A problem is served by the TMA path when its operands satisfy the TMA rules:
@@ -191,36 +187,82 @@ __device__ __forceinline__ void write_chunk_smem(const uint32_t (&v)[128 / sizeo
   }
 }
 
-// Row-tile epilogue of one warp through TMA: each chunk is staged in one of
-// the warp's two 4 KB blocks (double-buffered against the store still reading
-// the other) and written by one tensor store of 32 rows x 128 bytes; rows and
+// Writes 32 accumulator columns (one TMEM load unit) of row `lane` into the
+// warp's 32 x 128-byte block at unit position `u` of the row (16-bit: 64
+// bytes, units 0 / 1; fp32: the whole 128-byte row), 16-byte pieces rotated by
+// lane % 8 as in write_chunk_smem.
+template <typename T>
+__device__ __forceinline__ void write_unit_smem(const uint32_t (&v)[32], uint8_t* block, int lane, int u) {
+  uint8_t* my_row = block + lane * 128;
+  if constexpr (sizeof(T) == 4) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      *reinterpret_cast<uint4*>(my_row + ((j ^ (lane & 7)) << 4)) =
+          make_uint4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 packed = make_uint4(pack_pair<T>(v[8 * j], v[8 * j + 1]), pack_pair<T>(v[8 * j + 2], v[8 * j + 3]),
+                                      pack_pair<T>(v[8 * j + 4], v[8 * j + 5]),
+                                      pack_pair<T>(v[8 * j + 6], v[8 * j + 7]));
+      *reinterpret_cast<uint4*>(my_row + (((4 * u + j) ^ (lane & 7)) << 4)) = packed;
+    }
+  }
+}
+
+// Row-tile epilogue of one warp through TMA.  The warp's 32 rows x TN columns
+// are read from TMEM in 32-column units, software-pipelined: the load of unit
+// g + 1 is in flight while unit g is converted and staged.  Each 128-byte-
+// per-row chunk (2 units of 16-bit, 1 of fp32) is staged in one of the warp's
+// two 4 KB blocks (double-buffered against the tensor store still reading the
+// other) and written by one tensor store of 32 rows x 128 bytes; rows and
 // columns past C's extents are clipped by the tensor map.  `seq` counts the
 // warp's chunks across tiles and picks the block.
 template <typename T, int TN>
 __device__ __forceinline__ void store_rows_tma(const Problem& q, const void* cmap, uint32_t taddr, int32_t row0,
                                                int32_t n0, uint8_t* blocks, int lane, uint32_t& seq,
-                                               uint64_t policy) {
+                                               uint64_t policy, uint32_t* error_word) {
   constexpr int kChunkCols = 128 / static_cast<int>(sizeof(T));
+  constexpr int kUnits = kChunkCols / 32;  // TMEM load units per chunk
+  constexpr int kTotal = TN / 32;
   static_assert(TN % kChunkCols == 0, "tile width is a whole number of chunks");
   if (row0 >= q.m) return;  // all 32 rows of this warp lie past C (a ragged last M block)
-#pragma unroll 1
-  for (int c = 0; c < TN / kChunkCols; ++c) {
-    if (n0 + c * kChunkCols >= q.n) break;  // chunks past the last column
-    uint8_t* block = blocks + (seq & 1u) * kEpiWarpBytes;
-    uint32_t v[kChunkCols / 16][16];
-    load_chunk_tmem<T>(taddr, c * kChunkCols, v);
-    if (lane == 0) bulk_wait_group_read<1>();  // the store issued from `block` two chunks ago has read it
-    __syncwarp();
-    tmem_ld_wait();
-    write_chunk_smem<T>(v, block, lane);
-    fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA store
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d(cmap, block, n0 + c * kChunkCols, row0, policy);
-      bulk_commit_group();
+  const int64_t cols_left = q.n - n0;
+  const int chunks = cols_left >= TN ? TN / kChunkCols : static_cast<int>((cols_left + kChunkCols - 1) / kChunkCols);
+  const int units = chunks * kUnits;
+  uint32_t v[2][32];
+  tmem_ld32(taddr, v[0]);
+#pragma unroll
+  for (int g = 0; g < kTotal; ++g) {
+    if (g >= units) break;
+    const int c = g / kUnits;
+    const int u = g % kUnits;
+    uint8_t* block = blocks + ((seq + static_cast<uint32_t>(c)) & 1u) * kEpiWarpBytes;
+    if (u == 0) {
+      if (lane == 0) bulk_wait_group_read<1>();  // the store issued from `block` two chunks ago has read it
+      __syncwarp();
     }
-    ++seq;
+    tmem_ld_wait();  // unit g has landed
+    if (g + 1 < units) tmem_ld32(taddr + (g + 1) * 32, v[(g + 1) & 1]);
+    write_unit_smem<T>(v[g & 1], block, lane, u);
+    if (u == kUnits - 1) {
+      fence_proxy_async_smem();  // generic-proxy writes -> visible to the TMA store
+      __syncwarp();
+      if (lane == 0) {
+        // Guard: a box must start inside C (stores never start at a negative
+        // or past-the-end coordinate); the walk guarantees it.
+        const int32_t x = n0 + c * kChunkCols;
+        if (x >= 0 && row0 >= 0 && x < q.n && row0 < q.m) {
+          tma_store_2d(cmap, block, x, row0, policy);
+          bulk_commit_group();
+        } else {
+          atomicOr(error_word, kErrBadStore);
+        }
+      }
+    }
   }
+  seq += static_cast<uint32_t>(chunks);
 }
 
 // Row-tile epilogue of one warp without TMA (C not addressable by a tensor
@@ -272,48 +314,74 @@ __device__ __forceinline__ void store_rows_staged(const Problem& q, uint32_t tad
   }
 }
 
-// One epilogue warp's output maps: a ring of kOutSlots global maps and a
-// 128-byte shared staging copy.  A map is rebuilt when the warp's walk enters
-// a new problem, before the warp waits for that tile's accumulator, so the
-// rebuild overlaps the tile's MMAs.  A slot is rewritten kOutSlots problems
-// after its last use; by then the warp has waited for every earlier store to
-// finish reading (bulk_wait_group_read<0> below), and a tensor store takes its
-// map when it starts.
-struct OutMapRing {
-  CUtensorMap* slots;
-  CUtensorMap* staging;
-  int slot;
-  int built;
-  const void* current;
-};
+// Tensor maps of problem e in the scratch buffer: [A, B, C].
+__device__ __forceinline__ const CUtensorMap* problem_maps(const GroupedParams& p, int e) {
+  return reinterpret_cast<const CUtensorMap*>(p.desc_slots) + static_cast<int64_t>(kMapsPerProblem) * e;
+}
 
-template <typename T>
-__device__ __forceinline__ const void* out_map_for(OutMapRing& r, const GroupedParams& p, const CUtensorMap& tmpl,
-                                                   const Problem& q, int problem, int lane) {
-  if (p.single) return &tmpl;
-  if (problem != r.built) {
-    if (lane == 0) bulk_wait_group_read<0>();
-    r.slot = (r.slot + 1) % kOutSlots;
-    uint64_t* st = reinterpret_cast<uint64_t*>(r.staging);
-    if (lane < 16) st[lane] = reinterpret_cast<const uint64_t*>(&tmpl)[lane];
-    __syncwarp();
-    if (lane == 0) {
-      tmap_replace_address(r.staging, q.c);
-      if (!p.homogeneous) {
-        tmap_replace_dim(r.staging, 0, static_cast<uint32_t>(q.n));
-        tmap_replace_dim(r.staging, 1, static_cast<uint32_t>(q.m));
-        tmap_replace_stride1(r.staging, static_cast<uint64_t>(q.scm) * sizeof(T));
-      }
-    }
-    __syncwarp();
-    CUtensorMap* g = r.slots + r.slot;
-    tmap_publish(g, r.staging);
+// The output map of the epilogue's current problem: the launch's own map for a
+// single GEMM, else problem e's C map, acquired when the warp first meets e.
+__device__ __forceinline__ const void* out_map_for(const GroupedParams& p, const CUtensorMap& single_map, int e,
+                                                   int& built, int lane) {
+  if (p.single) return &single_map;
+  const CUtensorMap* g = &problem_maps(p, e)[2];
+  if (e != built) {
     if (lane == 0) tmap_acquire(g);
     __syncwarp();
-    r.built = problem;
-    r.current = g;
+    built = e;
   }
-  return r.current;
+  return g;
+}
+
+// Builds the tensor maps of every problem of a grouped launch, one warp per
+// problem: lane 0 copies the three templates (box shape, swizzle and element
+// type final) into shared memory and rewrites the base addresses -- and, for
+// heterogeneous groups, the extents and row pitches -- of the problem; the
+// warp then publishes the three maps to global memory with a release fence
+// for the tensormap proxy.  The GEMM kernel, launched next on the same
+// stream, acquires each map before its first TMA operation.  Problems the TMA
+// cannot address keep the unmodified template (the GEMM kernel never uses it).
+template <typename T>
+__global__ void __launch_bounds__(32)
+    build_maps_kernel(const __grid_constant__ CUtensorMap act_tmpl, const __grid_constant__ CUtensorMap wgt_tmpl,
+                      const __grid_constant__ CUtensorMap out_tmpl, const GroupedParams p) {
+  __shared__ alignas(128) CUtensorMap staging[kMapsPerProblem];
+  const int e = blockIdx.x;
+  const int lane = threadIdx.x;
+  if (e >= p.problem_count) return;
+  if (lane == 0) {
+    const Problem q = load_problem(p, e);
+    const CUtensorMap* tmpl[kMapsPerProblem] = {&act_tmpl, &wgt_tmpl, &out_tmpl};
+    for (int i = 0; i < kMapsPerProblem; ++i) {
+      const uint4* src = reinterpret_cast<const uint4*>(tmpl[i]);
+      uint4* dst = reinterpret_cast<uint4*>(&staging[i]);
+      for (int j = 0; j < 8; ++j) dst[j] = src[j];
+    }
+    const bool sane = q.m > 0 && q.n > 0 && q.k >= 0;
+    if (sane && tma_legal<T>(q)) {
+      tmap_replace_address(&staging[0], q.a);
+      tmap_replace_address(&staging[1], q.b);
+      if (!p.homogeneous) {
+        tmap_replace_dim(&staging[0], 0, static_cast<uint32_t>(q.k));
+        tmap_replace_dim(&staging[0], 1, static_cast<uint32_t>(q.m));
+        tmap_replace_stride1(&staging[0], static_cast<uint64_t>(q.sam) * sizeof(T));
+        tmap_replace_dim(&staging[1], 0, static_cast<uint32_t>(q.n));
+        tmap_replace_dim(&staging[1], 1, static_cast<uint32_t>(q.k));
+        tmap_replace_stride1(&staging[1], static_cast<uint64_t>(q.sbk) * sizeof(T));
+      }
+    }
+    if (sane && c_tma_legal<T>(q)) {
+      tmap_replace_address(&staging[2], q.c);
+      if (!p.homogeneous) {
+        tmap_replace_dim(&staging[2], 0, static_cast<uint32_t>(q.n));
+        tmap_replace_dim(&staging[2], 1, static_cast<uint32_t>(q.m));
+        tmap_replace_stride1(&staging[2], static_cast<uint64_t>(q.scm) * sizeof(T));
+      }
+    }
+  }
+  __syncwarp();
+  CUtensorMap* g = reinterpret_cast<CUtensorMap*>(p.desc_slots) + static_cast<int64_t>(kMapsPerProblem) * e;
+  for (int i = 0; i < kMapsPerProblem; ++i) tmap_publish(&g[i], &staging[i]);
 }
 
 template <typename T, bool SWAP, int TM, int TN>
@@ -337,8 +405,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);  // raised by a role that gave up
   volatile int* never = abort + 1;  // stays 0: for waits no abort may cut short
-  CUtensorMap* staging = reinterpret_cast<CUtensorMap*>(
-      (reinterpret_cast<uintptr_t>(tmem_slot + 4) + 127) & ~uintptr_t(127));  // [act, wgt, out x 4 warps]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -370,8 +436,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    CUtensorMap* slots = reinterpret_cast<CUtensorMap*>(p.desc_slots) +
-                         static_cast<int64_t>(blockIdx.x) * Cfg::kMapsPerCta;
     const CUtensorMap* act_map = &act_tmpl;
     const CUtensorMap* wgt_map = &wgt_tmpl;
     if (p.single && lane == 0) {
@@ -387,7 +451,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint64_t pol_act = policy_evict_last();
     TileWalk<TM, TN> walk;
     uint32_t it = 0;
-    int slot = -1;
     int built = -1;
     bool ok = true;
     for (int64_t t = 0; ok && walk.next_tile(p, blockIdx.x, gridDim.x, t);) {
@@ -409,31 +472,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           break;
         }
         if (kb == 0 && !p.single && walk.problem != built) {
-          // Entering a new problem: rebuild its two tensor maps in the next
-          // slot.  A slot is reused only kSlots problems later; each problem
-          // issues at least one load, so by then the stage wait just above
-          // has proven that every load that read the old maps has landed.
-          slot = (slot + 1) % Cfg::kSlots;
-          uint64_t* st = reinterpret_cast<uint64_t*>(staging);
-          st[lane] = lane < 16 ? reinterpret_cast<const uint64_t*>(&act_tmpl)[lane]
-                               : reinterpret_cast<const uint64_t*>(&wgt_tmpl)[lane - 16];
-          __syncwarp();
-          if (lane == 0) {
-            tmap_replace_address(&staging[0], q.a);
-            tmap_replace_address(&staging[1], q.b);
-            if (!p.homogeneous) {
-              tmap_replace_dim(&staging[0], 0, static_cast<uint32_t>(q.k));
-              tmap_replace_dim(&staging[0], 1, static_cast<uint32_t>(q.m));
-              tmap_replace_stride1(&staging[0], static_cast<uint64_t>(q.sam) * sizeof(T));
-              tmap_replace_dim(&staging[1], 0, static_cast<uint32_t>(q.n));
-              tmap_replace_dim(&staging[1], 1, static_cast<uint32_t>(q.k));
-              tmap_replace_stride1(&staging[1], static_cast<uint64_t>(q.sbk) * sizeof(T));
-            }
-          }
-          __syncwarp();
-          CUtensorMap* g = slots + 2 * slot;
-          tmap_publish(&g[0], &staging[0]);
-          tmap_publish(&g[1], &staging[1]);
+          // Entering a new problem: its maps were built before this kernel
+          // started (build_maps_kernel); acquire them for the tensormap proxy.
+          const CUtensorMap* g = problem_maps(p, walk.problem);
           if (lane == 0) {
             tmap_acquire(&g[0]);
             tmap_acquire(&g[1]);
@@ -551,13 +592,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     TileWalk<TM, TN> walk;
     uint32_t acc_it = 0;
     uint8_t* my_blocks = epi_stage + quarter * 2 * kEpiWarpBytes;
-    OutMapRing out_ring{nullptr, staging + 2 + quarter, -1, -1, nullptr};
-    if constexpr (!SWAP) {
-      if (!p.single) {
-        out_ring.slots = reinterpret_cast<CUtensorMap*>(p.desc_slots) +
-                         static_cast<int64_t>(blockIdx.x) * Cfg::kMapsPerCta + 2 * Cfg::kSlots + quarter * kOutSlots;
-      }
-    }
+    int c_built = -1;
     const uint64_t pol_out = policy_evict_first();
     uint32_t chunk_seq = 0;
     bool ok = true;
@@ -575,7 +610,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       const void* cmap = nullptr;
       if constexpr (!SWAP) {
-        if (c_tma_legal<T>(q)) cmap = out_map_for<T>(out_ring, p, out_tmpl, q, walk.problem, lane);
+        if (c_tma_legal<T>(q)) cmap = out_map_for(p, out_tmpl, walk.problem, c_built, lane);
       }
       const int buf = static_cast<int>(acc_it & 1u);
       if (!mbar_wait_warp(&acc_full[buf], (acc_it >> 1) & 1u, budget, abort)) {
@@ -607,7 +642,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       } else {
         if (cmap != nullptr) {
           store_rows_tma<T, TN>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32), static_cast<int32_t>(n0),
-                                my_blocks, lane, chunk_seq, pol_out);
+                                my_blocks, lane, chunk_seq, pol_out, p.error_word);
         } else {
           store_rows_staged<T, TN>(q, taddr, m0 + quarter * 32, n0, my_blocks, lane);
         }

@@ -48,6 +48,7 @@ ERROR_BITS = {
     1 << 5: "a problem's operands broke the TMA alignment promise and were skipped",
     1 << 6: "a problem had invalid dimensions and was skipped",
     1 << 7: "test-only barrier wait timed out",
+    1 << 8: "an output tile store fell outside C and was not issued (kernel bug)",
 }
 TEST_WAIT_BIT = 1 << 7
 
