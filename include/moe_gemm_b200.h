@@ -90,6 +90,25 @@ int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
                         int32_t precision, int32_t operands_tma_aligned, const mgb_tile_config* config,
                         void* scratch, size_t scratch_bytes, void* stream, mgb_launch_info* info);
 
+/* Grouped GEMM with the fused SwiGLU epilogue: for e in [0, problem_count)
+ *   C_e[M_e, N_e/2] = silu(A_e @ B_e[:, :N_e/2]) * (A_e @ B_e[:, N_e/2:])
+ * (silu(x) = x / (1 + exp(-x)), fp32 accumulate, epilogue math in fp32, one
+ * cast on store).  B_e is the packed W13 weight [gate | up] of
+ * build_fused_gate_up_workspace (kernels/grouped_gemm.py:575-594); the tables
+ * and arguments are those of grouped_gemm_launch, with (m, n, k) and `dims`
+ * giving the packed N and `strides` C's [M, N/2] strides.  Runs on the
+ * tensor-core path only: fp16 / bf16, or fp32 with MGB_TF32, TMA-aligned A / B
+ * (operands_tma_aligned = 1) and N/2 a multiple of 16 bytes of elements;
+ * otherwise MGB_ERR_UNSUPPORTED (MGB_ERR_INVALID for odd N).  No counterpart
+ * in the reference, which leaves SiLU(gate) * up outside its timed GEMM
+ * (README.md:55-60): this writes [M, F] instead of [M, 2F] and never reads
+ * the [gate | up] intermediate back. */
+int grouped_gemm_swiglu_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs,
+                               const int32_t* dims, const int64_t* strides, int32_t problem_count,
+                               int32_t homogeneous, int64_t m, int64_t n, int64_t k, int32_t dtype,
+                               int32_t precision, int32_t operands_tma_aligned, const mgb_tile_config* config,
+                               void* scratch, size_t scratch_bytes, void* stream, mgb_launch_info* info);
+
 /* Masked single GEMM C[m, n] = A[m, k] @ B[k, n] with arbitrary element strides.
  * Replaces the Triton launch of launch_matmul (kernels/matmul.py:332-392,
  * kernel _matmul_kernel_impl :223-273).  Operands that satisfy the TMA rules

@@ -251,15 +251,21 @@ size_t grouped_gemm_scratch_bytes(int32_t problem_count, int32_t sm_count) {
   return problems * kMapsPerProblem * kMapBytes;
 }
 
-int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs, const int32_t* dims,
+}  // extern "C"
+
+namespace {
+
+// Both grouped entry points: swiglu = 1 selects the fused SwiGLU epilogue.
+int grouped_launch_impl(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs, const int32_t* dims,
                         const int64_t* strides, int32_t problem_count, int32_t homogeneous, int64_t m, int64_t n,
                         int64_t k, int32_t dtype, int32_t precision, int32_t operands_tma_aligned,
                         const mgb_tile_config* config, void* scratch, size_t scratch_bytes, void* stream,
-                        mgb_launch_info* info) {
+                        mgb_launch_info* info, int swiglu) {
   if (!valid_dtype(dtype, precision) || problem_count <= 0 || a_ptrs == nullptr || b_ptrs == nullptr ||
       c_ptrs == nullptr || m < 0 || n < 0 || k < 0) {
     return MGB_ERR_INVALID;
   }
+  if (swiglu && n % 2 != 0) return MGB_ERR_INVALID;
   if (!homogeneous && (dims == nullptr || strides == nullptr)) return MGB_ERR_INVALID;
   DeviceState ds;
   if (int st = device_state(&ds)) return st;
@@ -280,11 +286,20 @@ int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
   p.wait_budget = g_wait_budget;
   p.test_flags = g_test_flags;
   p.error_word = ds.error_word;
+  p.swiglu = swiglu ? 1 : 0;
 
   const bool tensor_core = operands_tma_aligned && (dtype != MGB_FP32 || precision == MGB_TF32) && m > 0 &&
                            n > 0 && k > 0;
+  if (swiglu && !tensor_core) return MGB_ERR_UNSUPPORTED;  // the fused epilogue exists on the tensor-core path only
   if (tensor_core) {
-    const TcVariant v = pick_variant(config, dtype);
+    TcVariant v = pick_variant(config, dtype);
+    if (swiglu && !v.pair) {
+      // The SwiGLU epilogue pairs gate and up inside one tile: swap-AB tiles
+      // need two 128-column weight chunks, row tiles at least 64 output columns.
+      if (v.swap && v.tm == 256) v = TcVariant{false, 128, 256};
+      if (v.swap && v.tn < 256) v.tn = 256;
+      if (!v.swap && v.tn < 128) v.tn = 128;
+    }
     TcVariantInfo vi;
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
     const int grid = v.pair ? 2 * grid_for(problem_count, m, n, v.tm, v.tn, std::max(1, vi.max_clusters))
@@ -305,10 +320,12 @@ int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
     const int es = elem_size(dtype);
     const uint64_t act_pitch = ((static_cast<uint64_t>(k) * es + 15) / 16) * 16;
     const uint64_t wgt_pitch = ((static_cast<uint64_t>(n) * es + 15) / 16) * 16;
+    const uint64_t out_n = swiglu ? static_cast<uint64_t>(n) / 2 : static_cast<uint64_t>(n);
+    const uint64_t out_pitch = ((out_n * es + 15) / 16) * 16;
     CUtensorMap act, wgt, out;
     if (!encode_2d(&act, dtype, scratch, k, m, act_pitch, vi.bk, vi.box_rows, kActSwizzle) ||
         !encode_2d(&wgt, dtype, scratch, n, k, wgt_pitch, vi.bk, vi.bk, wgt_swizzle(dtype)) ||
-        !encode_out(&out, dtype, scratch, n, m, wgt_pitch)) {
+        !encode_out(&out, dtype, scratch, out_n, m, out_pitch)) {
       return MGB_ERR_CUDA;
     }
     if (maps_launch_typed(dtype, act, wgt, out, p, s) != 0) return MGB_ERR_CUDA;
@@ -322,6 +339,28 @@ int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
   if (e != 0) return MGB_ERR_CUDA;
   fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0}, grid);
   return MGB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs, const int32_t* dims,
+                        const int64_t* strides, int32_t problem_count, int32_t homogeneous, int64_t m, int64_t n,
+                        int64_t k, int32_t dtype, int32_t precision, int32_t operands_tma_aligned,
+                        const mgb_tile_config* config, void* scratch, size_t scratch_bytes, void* stream,
+                        mgb_launch_info* info) {
+  return grouped_launch_impl(a_ptrs, b_ptrs, c_ptrs, dims, strides, problem_count, homogeneous, m, n, k, dtype,
+                             precision, operands_tma_aligned, config, scratch, scratch_bytes, stream, info, 0);
+}
+
+int grouped_gemm_swiglu_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs,
+                               const int32_t* dims, const int64_t* strides, int32_t problem_count,
+                               int32_t homogeneous, int64_t m, int64_t n, int64_t k, int32_t dtype,
+                               int32_t precision, int32_t operands_tma_aligned, const mgb_tile_config* config,
+                               void* scratch, size_t scratch_bytes, void* stream, mgb_launch_info* info) {
+  return grouped_launch_impl(a_ptrs, b_ptrs, c_ptrs, dims, strides, problem_count, homogeneous, m, n, k, dtype,
+                             precision, operands_tma_aligned, config, scratch, scratch_bytes, stream, info, 1);
 }
 
 int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k, int64_t stride_am,

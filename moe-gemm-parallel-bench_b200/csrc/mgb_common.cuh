@@ -38,6 +38,7 @@ struct GroupedParams {
   // Scratch for the per-CTA tensor-map slots of the TMA path.
   uint8_t* desc_slots;
   int32_t unit_tiles;     // tensor-core kernels: consecutive tiles of one problem a CTA takes at a time
+  int32_t swiglu;         // 1: fused SwiGLU epilogue, C_e[M, N/2] = silu(A_e B_e[:, :N/2]) * (A_e B_e[:, N/2:])
   long long wait_budget;  // SM clock cycles a barrier wait may take before the launch gives up
   int32_t test_flags;     // bit 0: make the epilogue wait on a barrier nothing arrives on
   uint32_t* error_word;   // where error bits are OR-ed (a __device__ word of this library)
@@ -65,8 +66,9 @@ __device__ __forceinline__ Problem load_problem(const GroupedParams& p, int e) {
   q.b = reinterpret_cast<const char*>(p.b_ptrs[e]);
   q.c = reinterpret_cast<char*>(p.c_ptrs[e]);
   if (p.homogeneous) {
+    // Contiguous operands; C has N columns, or N/2 with the SwiGLU epilogue.
     q.m = p.m; q.n = p.n; q.k = p.k;
-    q.sam = p.k; q.sak = 1; q.sbk = p.n; q.sbn = 1; q.scm = p.n; q.scn = 1;
+    q.sam = p.k; q.sak = 1; q.sbk = p.n; q.sbn = 1; q.scm = p.swiglu ? p.n / 2 : p.n; q.scn = 1;
   } else {
     q.m = p.dims[3 * e + 0];
     q.n = p.dims[3 * e + 1];

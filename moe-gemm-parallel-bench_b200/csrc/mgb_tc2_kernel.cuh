@@ -137,14 +137,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     bool ok = true;
     for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
       const Problem& q = walk.prob;
-      if (!tma_legal<T>(q)) {
+      if (!tile_legal<T>(p, q)) {
         if (lane == 0 && walk.problem != built) atomicOr(p.error_word, kErrMisaligned);
         continue;
       }
       const int64_t kblocks = (q.k + BK - 1) / BK;
       const uint64_t pol_wgt = walk.m_blocks > 1 ? pol_shared : pol_stream;
       const int32_t m0 = static_cast<int32_t>(walk.m_block(t) * Cfg::kTileM + rank * Cfg::kHalf);
-      const int32_t n0 = static_cast<int32_t>(walk.n_block(t) * Cfg::kTileN + rank * Cfg::kHalf);  // + 256 h
+      const int64_t nb = walk.n_block(t);
       for (int64_t kb = 0; kb < kblocks; ++kb) {
         const int s = static_cast<int>(it % S);
         const uint32_t phase = (it / S) & 1u;
@@ -175,8 +175,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           for (int h = 0; h < NH; ++h) {
 #pragma unroll
             for (int j = 0; j < Cfg::kHalf / BK; ++j) {
+              // Tile-local column 256 h + 128 rank + 64 j (CTA rank's half of MMA half h).
               tma_load_2d_pair(wgt_map, bar, st_wgt + h * Cfg::kHalfWgtBytes + j * Cfg::kBoxBytes,
-                               n0 + 256 * h + j * BK, kx, pol_wgt);
+                               weight_col<Cfg::kTileN>(p, q, nb, 256 * h + Cfg::kHalf * rank + j * BK), kx,
+                               pol_wgt);
             }
           }
         }
@@ -202,7 +204,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       bool ok = true;
       for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
         const Problem& q = walk.prob;
-        if (!tma_legal<T>(q) || q.k <= 0) continue;
+        if (!tile_legal<T>(p, q) || q.k <= 0) continue;
         const int64_t kblocks = (q.k + BK - 1) / BK;
         const int buf = static_cast<int>(acc_it % NB);
         if (!mbar_wait(&acc_empty[buf], ((acc_it / NB) & 1u) ^ 1u, budget, abort)) {
@@ -260,18 +262,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     uint32_t chunk_seq = 0;
     bool ok = true;
     for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
-      const Problem& q = walk.prob;
-      if (!tma_legal<T>(q)) continue;
+      if (!tile_legal<T>(p, walk.prob)) continue;
+      Problem q = walk.prob;
+      q.n = out_cols(p, q);  // the epilogue addresses C: N/2 columns with SwiGLU
+      const int tile_out = p.swiglu ? Cfg::kTileN / 2 : Cfg::kTileN;
       const int64_t m0 = walk.m_block(t) * Cfg::kTileM + rank * Cfg::kHalf;
-      const int64_t n0 = walk.n_block(t) * Cfg::kTileN;
+      const int64_t n0 = walk.n_block(t) * tile_out;
       if (q.k <= 0) {
-        for (int idx = ethread; idx < Cfg::kHalf * Cfg::kTileN; idx += 128) {
-          const int64_t row = m0 + idx / Cfg::kTileN, col = n0 + idx % Cfg::kTileN;
+        for (int idx = ethread; idx < Cfg::kHalf * tile_out; idx += 128) {
+          const int64_t row = m0 + idx / tile_out, col = n0 + idx % tile_out;
           if (row < q.m && col < q.n) store_scalar<T>(q.c, row * q.scm + col * q.scn, 0.0f);
         }
         continue;
       }
-      const void* cmap = c_tma_legal<T>(q) ? out_map_for(p, out_tmpl, walk.problem, c_built, lane) : nullptr;
+      const void* cmap = c_tma_legal<T>(q, q.n) ? out_map_for(p, out_tmpl, walk.problem, c_built, lane) : nullptr;
       const int buf = static_cast<int>(acc_it % NB);
       if (!mbar_wait_warp(&acc_full[buf], (acc_it / NB) & 1u, budget, abort)) {
         if (lane == 0) raise_error(p, kErrWaitAccFull, abort);
@@ -281,7 +285,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(buf * Cfg::kAccCols);
-      if (cmap != nullptr) {
+      if (p.swiglu) {
+        if (cmap != nullptr) {
+          store_rows_tma_swiglu<T, Cfg::kTileN / 2>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
+                                                    static_cast<int32_t>(n0), my_blocks, lane, chunk_seq, pol_out,
+                                                    p.error_word);
+        } else {
+          store_rows_scalar_swiglu<T, Cfg::kTileN / 2>(q, taddr, m0 + quarter * 32, n0, lane);
+        }
+      } else if (cmap != nullptr) {
         store_rows_tma<T, Cfg::kTileN>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
                                        static_cast<int32_t>(n0), my_blocks, lane, chunk_seq, pol_out, p.error_word);
       } else {

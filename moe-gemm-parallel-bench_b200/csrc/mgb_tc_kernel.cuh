@@ -105,11 +105,41 @@ __device__ __forceinline__ bool tma_legal(const Problem& q) {
 // C is stored by TMA when its base is 16-byte aligned, its columns are unit
 // stride and its rows are whole multiples of 16 bytes apart (and do not overlap).
 template <typename T>
-__device__ __forceinline__ bool c_tma_legal(const Problem& q) {
+__device__ __forceinline__ bool c_tma_legal(const Problem& q, int64_t cols) {
   constexpr int E = static_cast<int>(sizeof(T));
-  return (reinterpret_cast<uint64_t>(q.c) % 16 == 0) && q.scn == 1 && q.scm >= q.n && (q.scm * E) % 16 == 0 &&
-         q.m < (1ll << 31) && q.n < (1ll << 31);
+  return (reinterpret_cast<uint64_t>(q.c) % 16 == 0) && q.scn == 1 && q.scm >= cols && (q.scm * E) % 16 == 0 &&
+         q.m < (1ll << 31) && cols < (1ll << 31);
 }
+
+// Columns of C: N, or N / 2 with the fused SwiGLU epilogue (B_e packed [gate | up]).
+__device__ __forceinline__ int64_t out_cols(const GroupedParams& p, const Problem& q) {
+  return p.swiglu ? q.n / 2 : q.n;
+}
+
+// A problem runs on the tensor-core path when its operands satisfy the TMA
+// rules; with the SwiGLU epilogue its packed weight must also split at a
+// 16-byte boundary, so the boxes of the up half start aligned.
+template <typename T>
+__device__ __forceinline__ bool tile_legal(const GroupedParams& p, const Problem& q) {
+  if (!tma_legal<T>(q)) return false;
+  if (!p.swiglu) return true;
+  return q.n % 2 == 0 && ((q.n / 2) * static_cast<int64_t>(sizeof(T))) % 16 == 0;
+}
+
+// Weight column loaded at tile-local column j of a TN-wide tile.  Plain: the
+// tile covers weight columns [TN nb, TN nb + TN).  SwiGLU: the tile produces
+// output columns [o, o + TN/2), o = nb TN/2, from gate columns o + j (j < TN/2)
+// and up columns N/2 + o + j - TN/2, so gate and up of one output column sit
+// TN/2 accumulator columns apart.  Columns past the gate half (last tile) read
+// up values into accumulator columns whose outputs lie past C and are not stored.
+template <int TN>
+__device__ __forceinline__ int32_t weight_col(const GroupedParams& p, const Problem& q, int64_t nb, int j) {
+  if (!p.swiglu) return static_cast<int32_t>(nb * TN + j);
+  const int64_t o = nb * (TN / 2);
+  return static_cast<int32_t>(j < TN / 2 ? o + j : q.n / 2 + o + (j - TN / 2));
+}
+
+__device__ __forceinline__ float silu_mul(float g, float u) { return g / (1.0f + __expf(-g)) * u; }
 
 __device__ __forceinline__ void raise_error(const GroupedParams& p, uint32_t bits, volatile int* abort) {
   atomicOr(p.error_word, bits);
@@ -265,6 +295,78 @@ __device__ __forceinline__ void store_rows_tma(const Problem& q, const void* cma
   seq += static_cast<uint32_t>(chunks);
 }
 
+// Row-tile SwiGLU epilogue of one warp through TMA: gate accumulators are
+// TMEM columns [0, TO), up columns [TO, 2 TO); each 32-column output unit
+// loads both, computes silu(gate) * up in fp32 and is staged and stored like
+// store_rows_tma.
+template <typename T, int TO>
+__device__ __forceinline__ void store_rows_tma_swiglu(const Problem& qo, const void* cmap, uint32_t taddr,
+                                                      int32_t row0, int32_t o0, uint8_t* blocks, int lane,
+                                                      uint32_t& seq, uint64_t policy, uint32_t* error_word) {
+  constexpr int kChunkCols = 128 / static_cast<int>(sizeof(T));
+  constexpr int kUnits = kChunkCols / 32;
+  static_assert(TO % kChunkCols == 0, "output tile width is a whole number of chunks");
+  if (row0 >= qo.m) return;
+  const int64_t cols_left = qo.n - o0;
+  const int chunks = cols_left >= TO ? TO / kChunkCols : static_cast<int>((cols_left + kChunkCols - 1) / kChunkCols);
+  const int units = chunks * kUnits;
+#pragma unroll 1
+  for (int g = 0; g < units; ++g) {
+    const int c = g / kUnits;
+    const int u = g % kUnits;
+    uint8_t* block = blocks + ((seq + static_cast<uint32_t>(c)) & 1u) * kEpiWarpBytes;
+    if (u == 0) {
+      if (lane == 0) bulk_wait_group_read<1>();
+      __syncwarp();
+    }
+    uint32_t gate[32], up[32];
+    tmem_ld32(taddr + g * 32, gate);
+    tmem_ld32(taddr + TO + g * 32, up);
+    tmem_ld_wait();
+#pragma unroll
+    for (int i = 0; i < 32; ++i) gate[i] = __float_as_uint(silu_mul(__uint_as_float(gate[i]), __uint_as_float(up[i])));
+    write_unit_smem<T>(gate, block, lane, u);
+    if (u == kUnits - 1) {
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int32_t x = o0 + c * kChunkCols;
+        if (x >= 0 && row0 >= 0 && x < qo.n && row0 < qo.m) {
+          tma_store_2d(cmap, block, x, row0, policy);
+          bulk_commit_group();
+        } else {
+          atomicOr(error_word, kErrBadStore);
+        }
+      }
+    }
+  }
+  seq += static_cast<uint32_t>(chunks);
+}
+
+// Row-tile SwiGLU epilogue without TMA (C not addressable by a tensor map):
+// element stores with bounds checks.
+template <typename T, int TO>
+__device__ __forceinline__ void store_rows_scalar_swiglu(const Problem& qo, uint32_t taddr, int64_t row0, int64_t o0,
+                                                         int lane) {
+  const int64_t row = row0 + lane;
+#pragma unroll 1
+  for (int g = 0; g < TO / 32; ++g) {
+    uint32_t gate[32], up[32];
+    tmem_ld32(taddr + g * 32, gate);
+    tmem_ld32(taddr + TO + g * 32, up);
+    tmem_ld_wait();
+    if (row < qo.m) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int64_t col = o0 + g * 32 + i;
+        if (col < qo.n) {
+          store_scalar<T>(qo.c, row * qo.scm + col * qo.scn, silu_mul(__uint_as_float(gate[i]), __uint_as_float(up[i])));
+        }
+      }
+    }
+  }
+}
+
 // Row-tile epilogue of one warp without TMA (C not addressable by a tensor
 // map): the chunk goes through `block` and is read back so that every global
 // store instruction writes four whole 128-byte row segments.
@@ -358,7 +460,7 @@ __global__ void __launch_bounds__(32)
       for (int j = 0; j < 8; ++j) dst[j] = src[j];
     }
     const bool sane = q.m > 0 && q.n > 0 && q.k >= 0;
-    if (sane && tma_legal<T>(q)) {
+    if (sane && tile_legal<T>(p, q)) {
       tmap_replace_address(&staging[0], q.a);
       tmap_replace_address(&staging[1], q.b);
       if (!p.homogeneous) {
@@ -370,10 +472,10 @@ __global__ void __launch_bounds__(32)
         tmap_replace_stride1(&staging[1], static_cast<uint64_t>(q.sbk) * sizeof(T));
       }
     }
-    if (sane && c_tma_legal<T>(q)) {
+    if (sane && c_tma_legal<T>(q, out_cols(p, q))) {
       tmap_replace_address(&staging[2], q.c);
       if (!p.homogeneous) {
-        tmap_replace_dim(&staging[2], 0, static_cast<uint32_t>(q.n));
+        tmap_replace_dim(&staging[2], 0, static_cast<uint32_t>(out_cols(p, q)));
         tmap_replace_dim(&staging[2], 1, static_cast<uint32_t>(q.m));
         tmap_replace_stride1(&staging[2], static_cast<uint64_t>(q.scm) * sizeof(T));
       }
@@ -455,14 +557,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     bool ok = true;
     for (int64_t t = 0; ok && walk.next_tile(p, blockIdx.x, gridDim.x, t);) {
       const Problem& q = walk.prob;
-      if (!tma_legal<T>(q)) {
+      if (!tile_legal<T>(p, q)) {
         if (lane == 0 && walk.problem != built) atomicOr(p.error_word, kErrMisaligned);
         continue;
       }
       const int64_t kblocks = (q.k + BK - 1) / BK;
       const uint64_t pol_wgt = walk.m_blocks > 1 ? pol_shared : pol_stream;
       const int32_t m0 = static_cast<int32_t>(walk.m_block(t) * TM);
-      const int32_t n0 = static_cast<int32_t>(walk.n_block(t) * TN);
+      const int64_t nb = walk.n_block(t);
       for (int64_t kb = 0; kb < kblocks; ++kb) {
         const int s = static_cast<int>(it % S);
         const uint32_t phase = (it / S) & 1u;
@@ -492,7 +594,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tma_load_2d(act_map, &full[s], st_act, kx, m0, pol_act);
 #pragma unroll
           for (int j = 0; j < TN / BK; ++j) {
-            tma_load_2d(wgt_map, &full[s], st_wgt + j * Cfg::kBoxBytes, n0 + j * BK, kx, pol_wgt);
+            tma_load_2d(wgt_map, &full[s], st_wgt + j * Cfg::kBoxBytes, weight_col<TN>(p, q, nb, j * BK), kx,
+                        pol_wgt);
           }
         }
         __syncwarp();
@@ -518,7 +621,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       bool ok = true;
       for (int64_t t = 0; ok && walk.next_tile(p, blockIdx.x, gridDim.x, t);) {
         const Problem& q = walk.prob;
-        if (!tma_legal<T>(q) || q.k <= 0) continue;
+        if (!tile_legal<T>(p, q) || q.k <= 0) continue;
         const int64_t kblocks = (q.k + BK - 1) / BK;
         const int buf = static_cast<int>(acc_it & 1u);
         if (!mbar_wait(&acc_empty[buf], ((acc_it >> 1) & 1u) ^ 1u, budget, abort)) {
@@ -597,20 +700,22 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint32_t chunk_seq = 0;
     bool ok = true;
     for (int64_t t = 0; ok && walk.next_tile(p, blockIdx.x, gridDim.x, t);) {
-      const Problem& q = walk.prob;
-      if (!tma_legal<T>(q)) continue;
+      if (!tile_legal<T>(p, walk.prob)) continue;
+      Problem q = walk.prob;
+      q.n = out_cols(p, q);  // the epilogue addresses C: N/2 columns with SwiGLU
+      const int tile_out = p.swiglu ? TN / 2 : TN;
       const int64_t m0 = walk.m_block(t) * TM;
-      const int64_t n0 = walk.n_block(t) * TN;
+      const int64_t n0 = walk.n_block(t) * tile_out;
       if (q.k <= 0) {
-        for (int idx = ethread; idx < TM * TN; idx += 128) {
-          const int64_t row = m0 + idx / TN, col = n0 + idx % TN;
+        for (int idx = ethread; idx < TM * tile_out; idx += 128) {
+          const int64_t row = m0 + idx / tile_out, col = n0 + idx % tile_out;
           if (row < q.m && col < q.n) store_scalar<T>(q.c, row * q.scm + col * q.scn, 0.0f);
         }
         continue;
       }
       const void* cmap = nullptr;
       if constexpr (!SWAP) {
-        if (c_tma_legal<T>(q)) cmap = out_map_for(p, out_tmpl, walk.problem, c_built, lane);
+        if (c_tma_legal<T>(q, q.n)) cmap = out_map_for(p, out_tmpl, walk.problem, c_built, lane);
       }
       const int buf = static_cast<int>(acc_it & 1u);
       if (!mbar_wait_warp(&acc_full[buf], (acc_it >> 1) & 1u, budget, abort)) {
@@ -622,6 +727,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(buf * Cfg::kAccCols);
       if constexpr (SWAP) {
+        if constexpr (TN >= 256) {
+          if (p.swiglu) {
+            // Chunk 0 holds gate, chunk 1 up, of the same 128 output columns:
+            // lane l of quarter w owns output column n0 + 32 w + l.
+            const int64_t col = n0 + quarter * 32 + lane;
+#pragma unroll 1
+            for (int j = 0; j < TM / 16; ++j) {
+              uint32_t g[16], u[16];
+              tmem_ld16(taddr + j * 16, g);
+              tmem_ld16(taddr + TM + j * 16, u);
+              tmem_ld_wait();
+              if (col < q.n) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const int64_t row = m0 + j * 16 + i;
+                  if (row < q.m) {
+                    store_scalar<T>(q.c, row * q.scm + col * q.scn,
+                                    silu_mul(__uint_as_float(g[i]), __uint_as_float(u[i])));
+                  }
+                }
+              }
+            }
+            tc_fence_before();
+            mbar_arrive(&acc_empty[buf]);
+            ++acc_it;
+            continue;
+          }
+        }
 #pragma unroll 1
         for (int c = 0; c < TN / 128; ++c) {
           const int64_t col = n0 + c * 128 + quarter * 32 + lane;
@@ -640,11 +773,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       } else {
-        if (cmap != nullptr) {
-          store_rows_tma<T, TN>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32), static_cast<int32_t>(n0),
-                                my_blocks, lane, chunk_seq, pol_out, p.error_word);
-        } else {
-          store_rows_staged<T, TN>(q, taddr, m0 + quarter * 32, n0, my_blocks, lane);
+        bool done = false;
+        if constexpr (TN >= 128) {
+          if (p.swiglu) {
+            if (cmap != nullptr) {
+              store_rows_tma_swiglu<T, TN / 2>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
+                                               static_cast<int32_t>(n0), my_blocks, lane, chunk_seq, pol_out,
+                                               p.error_word);
+            } else {
+              store_rows_scalar_swiglu<T, TN / 2>(q, taddr, m0 + quarter * 32, n0, lane);
+            }
+            done = true;
+          }
+        }
+        if (!done) {
+          if (cmap != nullptr) {
+            store_rows_tma<T, TN>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32), static_cast<int32_t>(n0),
+                                  my_blocks, lane, chunk_seq, pol_out, p.error_word);
+          } else {
+            store_rows_staged<T, TN>(q, taddr, m0 + quarter * 32, n0, my_blocks, lane);
+          }
         }
       }
       tc_fence_before();

@@ -8,6 +8,7 @@ comparison provider of the reference is not part of this package.
 from .grouped_gemm import (
     GroupedWorkspace,
     build_fused_gate_up_workspace,
+    build_fused_swiglu_workspace,
     build_grouped_workspace,
     check_device_errors,
     grouped_candidate_configs,
@@ -27,6 +28,7 @@ __all__ = [
     "GroupedWorkspace",
     "KernelConfig",
     "build_fused_gate_up_workspace",
+    "build_fused_swiglu_workspace",
     "build_grouped_workspace",
     "check_device_errors",
     "grouped_candidate_configs",

@@ -29,6 +29,7 @@ STATUS_SCRATCH = 4
 EXPORTED_SYMBOLS = (
     "grouped_gemm_scratch_bytes",
     "grouped_gemm_launch",
+    "grouped_gemm_swiglu_launch",
     "grouped_gemm_launch_noalloc",
     "matmul_launch",
     "matrix_repack",
@@ -106,6 +107,12 @@ def _declare(lib) -> None:
         ctypes.POINTER(TileConfig), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
     ]
     lib.grouped_gemm_launch.restype = ctypes.c_int
+    lib.grouped_gemm_swiglu_launch.argtypes = [
+        c_i64p, c_i64p, c_i64p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
+        ctypes.POINTER(TileConfig), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
+    ]
+    lib.grouped_gemm_swiglu_launch.restype = ctypes.c_int
     lib.grouped_gemm_launch_noalloc.argtypes = [
         c_i64p, c_i64p, c_i64p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32,
@@ -187,16 +194,19 @@ def scratch_bytes(problem_count: int, sm_count: int) -> int:
 def grouped_launch(
     a_ptrs: int, b_ptrs: int, c_ptrs: int, dims: int, strides: int, problem_count: int, homogeneous: bool,
     m: int, n: int, k: int, dtype: str, precision: str, tma_aligned: bool, config, scratch: int,
-    scratch_nbytes: int, stream: int,
+    scratch_nbytes: int, stream: int, swiglu: bool = False,
 ) -> LaunchInfo:
+    """grouped_gemm_launch, or grouped_gemm_swiglu_launch with `swiglu`."""
     info = LaunchInfo()
     cfg = tile_config(config)
-    status = load().grouped_gemm_launch(
+    lib = load()
+    entry = lib.grouped_gemm_swiglu_launch if swiglu else lib.grouped_gemm_launch
+    status = entry(
         a_ptrs, b_ptrs, c_ptrs, dims, strides, int(problem_count), int(bool(homogeneous)), int(m), int(n), int(k),
         DTYPE_CODES[dtype], PRECISION_CODES[precision], int(bool(tma_aligned)), ctypes.byref(cfg), scratch,
         int(scratch_nbytes), stream, ctypes.byref(info),
     )
-    _check(status, "grouped_gemm_launch")
+    _check(status, "grouped_gemm_swiglu_launch" if swiglu else "grouped_gemm_launch")
     return info
 
 

@@ -65,9 +65,10 @@ class GroupedWorkspace:
 
     Fields a_ptrs / b_ptrs / c_ptrs (int64 [E]), dims (int32 [E, 3], M N K
     order), strides (int64 [E, 6]: am ak bk bn cm cn) are the reference's
-    (kernels/grouped_gemm.py:67-111).  ``scratch`` holds the per-CTA
-    tensor-map slots of the TMA path; ``launch_info`` records the native
-    kernel of the most recent launch.
+    (kernels/grouped_gemm.py:67-111).  ``scratch`` holds the per-problem
+    tensor maps of the TMA path; ``launch_info`` records the native kernel of
+    the most recent launch.  ``operation == "swiglu"`` marks a workspace whose
+    C_e is [M_e, N/2] and whose launches apply the fused SwiGLU epilogue.
     """
 
     a: list
@@ -214,19 +215,25 @@ def _normalize(shapes: Sequence[tuple[int, int, int]], what: str) -> tuple[tuple
     return normalized
 
 
-def workspace_from_tensors(a_list, b_list, c_list, config: KernelConfig | None = None) -> GroupedWorkspace:
+def workspace_from_tensors(a_list, b_list, c_list, config: KernelConfig | None = None, *,
+                           swiglu: bool = False) -> GroupedWorkspace:
     """Builds the device tables for caller-owned per-expert tensors.
 
     The reference builds its tables inside build_grouped_workspace
     (kernels/grouped_gemm.py:528-572); this is the same step for tensors the
-    caller already holds (the bench, the multi-rank shards).
+    caller already holds (the bench, the multi-rank shards).  With ``swiglu``
+    each B_e is a packed [gate | up] weight [K, N] and C_e is [M, N/2]; the
+    workspace's operation is "swiglu".
     """
     if not a_list or not (len(a_list) == len(b_list) == len(c_list)):
         raise ValueError("grouped GEMM requires equally many A, B and C matrices (at least one)")
     shapes = []
     for a, b, c in zip(a_list, b_list, c_list):
-        if a.ndim != 2 or b.ndim != 2 or c.ndim != 2 or a.shape[1] != b.shape[0] or c.shape != (a.shape[0], b.shape[1]):
+        out_n = b.shape[1] // 2 if swiglu else b.shape[1]
+        if a.ndim != 2 or b.ndim != 2 or c.ndim != 2 or a.shape[1] != b.shape[0] or c.shape != (a.shape[0], out_n):
             raise ValueError(f"shape mismatch: A={tuple(a.shape)}, B={tuple(b.shape)}, C={tuple(c.shape)}")
+        if swiglu and b.shape[1] % 2:
+            raise ValueError("SwiGLU requires an even packed [gate | up] width")
         if a.dtype != b.dtype or a.dtype != c.dtype or a.dtype != a_list[0].dtype:
             raise ValueError("A, B, and C must share one dtype")
         if not (a.is_cuda and b.is_cuda and c.is_cuda) or len({a.device, b.device, c.device, a_list[0].device}) != 1:
@@ -256,10 +263,13 @@ def workspace_from_tensors(a_list, b_list, c_list, config: KernelConfig | None =
     homogeneous = all(shape == normalized[0] for shape in normalized) and all(
         x.is_contiguous() for x in [*a_list, *b_list, *c_list]
     )
-    return GroupedWorkspace(
+    workspace = GroupedWorkspace(
         list(a_list), list(b_list), list(c_list), a_ptrs, b_ptrs, c_ptrs, dims, strides, normalized, config,
         _shape_signature(normalized), device_signature, sm_count, storage_bytes, homogeneous,
     )
+    if swiglu:
+        workspace.operation = "swiglu"
+    return workspace
 
 
 def build_grouped_workspace(
@@ -301,6 +311,34 @@ def build_fused_gate_up_workspace(
     return workspace
 
 
+def build_fused_swiglu_workspace(
+    shapes: Sequence[tuple[int, int, int]],
+    dtype,
+    seed: int = 0,
+    config: KernelConfig | None = None,
+) -> GroupedWorkspace:
+    """Packed W13 problems with the SwiGLU epilogue fused: (M, K, N) with
+    N = 2 * local_ffn, B_e = [gate | up] drawn exactly as
+    build_fused_gate_up_workspace draws it, C_e = silu(A B_gate) * (A B_up)
+    of shape [M, N/2].  The reference computes SiLU(gate) * up outside its
+    timed GEMM (README.md:55-60); here one launch writes the activation."""
+    if torch is None or not torch.cuda.is_available():
+        raise RuntimeError("CUDA PyTorch is required")
+    normalized = tuple(tuple(int(value) for value in shape) for shape in shapes)
+    if not normalized:
+        raise ValueError("grouped GEMM requires at least one problem")
+    if any(len(shape) != 3 or shape[2] % 2 for shape in normalized):
+        raise ValueError("fused SwiGLU shapes require an even packed output dimension")
+    normalized = _normalize(normalized, "grouped")
+    generator = torch.Generator(device="cuda").manual_seed(seed)
+    a_list, b_list, c_list = [], [], []
+    for m, k, n in normalized:
+        a_list.append(torch.empty((m, k), device="cuda", dtype=dtype).normal_(generator=generator).mul_(0.1))
+        b_list.append(torch.empty((k, n), device="cuda", dtype=dtype).normal_(generator=generator).mul_(0.1))
+        c_list.append(torch.empty((m, n // 2), device="cuda", dtype=dtype))
+    return workspace_from_tensors(a_list, b_list, c_list, config, swiglu=True)
+
+
 def _grid_size(workspace: GroupedWorkspace, config: KernelConfig) -> int:
     """Persistent grid of the reference's kernels (kernels/grouped_gemm.py:597-599).
 
@@ -332,6 +370,7 @@ def _ensure_scratch(workspace: GroupedWorkspace):
 
 
 def _launch_native(workspace: GroupedWorkspace, config: KernelConfig, precision: str, aligned: bool) -> dict:
+    swiglu = workspace.operation == "swiglu"
     scratch = _ensure_scratch(workspace)
     device = workspace.a[0].device
     if workspace.homogeneous:
@@ -343,7 +382,7 @@ def _launch_native(workspace: GroupedWorkspace, config: KernelConfig, precision:
             workspace.a_ptrs.data_ptr(), workspace.b_ptrs.data_ptr(), workspace.c_ptrs.data_ptr(),
             workspace.dims.data_ptr(), workspace.strides.data_ptr(), workspace.problem_count,
             workspace.homogeneous, m, n, k, dtype_name(workspace.a[0].dtype), precision, aligned, config,
-            scratch.data_ptr(), scratch.numel(), torch.cuda.current_stream(device).cuda_stream,
+            scratch.data_ptr(), scratch.numel(), torch.cuda.current_stream(device).cuda_stream, swiglu=swiglu,
         )
     workspace.launch_info = info.as_dict()
     return workspace.launch_info
@@ -374,7 +413,7 @@ def launch_grouped(
     if input_precision not in _native.PRECISION_CODES:
         raise ValueError(f"input_precision must be 'ieee' or 'tf32', got {input_precision!r}")
     cfg = config or workspace.config
-    if workspace.problem_count == 1:
+    if workspace.problem_count == 1 and workspace.operation != "swiglu":
         launch_matmul(workspace.a[0], workspace.b[0], workspace.c[0], cfg, input_precision, autotune=autotune)
         from .matmul import last_launch_info
 

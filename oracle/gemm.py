@@ -73,6 +73,22 @@ def gate_up(a: np.ndarray, packed_b: np.ndarray, dtype: str) -> np.ndarray:
     return np.concatenate((matmul(a, packed_b[:, :half], dtype), matmul(a, packed_b[:, half:], dtype)), axis=1)
 
 
+def swiglu(a: np.ndarray, packed_b: np.ndarray, dtype: str) -> np.ndarray:
+    """SiLU(A @ gate) * (A @ up) from the packed W13 weight, float64 throughout and
+    one rounding to `dtype`.  The reference applies this activation after its
+    packed Gate+Up GEMM, outside the timed region (README.md:55-57,
+    kernels/grouped_gemm.py:585); the fused epilogue computes it in fp32 from the
+    fp32 accumulators."""
+    if packed_b.shape[1] % 2:
+        raise ValueError("packed gate+up weight needs an even output dimension")
+    a64 = np.asarray(a, dtype=np.float64)
+    b64 = np.asarray(packed_b, dtype=np.float64)
+    half = b64.shape[1] // 2
+    gate = a64 @ b64[:, :half]
+    up = a64 @ b64[:, half:]
+    return round_to_dtype(gate / (1.0 + np.exp(-gate)) * up, dtype)
+
+
 def exact_integer_outputs(shape: tuple[int, int, int], problems: int) -> list[np.ndarray]:
     """Known answer of tests/test_gpu.py:127-154: A = 1, B_e = e + 1 gives C_e = K * (e + 1)."""
     m, k, n = shape

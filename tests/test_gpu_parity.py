@@ -367,6 +367,108 @@ def test_fused_gate_up_packed_output_in_one_grouped_launch():
             _oracle_check(packed_output, a, packed_weight, dtype_name, gate_up=True)
 
 
+def _swiglu_check(ws, dtype_name, rows=None, precision="ieee"):
+    from oracle import gemm as oracle
+
+    for a, b, c in ws.problem_tensors():
+        if rows is not None:
+            idx = rows(a.shape[0])
+            a, c = a.index_select(0, idx), c.index_select(0, idx)
+        expected = oracle.swiglu(_host(a), _host(b), dtype_name)
+        got = _host(c)
+        assert np.isfinite(got).all(), "output has non-finite values (unwritten or overflow)"
+        key = "tf32" if (dtype_name == "fp32" and precision == "tf32") else dtype_name
+        err = oracle.relative_frobenius(got, expected)
+        assert err <= REL_FRO[key], f"relative Frobenius error {err:.3e} > {REL_FRO[key]:.1e}"
+        tol = ASSERT_CLOSE[dtype_name] if key != "tf32" else 5e-3
+        np.testing.assert_allclose(got, expected, rtol=tol, atol=tol)
+
+
+def _swiglu_workspace(shapes, dtype_name, seed, b_scale=None):
+    """Per-expert A, packed [gate | up] B and [M, N/2] C for the fused epilogue."""
+    torch = _torch()
+    from kernels import workspace_from_tensors
+
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    dtype = _dtype(dtype_name)
+    a_list, b_list, c_list = [], [], []
+    for m, k, n in shapes:
+        scale_a, scale_b = (0.1, 0.1) if b_scale is None else (1.0, b_scale)
+        a_list.append(_randn((m, k), dtype, gen, scale_a))
+        b_list.append(_randn((k, n), dtype, gen, scale_b))
+        c_list.append(torch.full((m, n // 2), float("nan"), device="cuda", dtype=dtype))
+    return workspace_from_tensors(a_list, b_list, c_list, swiglu=True)
+
+
+@pytest.mark.parametrize("dtype_name", ["fp16", "bf16"])
+def test_fused_swiglu_every_tile_family(dtype_name):
+    """silu(A B_gate) * (A B_up) written as [M, F] in one launch: every native
+    tile family (swap-AB, 128-row, CTA-pair 256 x 256 and 256 x 512) on a
+    heterogeneous group with ragged M and F, against the float64 oracle."""
+    torch = _torch()
+    from kernels import KernelConfig, launch_grouped
+
+    shapes = [(16, 256, 2 * 256), (40, 192, 2 * 136), (130, 320, 2 * 512), (1, 64, 2 * 64), (300, 128, 2 * 520)]
+    ws = _swiglu_workspace(shapes, dtype_name, seed=21)
+    assert ws.operation == "swiglu" and not ws.homogeneous
+    for cfg in (KernelConfig(16, 256, 64, 4, 8, 4), KernelConfig(32, 128, 64, 4, 4, 4),
+                KernelConfig(64, 256, 64, 8, 8, 4), KernelConfig(128, 64, 64, 8, 4, 3),
+                KernelConfig(128, 256, 64, 8, 8, 4), KernelConfig(256, 128, 64, 8, 8, 4),
+                KernelConfig(256, 256, 64, 8, 8, 4)):
+        _poison(ws)
+        launch_grouped(ws, config=cfg, autotune=False)
+        torch.cuda.synchronize()
+        assert ws.launch_info["path"].startswith("tcgen05_tma"), ws.launch_info
+        _swiglu_check(ws, dtype_name)
+
+
+@pytest.mark.parametrize("m_e", [16, 128, 1024])
+def test_fused_swiglu_deepseek_tp_rank(m_e):
+    """DeepSeek-V3 W13 TP rank miniature (4 experts of [M_e, 7168] @ [7168, 512]),
+    autotuned launch, A ~ N(0,1), B ~ N(0, 1/sqrt(K)); sampled rows."""
+    torch = _torch()
+    from kernels import check_device_errors, launch_grouped
+
+    ws = _swiglu_workspace([(m_e, 7168, 512)] * 4, "bf16", seed=m_e, b_scale=1.0 / math.sqrt(7168))
+    assert ws.homogeneous
+    launch_grouped(ws)
+    torch.cuda.synchronize()
+    check_device_errors()
+    rng = np.random.default_rng(m_e)
+    rows = lambda m: torch.as_tensor(np.unique(np.concatenate([[0, m - 1], rng.integers(0, m, 16)])), device="cuda")
+    _swiglu_check(ws, "bf16", rows=rows)
+
+
+def test_fused_swiglu_tf32_and_builder():
+    """fp32 operands on the TF32 tensor-core path, and the seeded builder."""
+    torch = _torch()
+    from kernels import build_fused_swiglu_workspace, launch_grouped
+
+    ws = build_fused_swiglu_workspace([(96, 128, 2 * 192)] * 3, torch.float32, seed=4)
+    launch_grouped(ws, input_precision="tf32")
+    torch.cuda.synchronize()
+    assert ws.launch_info["path"].startswith("tcgen05_tma")
+    _swiglu_check(ws, "fp32", precision="tf32")
+    ws16 = build_fused_swiglu_workspace([(64, 256, 2 * 128)], torch.bfloat16, seed=5)
+    launch_grouped(ws16)  # one problem still takes the fused grouped path
+    torch.cuda.synchronize()
+    assert ws16.scheduler == "homogeneous_persistent"
+    _swiglu_check(ws16, "bf16")
+
+
+def test_fused_swiglu_refuses_the_generic_path():
+    torch = _torch()
+    from kernels import launch_grouped
+    from kernels._native import NativeLaunchError
+
+    ws = _swiglu_workspace([(8, 13, 2 * 16)] * 2, "bf16", seed=1)  # 26-byte A rows: not TMA-addressable
+    with pytest.raises(NativeLaunchError, match="unsupported"):
+        launch_grouped(ws)
+    ws32 = _swiglu_workspace([(8, 64, 2 * 64)] * 2, "fp32", seed=1)  # fp32 "ieee" runs on the SIMT kernel
+    with pytest.raises(NativeLaunchError, match="unsupported"):
+        launch_grouped(ws32)
+
+
 def test_one_problem_group_dispatches_standard_matmul():
     """tests/test_gpu.py:190-195."""
     torch = _torch()

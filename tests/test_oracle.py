@@ -110,3 +110,27 @@ def test_relative_frobenius():
     assert oracle.relative_frobenius(a, a) == 0.0
     assert oracle.relative_frobenius(np.zeros((1, 2)), a) == pytest.approx(1.0)
     assert oracle.relative_frobenius(np.ones((2, 2)), np.zeros((2, 2))) == pytest.approx(2.0)
+
+
+def test_swiglu_is_silu_of_gate_times_up():
+    rng = np.random.default_rng(3)
+    a = rng.standard_normal((5, 7))
+    b = rng.standard_normal((7, 12))
+    got = oracle.swiglu(a, b, "fp32")
+    gate, up = a @ b[:, :6], a @ b[:, 6:]
+    expected = gate / (1.0 + np.exp(-gate)) * up
+    assert oracle.relative_frobenius(got, expected) < 1e-6
+    with pytest.raises(ValueError):
+        oracle.swiglu(a, b[:, :11], "fp32")
+
+
+def test_swiglu_known_answer():
+    # A = 1, gate = 1, up = 2: every output is silu(K) * 2K.
+    k = 4
+    a = np.ones((3, k))
+    b = np.concatenate((np.ones((k, 5)), 2 * np.ones((k, 5))), axis=1)
+    expected = k / (1.0 + np.exp(-k)) * 2 * k
+    np.testing.assert_allclose(oracle.swiglu(a, b, "fp32"), np.full((3, 5), expected), rtol=1e-6)
+    # silu(0) = 0 whatever up is; large negative gates vanish
+    assert np.all(oracle.swiglu(np.zeros((2, 3)), np.ones((3, 4)), "bf16") == 0)
+    assert abs(oracle.swiglu(np.full((1, 1), -50.0), np.ones((1, 2)), "fp32")[0, 0]) < 1e-15
