@@ -67,6 +67,8 @@ def parse_args(argv=None):
     p.add_argument("--m-values", type=str, default=",".join(map(str, M_VALUES)))
     p.add_argument("--projection", choices=("W1", "W2"), default="W1",
                    help="W1: packed W13 gate+up (the benchmark line); W2: down projection (BASELINE configs[2])")
+    p.add_argument("--fused-swiglu", action="store_true",
+                   help="W1 only: launch with the fused SwiGLU epilogue (C = silu(gate) * up, [M_e, F_local])")
     p.add_argument("--cache-mode", choices=("hot", "cold"), default="hot",
                    help="cold: two resident workspace sets, alternated step by step (rotating-cold)")
     # Profiling / diagnosis knobs (defaults give the benchmark workload).
@@ -116,11 +118,14 @@ def step_shapes(m_values, projection: str = "W1") -> list[tuple[str, int, tuple[
     return out
 
 
-def roofline_ms(m: int, k: int, n: int, count: int, peaks: dict, sustained: bool = True) -> tuple[float, str]:
+def roofline_ms(m: int, k: int, n: int, count: int, peaks: dict, sustained: bool = True,
+                out_cols: int | None = None) -> tuple[float, str]:
+    """Roofline time of one launch; `out_cols` is C's width when it is not N
+    (the fused SwiGLU epilogue writes N/2 columns)."""
     from moe_parallel import gemm_flops, ideal_bytes
 
     flops = gemm_flops(m, k, n) * count
-    nbytes = ideal_bytes(m, k, n, 2) * count
+    nbytes = ideal_bytes(m, k, n, 2) * count if out_cols is None else 2 * (m * k + k * n + m * out_cols) * count
     tc = flops / ((peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]) * 1e12) * 1e3
     hbm = nbytes / (peaks["hbm_gbs"] * 1e9) * 1e3
     return (tc, "tensor") if tc >= hbm else (hbm, "hbm")
@@ -195,8 +200,9 @@ def expert_weight(expert: int, device):
     return w.mul_(1.0 / math.sqrt(HIDDEN)).to(torch.bfloat16)
 
 
-def build_rank(rank: int, m_values, device, parallel=("EP", "TP"), expert_limit=None):
-    """Per-rank tensors and the grouped workspaces of one step (14 by default)."""
+def build_rank(rank: int, m_values, device, parallel=("EP", "TP"), expert_limit=None, swiglu: bool = False):
+    """Per-rank tensors and the grouped workspaces of one step (14 by default).
+    With `swiglu` the outputs are the fused SwiGLU activations [M_e, F_local]."""
     import torch
 
     from kernels import workspace_from_tensors
@@ -221,16 +227,17 @@ def build_rank(rank: int, m_values, device, parallel=("EP", "TP"), expert_limit=
         gen = torch.Generator(device=device).manual_seed(7919 * m)
         a_all = torch.randn((EXPERTS, m, HIDDEN), device=device, generator=gen).to(torch.bfloat16)
         activations[m] = a_all
-        c_ep = torch.empty((len(ep_experts), m, 2 * FFN), device=device, dtype=torch.bfloat16)
-        c_tp = torch.empty((len(tp_experts), m, tp.local_ffn * 2), device=device, dtype=torch.bfloat16)
+        width = 1 if swiglu else 2
+        c_ep = torch.empty((len(ep_experts), m, width * FFN), device=device, dtype=torch.bfloat16)
+        c_tp = torch.empty((len(tp_experts), m, tp.local_ffn * width), device=device, dtype=torch.bfloat16)
         outputs[m] = (c_ep, c_tp)
         if "EP" in parallel:
-            ws_ep = workspace_from_tensors([a_all[e] for e in ep_experts], ep_w, list(c_ep))
-            ws_ep.operation = "gate_up"
+            ws_ep = workspace_from_tensors([a_all[e] for e in ep_experts], ep_w, list(c_ep), swiglu=swiglu)
+            ws_ep.operation = "swiglu" if swiglu else "gate_up"
             workspaces.append(("EP", m, ws_ep))
         if "TP" in parallel:
-            ws_tp = workspace_from_tensors([a_all[e] for e in tp_experts], tp_w, list(c_tp))
-            ws_tp.operation = "gate_up"
+            ws_tp = workspace_from_tensors([a_all[e] for e in tp_experts], tp_w, list(c_tp), swiglu=swiglu)
+            ws_tp.operation = "swiglu" if swiglu else "gate_up"
             workspaces.append(("TP", m, ws_tp))
     return ep, tp, activations, outputs, workspaces
 
@@ -382,10 +389,12 @@ def graph_of_steps(workspaces, steps: int, stream, rings=None):
     return graph, events
 
 
-def verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_values) -> dict:
+def verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_values, swiglu: bool = False) -> dict:
     """After timing: NCCL all_gather of sampled output rows from every rank;
     rank 0 checks EP expert rows and TP [gate_r | up_r] slices against the
-    float64 product of the global weights (regenerated for sampled experts)."""
+    float64 product of the global weights (regenerated for sampled experts).
+    With `swiglu` the outputs are silu(gate) * up: EP rows against the full
+    activation, TP rank r against its F/P column slice of it."""
     import torch
     import torch.distributed as dist
 
@@ -395,7 +404,8 @@ def verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_val
     sampled_experts = sorted({0, per - 1} | {r * per + (r % per) for r in range(world)})
     rows_idx = {m: sorted({0, m - 1, m // 2}) for m in m_values}
     checks = [m_values[0], m_values[-1]]
-    width = 2 * FFN + 2 * tp.local_ffn
+    ep_w, tp_w = (FFN, tp.local_ffn) if swiglu else (2 * FFN, 2 * tp.local_ffn)
+    width = ep_w + tp_w
     worst = 0.0
     for m in checks:
         rows = torch.tensor(rows_idx[m], device=device)
@@ -403,8 +413,8 @@ def verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_val
         payload = torch.zeros((len(sampled_experts), len(rows), width), device=device, dtype=torch.float32)
         for i, e in enumerate(sampled_experts):
             if ep_owner(e, PARALLEL, EXPERTS) == rank:
-                payload[i, :, : 2 * FFN] = c_ep[ep.experts.index(e)].index_select(0, rows).float()
-            payload[i, :, 2 * FFN:] = c_tp[e].index_select(0, rows).float()
+                payload[i, :, :ep_w] = c_ep[ep.experts.index(e)].index_select(0, rows).float()
+            payload[i, :, ep_w:] = c_tp[e].index_select(0, rows).float()
         gathered = [torch.empty_like(payload) for _ in range(world)] if world > 1 else [payload]
         if world > 1:
             dist.all_gather(gathered, payload)
@@ -413,13 +423,19 @@ def verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_val
         local = tp.local_ffn
         for i, e in enumerate(sampled_experts):
             ref = activations[m][e].index_select(0, rows).double() @ expert_weight(e, device).double()
+            if swiglu:
+                gate, up = ref[:, :FFN], ref[:, FFN:]
+                ref = gate / (1.0 + torch.exp(-gate)) * up
             owner = ep_owner(e, PARALLEL, EXPERTS)
             if owner < world:
-                got = gathered[owner][i, :, : 2 * FFN].double()
+                got = gathered[owner][i, :, :ep_w].double()
                 worst = max(worst, float((got - ref).norm() / ref.norm()))
             for r in range(world):
-                sl = torch.cat((ref[:, r * local:(r + 1) * local], ref[:, FFN + r * local:FFN + (r + 1) * local]), 1)
-                got = gathered[r][i, :, 2 * FFN:].double()
+                if swiglu:
+                    sl = ref[:, r * local:(r + 1) * local]
+                else:
+                    sl = torch.cat((ref[:, r * local:(r + 1) * local], ref[:, FFN + r * local:FFN + (r + 1) * local]), 1)
+                got = gathered[r][i, :, ep_w:].double()
                 worst = max(worst, float((got - sl).norm() / sl.norm()))
     return {"checked_experts": sampled_experts, "checked_m": checks, "max_rel_frobenius": worst,
             "passed": worst <= 1e-2}
@@ -618,14 +634,19 @@ def main(argv=None) -> int:
             CLASS_CONFIGS[int(m_text)] = KernelConfig(bm, bn, 64, 8, 4, 4)
     parallel = tuple(p for p in ("EP", "TP") if p in args.parallel.split(","))
     progress("building rank tensors")
-    builder = build_rank if args.projection == "W1" else build_rank_w2
-    ep, tp, activations, outputs, workspaces = builder(rank, m_values, device, parallel, args.expert_limit)
+    if args.fused_swiglu and args.projection != "W1":
+        raise SystemExit("--fused-swiglu applies to the W1 (packed gate+up) projection")
+    if args.projection == "W1":
+        ep, tp, activations, outputs, workspaces = build_rank(rank, m_values, device, parallel, args.expert_limit,
+                                                              swiglu=args.fused_swiglu)
+    else:
+        ep, tp, activations, outputs, workspaces = build_rank_w2(rank, m_values, device, parallel, args.expert_limit)
     rings = None
     if args.cache_mode == "cold":
         if args.steps % 2:
             raise SystemExit("--cache-mode cold alternates two workspace sets: --steps must be even")
         if args.projection == "W1":
-            second = build_rank(rank, m_values, device, parallel, args.expert_limit)[4]
+            second = build_rank(rank, m_values, device, parallel, args.expert_limit, swiglu=args.fused_swiglu)[4]
         else:
             second = build_rank_w2(rank, m_values, device, parallel, args.expert_limit, seed=1)[4]
         rings = [workspaces, second]
@@ -689,7 +710,7 @@ def main(argv=None) -> int:
     for (par, m), times in per_launch.items():
         (mm, k, n), count = shapes[(par, m)]
         ms = statistics.median(times)
-        roof, bound = roofline_ms(mm, k, n, count, peaks)
+        roof, bound = roofline_ms(mm, k, n, count, peaks, out_cols=n // 2 if args.fused_swiglu else None)
         per_shape.append({"parallel": par, "M_e": m, "experts": count, "ms": round(ms, 4),
                           "tflops": round(gemm_flops(mm, k, n) * count / ms / 1e9, 1),
                           "roofline_frac": round(roof / ms, 3), "bound": bound})
@@ -697,7 +718,7 @@ def main(argv=None) -> int:
     dominant = max(per_shape, key=lambda r: r["ms"])
     (dm, dk, dn), dcount = shapes[(dominant["parallel"], dominant["M_e"])]
     d_flops = gemm_flops(dm, dk, dn) * dcount
-    d_bytes = 2 * (dm * dk + dk * dn + dm * dn) * dcount
+    d_bytes = 2 * (dm * dk + dk * dn + dm * (dn // 2 if args.fused_swiglu else dn)) * dcount
     if dominant["bound"] == "tensor":
         achieved = d_flops / (dominant["ms"] * 1e-3) / 1e12
         roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops_sustained"],
@@ -708,8 +729,9 @@ def main(argv=None) -> int:
                     "frac": round(achieved / peaks["hbm_gbs"], 3)}
     roofline.update({"kernel": f"{'W13' if args.projection == 'W1' else 'W2'} {dominant['parallel']} M_e={dominant['M_e']}",
                      "time_share": round(dominant["ms"] / total_ms, 3), "peak_source": peak_source,
-                     "traffic": traffic_from_profiles(dominant, args.projection)})
-    step_roof_ms = sum(roofline_ms(*shapes[key][0], shapes[key][1], peaks)[0] for key in shapes)
+                     "traffic": None if args.fused_swiglu else traffic_from_profiles(dominant, args.projection)})
+    step_roof_ms = sum(roofline_ms(*shapes[key][0], shapes[key][1], peaks,
+                                   out_cols=shapes[key][0][2] // 2 if args.fused_swiglu else None)[0] for key in shapes)
 
     # End to end through the public API with host buffers: per step, the
     # step's activations go host -> device from pinned memory, every launch
@@ -752,7 +774,8 @@ def main(argv=None) -> int:
     if parallel == ("EP", "TP") and not args.expert_limit and args.projection == "W2":
         verification = verify_w2_outputs(rank, world, ep, tp, outputs, device, m_values)
     elif parallel == ("EP", "TP") and not args.expert_limit:
-        verification = verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_values)
+        verification = verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_values,
+                                           swiglu=args.fused_swiglu)
     else:
         verification = {"skipped": "partial workload (--parallel / --expert-limit)"}
     # A tensor-core grouped launch is two kernels (tensor-map builder + GEMM);
@@ -774,7 +797,8 @@ def main(argv=None) -> int:
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD if args.projection == "W1" else WORKLOAD_W2,
+            "config": {"workload": (WORKLOAD if args.projection == "W1" else WORKLOAD_W2)
+                       + ("; fused SwiGLU epilogue: C = silu(gate) * up, [M_e, F_local]" if args.fused_swiglu else ""),
                        "parallelism": f"GPU r runs rank r of P=8 (EP and TP), {world} rank(s)",
                        "cache": ("hot; inputs larger than L2 (0.94-1.88 GB of weights per projection), no flush"
                                  if args.cache_mode == "hot" else
