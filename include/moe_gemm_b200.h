@@ -109,6 +109,28 @@ int grouped_gemm_swiglu_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, con
                                int32_t precision, int32_t operands_tma_aligned, const mgb_tile_config* config,
                                void* scratch, size_t scratch_bytes, void* stream, mgb_launch_info* info);
 
+/* Grouped GEMM over the expert-sorted aggregate layout: for e in [0, problem_count)
+ *   C[r0:r1, :] = A[r0:r1, :] @ B[e]      with r0 = offs[e-1] (0 for e = 0), r1 = offs[e]
+ * A is one [total_rows, k] matrix of tokens sorted by expert, B one [E, k, n]
+ * tensor, C one [total_rows, n] matrix (n / 2 columns with swiglu = 1, which
+ * applies the fused SwiGLU epilogue to a packed [gate | up] B).  Row strides
+ * are in elements; columns are contiguous; stride_be is the element distance
+ * between consecutive experts' B.  `offs` is int32 [problem_count] of
+ * cumulative row ends, read on the device (no host synchronisation; empty
+ * experts are fine), the format of torch.nn.functional.grouped_mm that the
+ * reference's torch provider builds (kernels/torch_grouped_gemm.py:142-158).
+ * No counterpart in the reference's own kernels, which take per-expert
+ * pointer tables; this removes the tables for callers whose tokens are
+ * already permuted by expert.  Tensor-core path when A / B are 16-byte
+ * aligned with 16-byte multiple row strides (fp16 / bf16, or fp32 with
+ * MGB_TF32); the generic kernel otherwise (swiglu requires the former).
+ * Scratch: grouped_gemm_scratch_bytes(problem_count, *). */
+int grouped_gemm_offsets_launch(const void* a, const void* b, void* c, const int32_t* offs, int32_t problem_count,
+                                int64_t total_rows, int64_t n, int64_t k, int64_t stride_am, int64_t stride_be,
+                                int64_t stride_bk, int64_t stride_cm, int32_t dtype, int32_t precision,
+                                int32_t swiglu, const mgb_tile_config* config, void* scratch, size_t scratch_bytes,
+                                void* stream, mgb_launch_info* info);
+
 /* Masked single GEMM C[m, n] = A[m, k] @ B[k, n] with arbitrary element strides.
  * Replaces the Triton launch of launch_matmul (kernels/matmul.py:332-392,
  * kernel _matmul_kernel_impl :223-273).  Operands that satisfy the TMA rules

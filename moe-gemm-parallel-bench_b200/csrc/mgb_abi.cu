@@ -255,39 +255,32 @@ size_t grouped_gemm_scratch_bytes(int32_t problem_count, int32_t sm_count) {
 
 namespace {
 
-// Both grouped entry points: swiglu = 1 selects the fused SwiGLU epilogue.
-int grouped_launch_impl(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs, const int32_t* dims,
-                        const int64_t* strides, int32_t problem_count, int32_t homogeneous, int64_t m, int64_t n,
-                        int64_t k, int32_t dtype, int32_t precision, int32_t operands_tma_aligned,
-                        const mgb_tile_config* config, void* scratch, size_t scratch_bytes, void* stream,
-                        mgb_launch_info* info, int swiglu) {
-  if (!valid_dtype(dtype, precision) || problem_count <= 0 || a_ptrs == nullptr || b_ptrs == nullptr ||
-      c_ptrs == nullptr || m < 0 || n < 0 || k < 0) {
-    return MGB_ERR_INVALID;
+// Upper bound on the tiles of a grouped launch for a tm x tn tile:
+// (problems * ceil(rows / tm) + extra_row_blocks) * ceil(n / tn).  Tables give
+// problems x the largest problem; the aggregate layout gives the total rows plus
+// one partial row block per expert.
+struct TileBound {
+  int64_t problems;
+  int64_t rows;
+  int64_t extra_row_blocks;
+  int64_t tiles(int tm, int tn, int64_t n) const {
+    return (problems * cdiv(std::max<int64_t>(rows, 1), tm) + extra_row_blocks) * cdiv(std::max<int64_t>(n, 1), tn);
   }
-  if (swiglu && n % 2 != 0) return MGB_ERR_INVALID;
-  if (!homogeneous && (dims == nullptr || strides == nullptr)) return MGB_ERR_INVALID;
-  DeviceState ds;
-  if (int st = device_state(&ds)) return st;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+};
 
-  GroupedParams p;
-  std::memset(&p, 0, sizeof(p));
-  p.a_ptrs = a_ptrs;
-  p.b_ptrs = b_ptrs;
-  p.c_ptrs = c_ptrs;
-  p.dims = dims;
-  p.strides = strides;
-  p.problem_count = problem_count;
-  p.homogeneous = homogeneous ? 1 : 0;
-  p.m = m;
-  p.n = n;
-  p.k = k;
-  p.wait_budget = g_wait_budget;
-  p.test_flags = g_test_flags;
-  p.error_word = ds.error_word;
-  p.swiglu = swiglu ? 1 : 0;
+int grid_from(const TileBound& b, int tm, int tn, int64_t n, int64_t cap) {
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(b.tiles(tm, tn, n), cap)));
+}
 
+// The launch of a filled GroupedParams (tables or aggregate layout): the
+// tensor-core path (map builder + GEMM kernel) when the operands are
+// TMA-addressable and the precision allows it, else the generic kernel.
+// (m, n, k) size the templates; p.swiglu selects the fused epilogue.
+int launch_grouped_params(GroupedParams& p, const DeviceState& ds, const TileBound& bound, int64_t m, int64_t n,
+                          int64_t k, int32_t dtype, int32_t precision, bool operands_tma_aligned,
+                          const mgb_tile_config* config, void* scratch, size_t scratch_bytes, cudaStream_t s,
+                          mgb_launch_info* info) {
+  const bool swiglu = p.swiglu != 0;
   const bool tensor_core = operands_tma_aligned && (dtype != MGB_FP32 || precision == MGB_TF32) && m > 0 &&
                            n > 0 && k > 0;
   if (swiglu && !tensor_core) return MGB_ERR_UNSUPPORTED;  // the fused epilogue exists on the tensor-core path only
@@ -302,15 +295,14 @@ int grouped_launch_impl(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
     }
     TcVariantInfo vi;
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
-    const int grid = v.pair ? 2 * grid_for(problem_count, m, n, v.tm, v.tn, std::max(1, vi.max_clusters))
-                            : grid_for(problem_count, m, n, v.tm, v.tn, ds.sm_count);
-    const size_t need = static_cast<size_t>(problem_count) * kMapsPerProblem * kMapBytes;
+    const int grid = v.pair ? 2 * grid_from(bound, v.tm, v.tn, n, std::max(1, vi.max_clusters))
+                            : grid_from(bound, v.tm, v.tn, n, ds.sm_count);
+    const size_t need = static_cast<size_t>(p.problem_count) * kMapsPerProblem * kMapBytes;
     if (scratch == nullptr || scratch_bytes < need || reinterpret_cast<uintptr_t>(scratch) % 128 != 0) {
       return MGB_ERR_SCRATCH;
     }
     p.desc_slots = static_cast<uint8_t*>(scratch);
-    const int64_t tiles = problem_count * cdiv(m, v.tm) * cdiv(n, v.tn);
-    p.unit_tiles = unit_tiles_for(tiles, k, vi.bk, v.pair ? grid / 2 : grid);
+    p.unit_tiles = unit_tiles_for(bound.tiles(v.tm, v.tn, n), k, vi.bk, v.pair ? grid / 2 : grid);
     // Templates: box shape, swizzle and element type are final; the device
     // rewrites the base address (and, for heterogeneous groups, the extents
     // and row pitch) of its copies per problem.  The scratch pointer stands in
@@ -323,9 +315,9 @@ int grouped_launch_impl(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
     const uint64_t out_n = swiglu ? static_cast<uint64_t>(n) / 2 : static_cast<uint64_t>(n);
     const uint64_t out_pitch = ((out_n * es + 15) / 16) * 16;
     CUtensorMap act, wgt, out;
-    if (!encode_2d(&act, dtype, scratch, k, m, act_pitch, vi.bk, vi.box_rows, kActSwizzle) ||
+    if (!encode_2d(&act, dtype, scratch, k, std::max<int64_t>(m, 1), act_pitch, vi.bk, vi.box_rows, kActSwizzle) ||
         !encode_2d(&wgt, dtype, scratch, n, k, wgt_pitch, vi.bk, vi.bk, wgt_swizzle(dtype)) ||
-        !encode_out(&out, dtype, scratch, out_n, m, out_pitch)) {
+        !encode_out(&out, dtype, scratch, out_n, std::max<int64_t>(m, 1), out_pitch)) {
       return MGB_ERR_CUDA;
     }
     if (maps_launch_typed(dtype, act, wgt, out, p, s) != 0) return MGB_ERR_CUDA;
@@ -334,11 +326,48 @@ int grouped_launch_impl(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
     fill_info(info, 0, v, vi, grid);
     return MGB_OK;
   }
-  const int grid = grid_for(problem_count, m, n, mgb::kSimtBM, mgb::kSimtBN, 4ll * ds.sm_count);
+  const int grid = grid_from(bound, mgb::kSimtBM, mgb::kSimtBN, n, 4ll * ds.sm_count);
   const int e = simt_launch_typed(dtype, p, grid, s);
   if (e != 0) return MGB_ERR_CUDA;
   fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0}, grid);
   return MGB_OK;
+}
+
+// Both table-driven grouped entry points: swiglu = 1 selects the fused SwiGLU epilogue.
+int grouped_launch_impl(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs, const int32_t* dims,
+                        const int64_t* strides, int32_t problem_count, int32_t homogeneous, int64_t m, int64_t n,
+                        int64_t k, int32_t dtype, int32_t precision, int32_t operands_tma_aligned,
+                        const mgb_tile_config* config, void* scratch, size_t scratch_bytes, void* stream,
+                        mgb_launch_info* info, int swiglu) {
+  if (!valid_dtype(dtype, precision) || problem_count <= 0 || a_ptrs == nullptr || b_ptrs == nullptr ||
+      c_ptrs == nullptr || m < 0 || n < 0 || k < 0) {
+    return MGB_ERR_INVALID;
+  }
+  if (swiglu && n % 2 != 0) return MGB_ERR_INVALID;
+  if (!homogeneous && (dims == nullptr || strides == nullptr)) return MGB_ERR_INVALID;
+  DeviceState ds;
+  if (int st = device_state(&ds)) return st;
+
+  GroupedParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.a_ptrs = a_ptrs;
+  p.b_ptrs = b_ptrs;
+  p.c_ptrs = c_ptrs;
+  p.dims = dims;
+  p.strides = strides;
+  p.problem_count = problem_count;
+  p.homogeneous = homogeneous ? 1 : 0;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.elem_bytes = elem_size(dtype);
+  p.wait_budget = g_wait_budget;
+  p.test_flags = g_test_flags;
+  p.error_word = ds.error_word;
+  p.swiglu = swiglu ? 1 : 0;
+  return launch_grouped_params(p, ds, TileBound{problem_count, m, 0}, m, n, k, dtype, precision,
+                               operands_tma_aligned != 0, config, scratch, scratch_bytes,
+                               static_cast<cudaStream_t>(stream), info);
 }
 
 }  // namespace
@@ -363,6 +392,55 @@ int grouped_gemm_swiglu_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, con
                              precision, operands_tma_aligned, config, scratch, scratch_bytes, stream, info, 1);
 }
 
+int grouped_gemm_offsets_launch(const void* a, const void* b, void* c, const int32_t* offs, int32_t problem_count,
+                                int64_t total_rows, int64_t n, int64_t k, int64_t stride_am, int64_t stride_be,
+                                int64_t stride_bk, int64_t stride_cm, int32_t dtype, int32_t precision,
+                                int32_t swiglu, const mgb_tile_config* config, void* scratch, size_t scratch_bytes,
+                                void* stream, mgb_launch_info* info) {
+  if (!valid_dtype(dtype, precision) || problem_count <= 0 || offs == nullptr || total_rows < 0 || n <= 0 ||
+      k < 0 || stride_am < k || stride_bk < n || stride_be < k * n || stride_cm < (swiglu ? n / 2 : n)) {
+    return MGB_ERR_INVALID;
+  }
+  if (total_rows > 0 && (a == nullptr || b == nullptr || c == nullptr)) return MGB_ERR_INVALID;
+  if (swiglu && n % 2 != 0) return MGB_ERR_INVALID;
+  DeviceState ds;
+  if (int st = device_state(&ds)) return st;
+  const int es = elem_size(dtype);
+  const auto aligned16 = [](const void* ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; };
+  const bool tma = aligned16(a) && aligned16(b) && (stride_am * es) % 16 == 0 && (stride_bk * es) % 16 == 0 &&
+                   (stride_be * es) % 16 == 0 && k < (1ll << 31) && n < (1ll << 31) && total_rows < (1ll << 31);
+
+  GroupedParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.offs = offs;
+  p.a = a;
+  p.b = b;
+  p.c = c;
+  p.sam = stride_am;
+  p.sak = 1;
+  p.sbk = stride_bk;
+  p.sbn = 1;
+  p.scm = stride_cm;
+  p.scn = 1;
+  p.sbe = stride_be;
+  p.elem_bytes = es;
+  p.problem_count = problem_count;
+  p.homogeneous = 0;
+  p.m = total_rows;
+  p.n = n;
+  p.k = k;
+  p.wait_budget = g_wait_budget;
+  p.test_flags = g_test_flags;
+  p.error_word = ds.error_word;
+  p.swiglu = swiglu ? 1 : 0;
+  if (total_rows == 0) {
+    fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0}, 0);
+    return MGB_OK;
+  }
+  return launch_grouped_params(p, ds, TileBound{1, total_rows, problem_count}, total_rows, n, k, dtype, precision,
+                               tma, config, scratch, scratch_bytes, static_cast<cudaStream_t>(stream), info);
+}
+
 int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k, int64_t stride_am,
                   int64_t stride_ak, int64_t stride_bk, int64_t stride_bn, int64_t stride_cm, int64_t stride_cn,
                   int32_t dtype, int32_t precision, const mgb_tile_config* config, void* stream,
@@ -377,6 +455,7 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
   std::memset(&p, 0, sizeof(p));
   p.single = 1;
   p.unit_tiles = 1;
+  p.elem_bytes = elem_size(dtype);
   p.problem_count = 1;
   p.m = m;
   p.n = n;

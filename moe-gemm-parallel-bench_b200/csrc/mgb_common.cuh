@@ -37,6 +37,12 @@ struct GroupedParams {
   int64_t sam, sak, sbk, sbn, scm, scn;
   // Scratch for the per-CTA tensor-map slots of the TMA path.
   uint8_t* desc_slots;
+  // Expert-sorted aggregate mode (offs != nullptr): one A [T, K] (rows of
+  // expert e are [offs[e-1], offs[e])), B [E, K, N] with `sbe` elements between
+  // experts, C [T, N]; pointers in a / b / c, row strides sam / sbk / scm.
+  const int32_t* offs;
+  int64_t sbe;
+  int32_t elem_bytes;
   int32_t unit_tiles;     // tensor-core kernels: consecutive tiles of one problem a CTA takes at a time
   int32_t swiglu;         // 1: fused SwiGLU epilogue, C_e[M, N/2] = silu(A_e B_e[:, :N/2]) * (A_e B_e[:, N/2:])
   long long wait_budget;  // SM clock cycles a barrier wait may take before the launch gives up
@@ -60,6 +66,18 @@ __device__ __forceinline__ Problem load_problem(const GroupedParams& p, int e) {
     q.b = static_cast<const char*>(p.b);
     q.c = static_cast<char*>(p.c);
     q.sam = p.sam; q.sak = p.sak; q.sbk = p.sbk; q.sbn = p.sbn; q.scm = p.scm; q.scn = p.scn;
+    return q;
+  }
+  if (p.offs != nullptr) {
+    const int64_t start = e > 0 ? p.offs[e - 1] : 0;
+    const int64_t es = p.elem_bytes;
+    q.m = static_cast<int64_t>(p.offs[e]) - start;
+    q.n = p.n;
+    q.k = p.k;
+    q.a = static_cast<const char*>(p.a) + start * p.sam * es;
+    q.b = static_cast<const char*>(p.b) + e * p.sbe * es;
+    q.c = static_cast<char*>(p.c) + start * p.scm * es;
+    q.sam = p.sam; q.sak = 1; q.sbk = p.sbk; q.sbn = 1; q.scm = p.scm; q.scn = 1;
     return q;
   }
   q.a = reinterpret_cast<const char*>(p.a_ptrs[e]);

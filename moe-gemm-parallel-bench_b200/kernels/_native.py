@@ -30,6 +30,7 @@ EXPORTED_SYMBOLS = (
     "grouped_gemm_scratch_bytes",
     "grouped_gemm_launch",
     "grouped_gemm_swiglu_launch",
+    "grouped_gemm_offsets_launch",
     "grouped_gemm_launch_noalloc",
     "matmul_launch",
     "matrix_repack",
@@ -119,6 +120,13 @@ def _declare(lib) -> None:
         ctypes.POINTER(TileConfig), ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
     ]
     lib.grouped_gemm_launch_noalloc.restype = ctypes.c_int
+    lib.grouped_gemm_offsets_launch.argtypes = [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(TileConfig), ctypes.c_void_p, ctypes.c_size_t,
+        ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
+    ]
+    lib.grouped_gemm_offsets_launch.restype = ctypes.c_int
     lib.matmul_launch.argtypes = [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
@@ -207,6 +215,23 @@ def grouped_launch(
         int(scratch_nbytes), stream, ctypes.byref(info),
     )
     _check(status, "grouped_gemm_swiglu_launch" if swiglu else "grouped_gemm_launch")
+    return info
+
+
+def offsets_launch(
+    a: int, b: int, c: int, offs: int, problem_count: int, total_rows: int, n: int, k: int, stride_am: int,
+    stride_be: int, stride_bk: int, stride_cm: int, dtype: str, precision: str, swiglu: bool, config, scratch: int,
+    scratch_nbytes: int, stream: int,
+) -> LaunchInfo:
+    """grouped_gemm_offsets_launch: the expert-sorted aggregate layout."""
+    info = LaunchInfo()
+    cfg = tile_config(config)
+    status = load().grouped_gemm_offsets_launch(
+        a, b, c, offs, int(problem_count), int(total_rows), int(n), int(k), int(stride_am), int(stride_be),
+        int(stride_bk), int(stride_cm), DTYPE_CODES[dtype], PRECISION_CODES[precision], int(bool(swiglu)),
+        ctypes.byref(cfg), scratch, int(scratch_nbytes), stream, ctypes.byref(info),
+    )
+    _check(status, "grouped_gemm_offsets_launch")
     return info
 
 

@@ -442,6 +442,68 @@ def launch_grouped(
     workspace.scheduler = scheduler
 
 
+_AGGREGATE_SCRATCH: dict[tuple[int, int], object] = {}
+
+
+def launch_grouped_mm(mat_a, mat_b, offs, out=None, *, config: KernelConfig | None = None,
+                      input_precision: str = "ieee", swiglu: bool = False):
+    """Grouped GEMM over the expert-sorted aggregate layout, in one native launch:
+    ``out[offs[e-1]:offs[e]] = mat_a[offs[e-1]:offs[e]] @ mat_b[e]``.
+
+    The layout of ``torch.nn.functional.grouped_mm(mat_a, mat_b, offs=offs)``
+    that the reference's torch provider builds (kernels/torch_grouped_gemm.py:
+    142-158): ``mat_a`` [T, K] with tokens sorted by expert, ``mat_b`` [E, K, N],
+    ``offs`` int32 [E] cumulative row ends on the same device (read by the
+    kernel, so no host synchronisation and CUDA-graph capturable once the
+    scratch exists: make the first call for a group size eagerly).  Rows of
+    ``mat_a`` / ``mat_b`` / ``out`` may be padded (row strides ≥ the logical
+    width); columns must be contiguous.  With ``swiglu`` each ``mat_b[e]`` is a
+    packed [gate | up] weight and ``out`` is [T, N/2] =
+    silu(A B_gate) * (A B_up).  ``config`` defaults to the native tile policy
+    for the average rows per expert.  Returns ``out``.
+    """
+    if torch is None or not torch.cuda.is_available():
+        raise RuntimeError("CUDA PyTorch and the native sm_100a library are required")
+    _native.load()
+    if mat_a.ndim != 2 or mat_b.ndim != 3 or offs.ndim != 1:
+        raise ValueError("expected mat_a [T, K], mat_b [E, K, N] and offs [E]")
+    total, k = mat_a.shape
+    experts, kb, n = mat_b.shape
+    if kb != k or offs.shape[0] != experts or experts == 0:
+        raise ValueError(f"shape mismatch: mat_a={tuple(mat_a.shape)}, mat_b={tuple(mat_b.shape)}, offs={tuple(offs.shape)}")
+    if offs.dtype != torch.int32:
+        raise ValueError("offs must be int32 cumulative row ends")
+    if mat_a.dtype != mat_b.dtype:
+        raise ValueError("mat_a and mat_b must share one dtype")
+    if len({mat_a.device, mat_b.device, offs.device}) != 1 or not mat_a.is_cuda:
+        raise ValueError("mat_a, mat_b and offs must be on the same CUDA device")
+    if swiglu and n % 2:
+        raise ValueError("SwiGLU requires an even packed [gate | up] width")
+    out_n = n // 2 if swiglu else n
+    if out is None:
+        out = torch.empty((total, out_n), device=mat_a.device, dtype=mat_a.dtype)
+    if out.shape != (total, out_n) or out.dtype != mat_a.dtype or out.device != mat_a.device:
+        raise ValueError(f"out must be [{total}, {out_n}] {mat_a.dtype} on {mat_a.device}")
+    if mat_a.stride(1) != 1 or mat_b.stride(2) != 1 or out.stride(1) != 1 or mat_b.stride(0) < k * mat_b.stride(1):
+        raise ValueError("columns of mat_a, mat_b and out must be contiguous (row padding is allowed)")
+    if input_precision not in _native.PRECISION_CODES:
+        raise ValueError(f"input_precision must be 'ieee' or 'tf32', got {input_precision!r}")
+    key = (mat_a.device.index or 0, experts)
+    scratch = _AGGREGATE_SCRATCH.get(key)
+    if scratch is None:
+        scratch = torch.empty(_native.scratch_bytes(experts, 0), dtype=torch.uint8, device=mat_a.device)
+        _AGGREGATE_SCRATCH[key] = scratch
+    cfg = config or native_candidates(max(1, -(-total // experts)), k)[0]
+    with torch.cuda.device(mat_a.device):
+        _native.offsets_launch(
+            mat_a.data_ptr(), mat_b.data_ptr(), out.data_ptr(), offs.data_ptr(), experts, total, n, k,
+            mat_a.stride(0), mat_b.stride(0), mat_b.stride(1), out.stride(0), dtype_name(mat_a.dtype),
+            input_precision, swiglu, cfg, scratch.data_ptr(), scratch.numel(),
+            torch.cuda.current_stream(mat_a.device).cuda_stream,
+        )
+    return out
+
+
 def check_device_errors(device=None) -> None:
     """Synchronises ``device`` and raises RuntimeError if a native kernel
     reported a device-side failure (bounded wait expiry, skipped problem)."""

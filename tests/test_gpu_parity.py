@@ -469,6 +469,114 @@ def test_fused_swiglu_refuses_the_generic_path():
         launch_grouped(ws32)
 
 
+# ------------------------------------------- expert-sorted aggregate layout
+def _aggregate(sizes, k, n, dtype_name, seed, pad=0, b_scale=0.1):
+    """mat_a [T, K] (row pitch K + pad), mat_b [E, K, N] (row pitch N + pad), int32 offs."""
+    torch = _torch()
+    gen = torch.Generator(device="cuda").manual_seed(seed)
+    dtype = _dtype(dtype_name)
+    total = int(sum(sizes))
+    mat_a = _randn((total, k + pad), dtype, gen, 1.0)[:, :k]
+    mat_b = _randn((len(sizes), k, n + pad), dtype, gen, b_scale)[:, :, :n]
+    offs = torch.tensor(np.cumsum(sizes), device="cuda", dtype=torch.int32)
+    return mat_a, mat_b, offs
+
+
+def _aggregate_check(out, mat_a, mat_b, sizes, dtype_name, precision="ieee", swiglu=False):
+    from oracle import gemm as oracle
+
+    start = 0
+    for e, size in enumerate(sizes):
+        if size:
+            a = _host(mat_a[start:start + size])
+            b = _host(mat_b[e])
+            expected = oracle.swiglu(a, b, dtype_name) if swiglu else oracle.matmul(a, b, dtype_name)
+            got = _host(out[start:start + size])
+            assert np.isfinite(got).all(), f"expert {e}: unwritten rows"
+            key = "tf32" if (dtype_name == "fp32" and precision == "tf32") else dtype_name
+            err = oracle.relative_frobenius(got, expected)
+            assert err <= REL_FRO[key], f"expert {e}: relative Frobenius error {err:.3e}"
+        start += size
+
+
+@pytest.mark.parametrize("dtype_name", ["fp16", "bf16"])
+def test_aggregate_layout_uneven_experts_every_tile(dtype_name):
+    """launch_grouped_mm over tokens sorted by expert with uneven and empty
+    groups, for every native tile family; oracle per expert segment."""
+    torch = _torch()
+    from kernels import KernelConfig, launch_grouped_mm
+
+    sizes = [37, 0, 300, 1, 0, 129, 16, 64]
+    mat_a, mat_b, offs = _aggregate(sizes, 192, 320, dtype_name, seed=9)
+    out = torch.full((sum(sizes), 320), float("nan"), device="cuda", dtype=_dtype(dtype_name))
+    for cfg in (None, KernelConfig(16, 256, 64, 4, 8, 4), KernelConfig(64, 128, 64, 8, 4, 4),
+                KernelConfig(128, 256, 64, 8, 8, 4), KernelConfig(256, 128, 64, 8, 8, 4),
+                KernelConfig(256, 256, 64, 8, 8, 4)):
+        out.fill_(float("nan"))
+        launch_grouped_mm(mat_a, mat_b, offs, out, config=cfg)
+        torch.cuda.synchronize()
+        _aggregate_check(out, mat_a, mat_b, sizes, dtype_name)
+
+
+def test_aggregate_layout_padding_precisions_and_swiglu():
+    """Padded row pitches (C not TMA-addressable -> staged stores), fp32 on the
+    generic kernel and on TF32 tensor cores, the fused SwiGLU epilogue, and a
+    cross-check with torch's grouped_mm where it exists."""
+    torch = _torch()
+    from kernels import check_device_errors, launch_grouped_mm
+
+    sizes = [5, 70, 0, 200]
+    mat_a, mat_b, offs = _aggregate(sizes, 100, 100, "bf16", seed=2, pad=4)
+    out = launch_grouped_mm(mat_a, mat_b, offs)
+    torch.cuda.synchronize()
+    _aggregate_check(out, mat_a, mat_b, sizes, "bf16")
+    grouped_mm = getattr(torch.nn.functional, "grouped_mm", None)
+    if grouped_mm is not None:
+        try:
+            ref = grouped_mm(mat_a, mat_b, offs=offs)
+        except RuntimeError:
+            ref = None
+        if ref is not None:
+            torch.testing.assert_close(out.float(), ref.float(), rtol=5e-2, atol=5e-2)
+    for precision in ("ieee", "tf32"):
+        a32, b32, offs32 = _aggregate(sizes, 64, 96, "fp32", seed=3)
+        out32 = launch_grouped_mm(a32, b32, offs32, input_precision=precision)
+        torch.cuda.synchronize()
+        _aggregate_check(out32, a32, b32, sizes, "fp32", precision=precision)
+    sw_sizes = [16, 0, 130, 300]
+    a, b, offs_sw = _aggregate(sw_sizes, 256, 2 * 192, "bf16", seed=4, b_scale=1.0 / 16)
+    h = launch_grouped_mm(a, b, offs_sw, swiglu=True)
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert h.shape == (sum(sw_sizes), 192)
+    _aggregate_check(h, a, b, sw_sizes, "bf16", swiglu=True)
+
+
+def test_aggregate_layout_graph_replay_follows_device_offsets():
+    """Captured once; the routing (offs) changes on the device between
+    replays and the output follows it."""
+    torch = _torch()
+    from kernels import launch_grouped_mm
+
+    sizes = [64, 64, 64, 64]
+    mat_a, mat_b, offs = _aggregate(sizes, 128, 256, "bf16", seed=6)
+    out = torch.empty((256, 256), device="cuda", dtype=torch.bfloat16)
+    launch_grouped_mm(mat_a, mat_b, offs, out)  # eager first call: scratch exists before capture
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        launch_grouped_mm(mat_a, mat_b, offs, out)
+    new_sizes = [10, 0, 200, 46]
+    offs.copy_(torch.tensor(np.cumsum(new_sizes), device="cuda", dtype=torch.int32))
+    out.fill_(float("nan"))
+    graph.replay()
+    torch.cuda.synchronize()
+    _aggregate_check(out, mat_a, mat_b, new_sizes, "bf16")
+    del graph
+
+
 def test_one_problem_group_dispatches_standard_matmul():
     """tests/test_gpu.py:190-195."""
     torch = _torch()
