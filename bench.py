@@ -67,6 +67,9 @@ def parse_args(argv=None):
     p.add_argument("--m-values", type=str, default=",".join(map(str, M_VALUES)))
     p.add_argument("--projection", choices=("W1", "W2"), default="W1",
                    help="W1: packed W13 gate+up (the benchmark line); W2: down projection (BASELINE configs[2])")
+    p.add_argument("--layout", choices=("tables", "aggregate"), default="tables",
+                   help="W1: per-expert pointer tables (the reference's workspaces) or the expert-sorted "
+                        "aggregate layout (launch_grouped_mm: A [E*M_e, K], B [E, K, N], int32 offsets)")
     p.add_argument("--fused-swiglu", action="store_true",
                    help="W1 only: launch with the fused SwiGLU epilogue (C = silu(gate) * up, [M_e, F_local])")
     p.add_argument("--cache-mode", choices=("hot", "cold"), default="hot",
@@ -355,6 +358,76 @@ def verify_w2_outputs(rank, world, ep, tp, outputs, device, m_values, seed: int 
     return {"checked_experts": sampled, "checked_m": checks, "max_rel_frobenius": worst, "passed": worst <= 1e-2}
 
 
+class AggregateLaunch:
+    """One launch_grouped_mm call of the step (expert-sorted aggregate layout),
+    standing in for a grouped workspace: same shapes, counts and launch info."""
+
+    def __init__(self, mat_a, mat_b, offs, out, shape, count, swiglu):
+        self.mat_a, self.mat_b, self.offs, self.out = mat_a, mat_b, offs, out
+        self.shapes = (shape,)
+        self.problem_count = count
+        self.max_m = shape[0]
+        self.swiglu = swiglu
+        self.config = None
+        self.launch_info = None
+
+    def run(self, config=None) -> None:
+        from kernels import last_aggregate_launch_info, launch_grouped_mm
+
+        launch_grouped_mm(self.mat_a, self.mat_b, self.offs, self.out, config=config, swiglu=self.swiglu)
+        self.launch_info = last_aggregate_launch_info()
+        self.config = config or "native policy"
+
+
+def build_rank_aggregate(rank: int, m_values, device, parallel=("EP", "TP"), expert_limit=None,
+                         swiglu: bool = False):
+    """W13 rank tensors in the expert-sorted aggregate layout: per M_e one
+    activation block [E, M_e, 7168] (EP ranks use their experts' contiguous
+    slice), stacked weights [E, 7168, N] and uniform int32 offsets."""
+    import torch
+
+    from moe_parallel import rank_plan, shard_weight
+
+    ep = rank_plan("W1", "EP", rank, PARALLEL, EXPERTS, FFN, HIDDEN)
+    tp = rank_plan("W1", "TP", rank, PARALLEL, EXPERTS, FFN, HIDDEN)
+    ep_experts = ep.experts[:expert_limit] if expert_limit else ep.experts
+    tp_experts = tp.experts[:expert_limit] if expert_limit else tp.experts
+    w_ep = torch.empty((len(ep_experts), HIDDEN, 2 * FFN), device=device, dtype=torch.bfloat16) \
+        if "EP" in parallel else None
+    w_tp = torch.empty((len(tp_experts), HIDDEN, 2 * tp.local_ffn), device=device, dtype=torch.bfloat16) \
+        if "TP" in parallel else None
+    for e in range(EXPERTS):
+        if not ((e in ep_experts and w_ep is not None) or (e in tp_experts and w_tp is not None)):
+            continue
+        w = expert_weight(e, device)
+        if e in ep_experts and w_ep is not None:
+            w_ep[ep_experts.index(e)].copy_(w)
+        if e in tp_experts and w_tp is not None:
+            w_tp[tp_experts.index(e)].copy_(shard_weight(w, tp))
+        del w
+    width = 1 if swiglu else 2
+    activations, outputs, launches = {}, {}, []
+    for m in m_values:
+        gen = torch.Generator(device=device).manual_seed(7919 * m)
+        a_all = torch.randn((EXPERTS, m, HIDDEN), device=device, generator=gen).to(torch.bfloat16)
+        activations[m] = a_all
+        c_ep = torch.empty((len(ep_experts), m, width * FFN), device=device, dtype=torch.bfloat16)
+        c_tp = torch.empty((len(tp_experts), m, width * tp.local_ffn), device=device, dtype=torch.bfloat16)
+        outputs[m] = (c_ep, c_tp)
+        if w_ep is not None:
+            lo = ep_experts[0]
+            a_ep = a_all[lo:lo + len(ep_experts)].reshape(-1, HIDDEN)
+            offs = torch.arange(1, len(ep_experts) + 1, device=device, dtype=torch.int32) * m
+            launches.append(("EP", m, AggregateLaunch(a_ep, w_ep, offs, c_ep.view(-1, c_ep.shape[-1]),
+                                                      (m, HIDDEN, 2 * FFN), len(ep_experts), swiglu)))
+        if w_tp is not None:
+            a_tp = a_all[:len(tp_experts)].reshape(-1, HIDDEN)
+            offs = torch.arange(1, len(tp_experts) + 1, device=device, dtype=torch.int32) * m
+            launches.append(("TP", m, AggregateLaunch(a_tp, w_tp, offs, c_tp.view(-1, c_tp.shape[-1]),
+                                                      (m, HIDDEN, 2 * tp.local_ffn), len(tp_experts), swiglu)))
+    return ep, tp, activations, outputs, launches
+
+
 FIXED_CONFIG = None  # set by --config: launches use it instead of the autotuned winner
 CLASS_CONFIGS: dict[str, object] = {}  # set by --config-small / --config-large
 
@@ -363,7 +436,9 @@ def launch(ws) -> None:
     from kernels import launch_grouped
 
     fixed = FIXED_CONFIG or CLASS_CONFIGS.get(ws.max_m) or CLASS_CONFIGS.get("small" if ws.max_m <= 128 else "large")
-    if fixed is None:
+    if isinstance(ws, AggregateLaunch):
+        ws.run(fixed)
+    elif fixed is None:
         launch_grouped(ws)
     else:
         launch_grouped(ws, config=fixed, autotune=False)
@@ -636,7 +711,12 @@ def main(argv=None) -> int:
     progress("building rank tensors")
     if args.fused_swiglu and args.projection != "W1":
         raise SystemExit("--fused-swiglu applies to the W1 (packed gate+up) projection")
-    if args.projection == "W1":
+    if args.layout == "aggregate" and (args.projection != "W1" or args.cache_mode != "hot"):
+        raise SystemExit("--layout aggregate measures the hot W1 step")
+    if args.layout == "aggregate":
+        ep, tp, activations, outputs, workspaces = build_rank_aggregate(rank, m_values, device, parallel,
+                                                                        args.expert_limit, swiglu=args.fused_swiglu)
+    elif args.projection == "W1":
         ep, tp, activations, outputs, workspaces = build_rank(rank, m_values, device, parallel, args.expert_limit,
                                                               swiglu=args.fused_swiglu)
     else:
@@ -798,7 +878,9 @@ def main(argv=None) -> int:
             "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": (WORKLOAD if args.projection == "W1" else WORKLOAD_W2)
-                       + ("; fused SwiGLU epilogue: C = silu(gate) * up, [M_e, F_local]" if args.fused_swiglu else ""),
+                       + ("; fused SwiGLU epilogue: C = silu(gate) * up, [M_e, F_local]" if args.fused_swiglu else "")
+                       + ("; expert-sorted aggregate layout (launch_grouped_mm, int32 offsets)"
+                          if args.layout == "aggregate" else ""),
                        "parallelism": f"GPU r runs rank r of P=8 (EP and TP), {world} rank(s)",
                        "cache": ("hot; inputs larger than L2 (0.94-1.88 GB of weights per projection), no flush"
                                  if args.cache_mode == "hot" else

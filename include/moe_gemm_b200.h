@@ -53,9 +53,9 @@ typedef struct mgb_launch_info {
 } mgb_launch_info;
 
 /* Bytes of scratch a grouped launch of `problem_count` problems needs: the
- * A, B and C tensor maps of every problem (3 x 128 bytes each), built on the
- * device by a small kernel that runs just before the GEMM kernel.  `sm_count`
- * is not used.  Replaces nothing in the reference: Triton kernels there take
+ * A, B and C tensor maps of every problem (3 x 128 bytes each) plus
+ * problem_count + 1 int64 tile-walk offsets, built on the device by a small
+ * kernel that runs just before the GEMM kernel.  `sm_count` is not used.  Replaces nothing in the reference: Triton kernels there take
  * raw pointers and need no descriptors. */
 size_t grouped_gemm_scratch_bytes(int32_t problem_count, int32_t sm_count);
 
@@ -166,7 +166,7 @@ int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r,
  *   - The first call on a device looks up the array's device address (once per
  *     device, with that device current); make that first call before any
  *     stream capture.
- *   - A launch that needs more than MGB_NOALLOC_SCRATCH_BYTES (more than 2730
+ *   - A launch that needs more than MGB_NOALLOC_SCRATCH_BYTES (more than 2674
  *     problems) is refused with MGB_ERR_SCRATCH.
  *   - Every call shares the one array and leaves its last contents behind;
  *     nothing in it has to start at zero (each launch writes every map before

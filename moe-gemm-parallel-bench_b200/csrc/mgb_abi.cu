@@ -248,7 +248,7 @@ int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r,
 size_t grouped_gemm_scratch_bytes(int32_t problem_count, int32_t sm_count) {
   (void)sm_count;
   const size_t problems = problem_count > 0 ? static_cast<size_t>(problem_count) : 1;
-  return problems * kMapsPerProblem * kMapBytes;
+  return problems * kMapsPerProblem * kMapBytes + (problems + 1) * sizeof(int64_t);
 }
 
 }  // extern "C"
@@ -297,12 +297,20 @@ int launch_grouped_params(GroupedParams& p, const DeviceState& ds, const TileBou
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
     const int grid = v.pair ? 2 * grid_from(bound, v.tm, v.tn, n, std::max(1, vi.max_clusters))
                             : grid_from(bound, v.tm, v.tn, n, ds.sm_count);
-    const size_t need = static_cast<size_t>(p.problem_count) * kMapsPerProblem * kMapBytes;
+    const size_t maps_bytes = static_cast<size_t>(p.problem_count) * kMapsPerProblem * kMapBytes;
+    const size_t need = maps_bytes + (static_cast<size_t>(p.problem_count) + 1) * sizeof(int64_t);
     if (scratch == nullptr || scratch_bytes < need || reinterpret_cast<uintptr_t>(scratch) % 128 != 0) {
       return MGB_ERR_SCRATCH;
     }
     p.desc_slots = static_cast<uint8_t*>(scratch);
     p.unit_tiles = unit_tiles_for(bound.tiles(v.tm, v.tn, n), k, vi.bk, v.pair ? grid / 2 : grid);
+    if (!p.homogeneous && !p.single) {
+      // Heterogeneous groups: the map builder also writes the walk's unit
+      // prefix sums after the maps, for this tile shape.
+      p.unit_start = reinterpret_cast<int64_t*>(static_cast<uint8_t*>(scratch) + maps_bytes);
+      p.walk_tm = v.tm;
+      p.walk_tn = v.tn;
+    }
     // Templates: box shape, swizzle and element type are final; the device
     // rewrites the base address (and, for heterogeneous groups, the extents
     // and row pitch) of its copies per problem.  The scratch pointer stands in

@@ -44,6 +44,12 @@ struct GroupedParams {
   int64_t sbe;
   int32_t elem_bytes;
   int32_t unit_tiles;     // tensor-core kernels: consecutive tiles of one problem a CTA takes at a time
+  // Heterogeneous tensor-core launches: unit_start[e] = units of problems
+  // [0, e) (E + 1 entries, written by the map builder before the GEMM kernel
+  // runs) for the tile shape walk_tm x walk_tn, so the walk finds a unit's
+  // problem by binary search instead of scanning the table.
+  int64_t* unit_start;
+  int32_t walk_tm, walk_tn;
   int32_t swiglu;         // 1: fused SwiGLU epilogue, C_e[M, N/2] = silu(A_e B_e[:, :N/2]) * (A_e B_e[:, N/2:])
   long long wait_budget;  // SM clock cycles a barrier wait may take before the launch gives up
   int32_t test_flags;     // bit 0: make the epilogue wait on a barrier nothing arrives on
@@ -143,6 +149,30 @@ struct TileWalk {
         prob = load_problem(p, problem);
       }
       ufirst = e * ucount;
+    } else if (p.unit_start != nullptr) {
+      // Largest problem whose first unit is <= u (empty problems share their
+      // successor's start, so the search lands on the one that owns u).
+      const int64_t* us = p.unit_start;
+      if (u >= us[p.problem_count]) return false;
+      if (problem < 0 || u >= ufirst + ucount) {
+        int lo = problem < 0 ? 0 : problem;
+        int hi = p.problem_count - 1;
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (us[mid] <= u) {
+            lo = mid;
+          } else {
+            hi = mid - 1;
+          }
+        }
+        problem = lo;
+        prob = load_problem(p, problem);
+        m_blocks = ceil_div64(prob.m, TM);
+        count = m_blocks * ceil_div64(prob.n, TN);
+        first = 0;  // tiles are numbered inside the problem
+        ufirst = us[problem];
+        ucount = us[problem + 1] - ufirst;
+      }
     } else {
       while (problem < 0 || u >= ufirst + ucount) {
         first += count;

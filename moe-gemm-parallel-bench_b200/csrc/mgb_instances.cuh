@@ -149,7 +149,8 @@ int tc_launch<MGB_ELEM>(const TcVariant& v, const CUtensorMap& act, const CUtens
 template <>
 int maps_launch<MGB_ELEM>(const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
                           const GroupedParams& p, cudaStream_t stream) {
-  build_maps_kernel<MGB_ELEM><<<p.problem_count, 32, 0, stream>>>(act, wgt, out, p);
+  const int blocks = p.problem_count + (p.unit_start != nullptr ? 1 : 0);  // + the unit prefix-sum block
+  build_maps_kernel<MGB_ELEM><<<blocks, 32, 0, stream>>>(act, wgt, out, p);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -23,8 +23,9 @@
 
 namespace {
 
-// Largest scratch one launch may use: 3 tensor maps of 128 bytes per problem,
-// so 1 MiB covers groups of up to 2730 problems (DeepSeek-V3 TP ranks hold 256).
+// Largest scratch one launch may use: 3 tensor maps of 128 bytes and one int64
+// walk offset per problem (+ 8 bytes), so 1 MiB covers groups of up to 2674
+// problems (DeepSeek-V3 TP ranks hold 256).
 constexpr size_t kNoAllocScratchBytes = MGB_NOALLOC_SCRATCH_BYTES;
 
 static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];

@@ -453,6 +453,39 @@ __global__ void __launch_bounds__(32)
   __shared__ alignas(128) CUtensorMap staging[kMapsPerProblem];
   const int e = blockIdx.x;
   const int lane = threadIdx.x;
+  if (e == p.problem_count && p.unit_start != nullptr) {
+    // The extra block of a heterogeneous launch: exclusive prefix sum of the
+    // walk's units per problem (the tile walk's rules: empty or invalid
+    // problems have none), lane l summing a contiguous run of problems.
+    const int per = (p.problem_count + 31) / 32;
+    const int lo = lane * per;
+    const int hi = lo + per < p.problem_count ? lo + per : p.problem_count;
+    const int64_t unit = p.unit_tiles > 0 ? p.unit_tiles : 1;
+    int64_t sum = 0;
+    for (int i = lo; i < hi; ++i) {
+      const Problem q = load_problem(p, i);
+      if (q.m > 0 && q.n > 0 && q.k >= 0) {
+        const int64_t tiles = ceil_div64(q.m, p.walk_tm) * ceil_div64(q.n, p.walk_tn);
+        sum += ceil_div64(tiles, unit);
+      }
+    }
+    int64_t incl = sum;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const int64_t v = __shfl_up_sync(0xffffffffu, incl, d);
+      if (lane >= d) incl += v;
+    }
+    int64_t run = incl - sum;
+    for (int i = lo; i < hi; ++i) {
+      p.unit_start[i] = run;
+      const Problem q = load_problem(p, i);
+      if (q.m > 0 && q.n > 0 && q.k >= 0) {
+        run += ceil_div64(ceil_div64(q.m, p.walk_tm) * ceil_div64(q.n, p.walk_tn), unit);
+      }
+    }
+    if (lane == 31) p.unit_start[p.problem_count] = incl;
+    return;
+  }
   if (e >= p.problem_count) return;
   if (lane == 0) {
     const Problem q = load_problem(p, e);

@@ -10,6 +10,7 @@ from .grouped_gemm import (
     build_fused_gate_up_workspace,
     build_fused_swiglu_workspace,
     build_grouped_workspace,
+    last_aggregate_launch_info,
     launch_grouped_mm,
     check_device_errors,
     grouped_candidate_configs,
@@ -30,6 +31,7 @@ __all__ = [
     "KernelConfig",
     "build_fused_gate_up_workspace",
     "build_fused_swiglu_workspace",
+    "last_aggregate_launch_info",
     "launch_grouped_mm",
     "build_grouped_workspace",
     "check_device_errors",

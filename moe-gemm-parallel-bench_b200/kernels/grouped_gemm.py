@@ -443,6 +443,12 @@ def launch_grouped(
 
 
 _AGGREGATE_SCRATCH: dict[tuple[int, int], object] = {}
+_last_aggregate_info: dict | None = None
+
+
+def last_aggregate_launch_info() -> dict | None:
+    """Native kernel of the most recent launch_grouped_mm call (path, tile, grid)."""
+    return _last_aggregate_info
 
 
 def launch_grouped_mm(mat_a, mat_b, offs, out=None, *, config: KernelConfig | None = None,
@@ -493,14 +499,16 @@ def launch_grouped_mm(mat_a, mat_b, offs, out=None, *, config: KernelConfig | No
     if scratch is None:
         scratch = torch.empty(_native.scratch_bytes(experts, 0), dtype=torch.uint8, device=mat_a.device)
         _AGGREGATE_SCRATCH[key] = scratch
+    global _last_aggregate_info
     cfg = config or native_candidates(max(1, -(-total // experts)), k)[0]
     with torch.cuda.device(mat_a.device):
-        _native.offsets_launch(
+        info = _native.offsets_launch(
             mat_a.data_ptr(), mat_b.data_ptr(), out.data_ptr(), offs.data_ptr(), experts, total, n, k,
             mat_a.stride(0), mat_b.stride(0), mat_b.stride(1), out.stride(0), dtype_name(mat_a.dtype),
             input_precision, swiglu, cfg, scratch.data_ptr(), scratch.numel(),
             torch.cuda.current_stream(mat_a.device).cuda_stream,
         )
+    _last_aggregate_info = info.as_dict()
     return out
 
 

@@ -61,11 +61,11 @@ def test_host_only_entry_points():
     assert _native.status_text(_native.STATUS_OK) == "ok"
     assert "scratch" in _native.status_text(_native.STATUS_SCRATCH)
     assert _native.status_text(99) == "unknown status"
-    # A, B and C tensor maps of 128 bytes per problem.
-    assert _native.scratch_bytes(256, 148) == 256 * 3 * 128
-    assert _native.scratch_bytes(1, 0) == 3 * 128
-    assert _native.scratch_bytes(0, 0) == 3 * 128
-    assert _native.scratch_bytes(2730, 148) <= _native.NOALLOC_SCRATCH_BYTES < _native.scratch_bytes(2731, 148)
+    # A, B and C tensor maps of 128 bytes per problem, plus E + 1 int64 walk offsets.
+    assert _native.scratch_bytes(256, 148) == 256 * 3 * 128 + 257 * 8
+    assert _native.scratch_bytes(1, 0) == 3 * 128 + 2 * 8
+    assert _native.scratch_bytes(0, 0) == 3 * 128 + 2 * 8
+    assert _native.scratch_bytes(2674, 148) <= _native.NOALLOC_SCRATCH_BYTES < _native.scratch_bytes(2675, 148)
     _native.set_debug(1000, 1)
     _native.set_debug(0, 0)
 
