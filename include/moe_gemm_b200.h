@@ -131,6 +131,29 @@ int grouped_gemm_offsets_launch(const void* a, const void* b, void* c, const int
                                 int32_t swiglu, const mgb_tile_config* config, void* scratch, size_t scratch_bytes,
                                 void* stream, mgb_launch_info* info);
 
+/* FP8 block-scaled grouped GEMM (DeepSeek-V3 quantization): for e in [0, problem_count)
+ *   C_e[M, N] = sum_kb (A_e[:, kb] @ B_e[:, kb]^T) * SA_e[:, kb] * SB_e[n / 128, kb]
+ * over 128-deep K blocks kb, fp32 accumulation, bf16 output.
+ *   a_ptrs   e4m3 A_e [M, K], contiguous (tokens)
+ *   b_ptrs   e4m3 B_e [N, K], contiguous (a linear weight as checkpoints store it)
+ *   c_ptrs   bf16 C_e [M, N], contiguous
+ *   sa_ptrs  fp32 SA_e [M, ceil(K/128)]: one scale per token and K block
+ *   sb_ptrs  fp32 SB_e [ceil(N/128), ceil(K/128)]: one scale per 128 x 128 weight block
+ *   dims     int32 [problem_count, 3] (M, N, K) unless homogeneous (then m, n, k)
+ * The tensor-core path needs 16-byte aligned bases, K a multiple of 16 and N a
+ * multiple of 8; a homogeneous group that breaks it is refused with
+ * MGB_ERR_UNSUPPORTED, a heterogeneous entry is skipped and reported in the
+ * error word.  config->block_m picks the tile (<= 16 / 32 / 64: swap-AB with
+ * that many tokens x 256 weight rows; larger: 128 x 128).  Scratch:
+ * grouped_gemm_scratch_bytes(problem_count, *).  No counterpart in the
+ * reference, which runs every expert in fp16 / bf16 / fp32 and notes that the
+ * model's FP8 quantization is not emulated (README.md:298). */
+int grouped_gemm_fp8_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs,
+                            const int64_t* sa_ptrs, const int64_t* sb_ptrs, const int32_t* dims,
+                            int32_t problem_count, int32_t homogeneous, int64_t m, int64_t n, int64_t k,
+                            const mgb_tile_config* config, void* scratch, size_t scratch_bytes, void* stream,
+                            mgb_launch_info* info);
+
 /* Masked single GEMM C[m, n] = A[m, k] @ B[k, n] with arbitrary element strides.
  * Replaces the Triton launch of launch_matmul (kernels/matmul.py:332-392,
  * kernel _matmul_kernel_impl :223-273).  Operands that satisfy the TMA rules

@@ -74,7 +74,10 @@ int device_state(DeviceState* out) {
   return MGB_OK;
 }
 
-int elem_size(int dtype) { return dtype == MGB_FP32 ? 4 : 2; }
+// Internal element type of the FP8 path's operand maps (raw bytes; e4m3 data).
+constexpr int kDtypeU8 = 100;
+
+int elem_size(int dtype) { return dtype == MGB_FP32 ? 4 : dtype == kDtypeU8 ? 1 : 2; }
 
 // Activations (K-major) always use the 128-byte swizzle.  Weights are the
 // MN-major operand: MN-major TF32 needs the 32-byte-granule 128-byte swizzle.
@@ -84,7 +87,8 @@ CUtensorMapSwizzle wgt_swizzle(int dtype) {
 }
 
 CUtensorMapDataType map_type(int dtype) {
-  return dtype == MGB_FP32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+  return dtype == kDtypeU8   ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+         : dtype == MGB_FP32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
          : dtype == MGB_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                              : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
@@ -447,6 +451,83 @@ int grouped_gemm_offsets_launch(const void* a, const void* b, void* c, const int
   }
   return launch_grouped_params(p, ds, TileBound{1, total_rows, problem_count}, total_rows, n, k, dtype, precision,
                                tma, config, scratch, scratch_bytes, static_cast<cudaStream_t>(stream), info);
+}
+
+int grouped_gemm_fp8_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs,
+                            const int64_t* sa_ptrs, const int64_t* sb_ptrs, const int32_t* dims,
+                            int32_t problem_count, int32_t homogeneous, int64_t m, int64_t n, int64_t k,
+                            const mgb_tile_config* config, void* scratch, size_t scratch_bytes, void* stream,
+                            mgb_launch_info* info) {
+  if (problem_count <= 0 || a_ptrs == nullptr || b_ptrs == nullptr || c_ptrs == nullptr || sa_ptrs == nullptr ||
+      sb_ptrs == nullptr || m < 0 || n < 0 || k < 0 || (!homogeneous && dims == nullptr)) {
+    return MGB_ERR_INVALID;
+  }
+  if (homogeneous && (k % 16 != 0 || n % 8 != 0)) return MGB_ERR_UNSUPPORTED;  // TMA row pitches
+  DeviceState ds;
+  if (int st = device_state(&ds)) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (m == 0 || n == 0) {
+    fill_info(info, 0, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0}, 0);
+    return MGB_OK;
+  }
+  const int bm = config ? config->block_m : 64;
+  const TcVariant v = bm <= 16 ? TcVariant{true, 16, 256}
+                      : bm <= 32 ? TcVariant{true, 32, 256}
+                      : bm <= 64 ? TcVariant{true, 64, 256}
+                                 : TcVariant{false, 128, 128};
+  TcVariantInfo vi;
+  if (!mgb::fp8_variant_info(v, &vi)) return MGB_ERR_UNSUPPORTED;
+
+  GroupedParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.a_ptrs = a_ptrs;
+  p.b_ptrs = b_ptrs;
+  p.c_ptrs = c_ptrs;
+  p.sa_ptrs = sa_ptrs;
+  p.sb_ptrs = sb_ptrs;
+  p.dims = dims;
+  p.problem_count = problem_count;
+  p.homogeneous = homogeneous ? 1 : 0;
+  p.m = m;
+  p.n = n;
+  p.k = k;
+  p.elem_bytes = 1;
+  p.wait_budget = g_wait_budget;
+  p.test_flags = g_test_flags;
+  p.error_word = ds.error_word;
+  // Heterogeneous groups read their dims from `dims`; strides are implied
+  // (contiguous A [M, K], B [N, K], C [M, N]), so no stride table is read.
+
+  const TileBound bound{problem_count, m, 0};
+  const int grid = grid_from(bound, v.tm, v.tn, n, ds.sm_count);
+  const size_t maps_bytes = static_cast<size_t>(problem_count) * kMapsPerProblem * kMapBytes;
+  const size_t need = maps_bytes + (static_cast<size_t>(problem_count) + 1) * sizeof(int64_t);
+  if (scratch == nullptr || scratch_bytes < need || reinterpret_cast<uintptr_t>(scratch) % 128 != 0) {
+    return MGB_ERR_SCRATCH;
+  }
+  p.desc_slots = static_cast<uint8_t*>(scratch);
+  p.unit_tiles = unit_tiles_for(bound.tiles(v.tm, v.tn, n), k, vi.bk, grid);
+  if (!homogeneous) {
+    p.unit_start = reinterpret_cast<int64_t*>(static_cast<uint8_t*>(scratch) + maps_bytes);
+    p.walk_tm = v.tm;
+    p.walk_tn = v.tn;
+  }
+  // Templates (box, swizzle, element type final; the device rewrites base
+  // addresses, and for heterogeneous groups extents and pitches, per problem).
+  const uint64_t row_bytes = ((static_cast<uint64_t>(std::max<int64_t>(k, 1)) + 15) / 16) * 16;
+  const uint64_t out_pitch = ((static_cast<uint64_t>(n) * 2 + 15) / 16) * 16;
+  CUtensorMap act, wgt, out;
+  if (!encode_2d(&act, kDtypeU8, scratch, std::max<int64_t>(k, 1), m, row_bytes, 128, vi.box_rows,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_2d(&wgt, kDtypeU8, scratch, std::max<int64_t>(k, 1), n, row_bytes, 128, vi.box_cols,
+                 CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !encode_out(&out, MGB_BF16, scratch, n, m, out_pitch)) {
+    return MGB_ERR_CUDA;
+  }
+  if (mgb::fp8_maps_launch(act, wgt, out, p, s) != 0) return MGB_ERR_CUDA;
+  if (mgb::fp8_launch(v, act, wgt, out, p, grid, s) != 0) return MGB_ERR_CUDA;
+  fill_info(info, 0, v, vi, grid);
+  return MGB_OK;
 }
 
 int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, int64_t k, int64_t stride_am,

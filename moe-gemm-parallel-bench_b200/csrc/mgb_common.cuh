@@ -50,6 +50,11 @@ struct GroupedParams {
   // problem by binary search instead of scanning the table.
   int64_t* unit_start;
   int32_t walk_tm, walk_tn;
+  // FP8 block-scaled launches: per-problem fp32 scale tables, SA_e
+  // [M, ceil(K/128)] (per token and 128-deep K block) and SB_e
+  // [ceil(N/128), ceil(K/128)] (per 128 x 128 weight block), row-major.
+  const int64_t* sa_ptrs;
+  const int64_t* sb_ptrs;
   int32_t swiglu;         // 1: fused SwiGLU epilogue, C_e[M, N/2] = silu(A_e B_e[:, :N/2]) * (A_e B_e[:, N/2:])
   long long wait_budget;  // SM clock cycles a barrier wait may take before the launch gives up
   int32_t test_flags;     // bit 0: make the epilogue wait on a barrier nothing arrives on
@@ -97,8 +102,12 @@ __device__ __forceinline__ Problem load_problem(const GroupedParams& p, int e) {
     q.m = p.dims[3 * e + 0];
     q.n = p.dims[3 * e + 1];
     q.k = p.dims[3 * e + 2];
-    const int64_t* s = p.strides + 6 * e;
-    q.sam = s[0]; q.sak = s[1]; q.sbk = s[2]; q.sbn = s[3]; q.scm = s[4]; q.scn = s[5];
+    if (p.strides != nullptr) {
+      const int64_t* s = p.strides + 6 * e;
+      q.sam = s[0]; q.sak = s[1]; q.sbk = s[2]; q.sbn = s[3]; q.scm = s[4]; q.scn = s[5];
+    } else {  // tables without strides (the FP8 path): contiguous A [M, K], B [N, K], C [M, N]
+      q.sam = q.k; q.sak = 1; q.sbk = q.k; q.sbn = 1; q.scm = q.n; q.scn = 1;
+    }
   }
   return q;
 }

@@ -46,6 +46,14 @@ template <typename T>
 int maps_launch(const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out, const GroupedParams& p,
                 cudaStream_t stream);
 
+// FP8 block-scaled variants (mgb_fp8.cu): tiles swap-AB {16, 32, 64} x 256
+// and 128 x 128; returns false / cudaErrorInvalidValue for others.
+bool fp8_variant_info(const TcVariant& v, TcVariantInfo* info);
+int fp8_launch(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
+               const GroupedParams& p, int grid, cudaStream_t stream);
+int fp8_maps_launch(const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out, const GroupedParams& p,
+                    cudaStream_t stream);
+
 // Launches simt_grouped_kernel<T>; returns a cudaError_t value.
 template <typename T>
 int simt_launch(const GroupedParams& p, int grid, cudaStream_t stream);

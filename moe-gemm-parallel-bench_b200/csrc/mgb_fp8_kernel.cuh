@@ -1,0 +1,461 @@
+// Grouped FP8 GEMM with DeepSeek-V3 block scales, sm_100a.
+//
+//   C_e[M, N] (bf16) = sum over 128-deep K blocks kb of
+//       (A_e[:, kb] @ B_e[:, kb]^T) * SA_e[m, kb] * SB_e[n / 128, kb]
+//
+// A_e: e4m3 [M, K] tokens, K contiguous; SA_e: fp32 [M, ceil(K/128)], one scale
+// per token and 128-deep K block (the dynamic 1 x 128 activation blocks).
+// B_e: e4m3 [N, K] as checkpoints store a linear weight (output x input
+// features, K contiguous); SB_e: fp32 [ceil(N/128), ceil(K/128)], one scale
+// per 128 x 128 weight block (quantization_config.weight_block_size of
+// model_configs/deepseek-v3.json).  fp32 accumulation, one cast to bf16.
+//
+// The scales are arbitrary fp32 values, not the power-of-two scales the
+// block-scaled MMA kinds take.  So every 128-deep K block is one group of four
+// tcgen05.mma.kind::f8f6f4 (K = 32 each, both operands K-major) into a TMEM
+// partial that starts from zero, and the epilogue warps "promote" it: read the
+// partial, multiply by its token and weight-block scales and add it into fp32
+// accumulators held in registers, while the MMA warp fills the other of two
+// partial buffers with the next K block.
+//
+// Roles (192 threads), as in tc_grouped_kernel:
+//   warp 0      TMA producer (per stage: TM token rows and TN weight rows of
+//               one 128-deep K block, 128 bytes per row, 128-byte swizzle)
+//   warp 1      TMEM allocator; lane 0 issues the MMAs
+//   warps 2..5  promotion and the output stores
+// Tiles: SWAP (narrow M): MMA M = 128 weight rows per chunk (TN / 128
+// chunks), MMA N = TM tokens; the lane owns a weight row, the registers hold
+// its TM token columns.  Row tiles: MMA M = 128 tokens, N = TN = 128 weight
+// rows (one scale block); the lane owns a token row and 128 columns.
+#pragma once
+
+#include "mgb_tc_kernel.cuh"
+
+namespace mgb {
+
+constexpr int kFp8Block = 128;  // scale block along K (and along N for the weights)
+
+template <bool SWAP, int TM, int TN>
+struct Fp8Cfg {
+  static constexpr int kBK = kFp8Block;  // K per stage: one 128-byte row, one scale block
+  static constexpr int kActBytes = TM * 128;
+  static constexpr int kWgtBytes = TN * 128;
+  static constexpr int kStageBytes = kActBytes + kWgtBytes;
+  static constexpr int kEpiBytes = SWAP ? 0 : kEpiBytesRowTile;
+  static constexpr int kStagesRaw = (kTcSmemBudget - kEpiBytes) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
+  static constexpr int kPartCols = SWAP ? (TN / 128) * TM : TN;  // TMEM columns of one partial
+  static constexpr int kTmemCols = pow2_at_least(2 * kPartCols);
+  // E4M3 x E4M3 (format code 0 for both operands), both K-major, fp32 D.
+  static constexpr uint32_t kIdesc = SWAP ? instr_desc(0, 0, 0, 128, TM) : instr_desc(0, 0, 0, TM, TN);
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 2048 + 1024;
+  static_assert(TN % 128 == 0 && TN <= 256, "weight tile: whole 128-row scale blocks, one TMA box");
+  static_assert(SWAP ? (TM % 16 == 0 && TM >= 16 && TM <= 64) : (TM == 128 && TN == 128), "token tile");
+  static_assert(kStages >= 3, "operand ring depth");
+  static_assert(2 * kPartCols <= 512, "two partials fit in TMEM");
+  static_assert(kSmemBytes <= 232448, "shared memory");
+};
+
+// A problem runs when TMA can address its operands: 16-byte aligned bases,
+// K a multiple of 16 (byte rows of A and B), N a multiple of 8 (bf16 C rows).
+__device__ __forceinline__ bool fp8_legal(const Problem& q) {
+  const uint64_t a = reinterpret_cast<uint64_t>(q.a), b = reinterpret_cast<uint64_t>(q.b),
+                 c = reinterpret_cast<uint64_t>(q.c);
+  return q.m > 0 && q.n > 0 && q.k >= 0 && a % 16 == 0 && b % 16 == 0 && c % 16 == 0 && q.k % 16 == 0 &&
+         q.n % 8 == 0 && q.m < (1ll << 31) && q.n < (1ll << 31) && q.k < (1ll << 31);
+}
+
+// Tensor maps of every problem of an FP8 launch (one warp per problem), and
+// in the extra block of a heterogeneous launch the walk's unit prefix sums.
+// A: u8 [M, K] rows of K bytes; B: u8 [N, K]; C: bf16 [M, N].
+__global__ void __launch_bounds__(32)
+    build_fp8_maps_kernel(const __grid_constant__ CUtensorMap act_tmpl, const __grid_constant__ CUtensorMap wgt_tmpl,
+                          const __grid_constant__ CUtensorMap out_tmpl, const GroupedParams p) {
+  __shared__ alignas(128) CUtensorMap staging[kMapsPerProblem];
+  const int e = blockIdx.x;
+  const int lane = threadIdx.x;
+  if (e == p.problem_count && p.unit_start != nullptr) {
+    write_unit_prefix(p, lane);
+    return;
+  }
+  if (e >= p.problem_count) return;
+  if (lane == 0) {
+    const Problem q = load_problem(p, e);
+    const CUtensorMap* tmpl[kMapsPerProblem] = {&act_tmpl, &wgt_tmpl, &out_tmpl};
+    for (int i = 0; i < kMapsPerProblem; ++i) {
+      const uint4* src = reinterpret_cast<const uint4*>(tmpl[i]);
+      uint4* dst = reinterpret_cast<uint4*>(&staging[i]);
+      for (int j = 0; j < 8; ++j) dst[j] = src[j];
+    }
+    if (fp8_legal(q)) {
+      tmap_replace_address(&staging[0], q.a);
+      tmap_replace_address(&staging[1], q.b);
+      tmap_replace_address(&staging[2], q.c);
+      if (!p.homogeneous) {
+        tmap_replace_dim(&staging[0], 0, static_cast<uint32_t>(q.k));
+        tmap_replace_dim(&staging[0], 1, static_cast<uint32_t>(q.m));
+        tmap_replace_stride1(&staging[0], static_cast<uint64_t>(q.k));
+        tmap_replace_dim(&staging[1], 0, static_cast<uint32_t>(q.k));
+        tmap_replace_dim(&staging[1], 1, static_cast<uint32_t>(q.n));
+        tmap_replace_stride1(&staging[1], static_cast<uint64_t>(q.k));
+        tmap_replace_dim(&staging[2], 0, static_cast<uint32_t>(q.n));
+        tmap_replace_dim(&staging[2], 1, static_cast<uint32_t>(q.m));
+        tmap_replace_stride1(&staging[2], static_cast<uint64_t>(q.n) * 2);
+      }
+    }
+  }
+  __syncwarp();
+  CUtensorMap* g = reinterpret_cast<CUtensorMap*>(p.desc_slots) + static_cast<int64_t>(kMapsPerProblem) * e;
+  for (int i = 0; i < kMapsPerProblem; ++i) tmap_publish(&g[i], &staging[i]);
+}
+
+// Row-tile output: 32 rows (one per lane) x 128 fp32 accumulators in
+// registers -> bf16, staged per 64-column chunk like store_rows_tma and
+// written with one tensor store each (TMA clips rows / columns past C).
+__device__ __forceinline__ void store_acc_rows_tma(const Problem& q, const void* cmap, const float (&acc)[128],
+                                                   int32_t row0, int32_t n0, uint8_t* blocks, int lane,
+                                                   uint32_t& seq, uint64_t policy, uint32_t* error_word) {
+  if (row0 >= q.m) return;
+#pragma unroll
+  for (int c = 0; c < 2; ++c) {
+    if (n0 + c * 64 >= q.n) break;
+    uint8_t* block = blocks + ((seq + static_cast<uint32_t>(c)) & 1u) * kEpiWarpBytes;
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+    uint8_t* my_row = block + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float* v = acc + c * 64 + 8 * j;
+      const uint4 packed = make_uint4(
+          pack_pair<__nv_bfloat16>(__float_as_uint(v[0]), __float_as_uint(v[1])),
+          pack_pair<__nv_bfloat16>(__float_as_uint(v[2]), __float_as_uint(v[3])),
+          pack_pair<__nv_bfloat16>(__float_as_uint(v[4]), __float_as_uint(v[5])),
+          pack_pair<__nv_bfloat16>(__float_as_uint(v[6]), __float_as_uint(v[7])));
+      *reinterpret_cast<uint4*>(my_row + ((j ^ (lane & 7)) << 4)) = packed;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      const int32_t x = n0 + c * 64;
+      if (x >= 0 && row0 >= 0 && x < q.n && row0 < q.m) {
+        tma_store_2d(cmap, block, x, row0, policy);
+        bulk_commit_group();
+      } else {
+        atomicOr(error_word, kErrBadStore);
+      }
+    }
+  }
+  const int chunks = q.n - n0 >= 128 ? 2 : static_cast<int>((q.n - n0 + 63) / 64);
+  seq += static_cast<uint32_t>(chunks);
+}
+
+template <bool SWAP, int TM, int TN>
+__global__ void __launch_bounds__(kTcThreads, 1)
+    fp8_grouped_kernel(const __grid_constant__ CUtensorMap act_tmpl, const __grid_constant__ CUtensorMap wgt_tmpl,
+                       const __grid_constant__ CUtensorMap out_tmpl, const GroupedParams p) {
+  using Cfg = Fp8Cfg<SWAP, TM, TN>;
+  constexpr int S = Cfg::kStages;
+  constexpr int BK = Cfg::kBK;
+  constexpr int kChunks = TN / 128;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint8_t* epi_stage = smem + S * Cfg::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + Cfg::kEpiBytes);
+  uint64_t* empty = full + S;
+  uint64_t* part_full = empty + S;       // [2] MMA commit: a partial is ready
+  uint64_t* part_empty = part_full + 2;  // [2] 4 epilogue warps: a partial was read
+  uint64_t* drain_bar = part_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* never = abort + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&part_full[b], 1);
+      mbar_init(&part_empty[b], 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort = 0;
+    *never = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const long long budget = p.wait_budget;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const CUtensorMap* act_map = &act_tmpl;
+    const CUtensorMap* wgt_map = &wgt_tmpl;
+    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_shared = policy_evict_normal();
+    const uint64_t pol_act = policy_evict_last();
+    TileWalk<TM, TN> walk;
+    uint32_t it = 0;
+    int built = -1;
+    bool ok = true;
+    for (int64_t t = 0; ok && walk.next_tile(p, blockIdx.x, gridDim.x, t);) {
+      const Problem& q = walk.prob;
+      if (!fp8_legal(q)) {
+        if (lane == 0 && walk.problem != built) atomicOr(p.error_word, kErrMisaligned);
+        continue;
+      }
+      const int64_t kblocks = (q.k + BK - 1) / BK;
+      const uint64_t pol_wgt = walk.m_blocks > 1 ? pol_shared : pol_stream;
+      const int32_t m0 = static_cast<int32_t>(walk.m_block(t) * TM);
+      const int32_t n0 = static_cast<int32_t>(walk.n_block(t) * TN);
+      for (int64_t kb = 0; kb < kblocks; ++kb) {
+        const int s = static_cast<int>(it % S);
+        if (!mbar_wait_warp(&empty[s], ((it / S) & 1u) ^ 1u, budget, abort)) {
+          if (lane == 0) raise_error(p, kErrWaitEmpty, abort);
+          ok = false;
+          break;
+        }
+        if (kb == 0 && walk.problem != built) {
+          const CUtensorMap* g = problem_maps(p, walk.problem);  // built by build_fp8_maps_kernel
+          if (lane == 0) {
+            tmap_acquire(&g[0]);
+            tmap_acquire(&g[1]);
+          }
+          __syncwarp();
+          act_map = &g[0];
+          wgt_map = &g[1];
+          built = walk.problem;
+        }
+        if (lane == 0) {
+          uint8_t* st_act = ring + s * Cfg::kStageBytes;
+          uint8_t* st_wgt = st_act + Cfg::kActBytes;
+          const int32_t kx = static_cast<int32_t>(kb * BK);
+          mbar_arrive_expect_tx(&full[s], Cfg::kStageBytes);
+          tma_load_2d(act_map, &full[s], st_act, kx, m0, pol_act);
+          tma_load_2d(wgt_map, &full[s], st_wgt, kx, n0, pol_wgt);
+        }
+        __syncwarp();
+        ++it;
+      }
+    }
+    if (*abort && lane == 0) {
+      const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0u;
+      for (uint32_t j = first; j < it; ++j) {
+        if (!mbar_wait(&full[j % S], (j / S) & 1u, budget, never)) {
+          atomicOr(p.error_word, kErrWaitTeardown);
+          break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // --------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      TileWalk<TM, TN> walk;
+      uint32_t it = 0;
+      uint32_t pit = 0;  // partials issued (all tiles)
+      bool ok = true;
+      for (int64_t t = 0; ok && walk.next_tile(p, blockIdx.x, gridDim.x, t);) {
+        const Problem& q = walk.prob;
+        if (!fp8_legal(q)) continue;
+        const int64_t kblocks = (q.k + BK - 1) / BK;
+        for (int64_t kb = 0; kb < kblocks; ++kb) {
+          const int s = static_cast<int>(it % S);
+          const int pb = static_cast<int>(pit & 1u);
+          if (!mbar_wait(&part_empty[pb], ((pit >> 1) & 1u) ^ 1u, budget, abort)) {
+            raise_error(p, kErrWaitAccEmpty, abort);
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&full[s], (it / S) & 1u, budget, abort)) {
+            raise_error(p, kErrWaitFull, abort);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(pb * Cfg::kPartCols);
+          const uint32_t a_base = smem_u32(ring + s * Cfg::kStageBytes);
+          const uint32_t w_base = a_base + Cfg::kActBytes;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint32_t acc = ks > 0 ? 1u : 0u;  // every partial starts from zero
+            const uint64_t act_desc = smem_desc(a_base + ks * 32, 16, 1024, kLayoutSw128);
+            if constexpr (SWAP) {
+#pragma unroll
+              for (int c = 0; c < kChunks; ++c) {
+                const uint64_t wgt_desc = smem_desc(w_base + c * 16384 + ks * 32, 16, 1024, kLayoutSw128);
+                mma_f8(d_tmem + c * TM, wgt_desc, act_desc, Cfg::kIdesc, acc);
+              }
+            } else {
+              const uint64_t wgt_desc = smem_desc(w_base + ks * 32, 16, 1024, kLayoutSw128);
+              mma_f8(d_tmem, act_desc, wgt_desc, Cfg::kIdesc, acc);
+            }
+          }
+          mma_commit(&empty[s]);
+          mma_commit(&part_full[pb]);
+          ++it;
+          ++pit;
+        }
+      }
+      if (*abort) {
+        mma_commit(drain_bar);
+        if (!mbar_wait(drain_bar, 0, budget, never)) atomicOr(p.error_word, kErrWaitTeardown);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------- promotion and the stores
+    const int quarter = warp & 3;
+    TileWalk<TM, TN> walk;
+    uint32_t pit = 0;
+    uint8_t* my_blocks = epi_stage + quarter * 2 * kEpiWarpBytes;
+    int c_built = -1;
+    const uint64_t pol_out = policy_evict_first();
+    uint32_t chunk_seq = 0;
+    bool ok = true;
+    for (int64_t t = 0; ok && walk.next_tile(p, blockIdx.x, gridDim.x, t);) {
+      const Problem& q = walk.prob;
+      if (!fp8_legal(q)) continue;
+      const int64_t kblocks = (q.k + BK - 1) / BK;
+      const int64_t m0 = walk.m_block(t) * TM;
+      const int64_t n0 = walk.n_block(t) * TN;
+      const float* sa = reinterpret_cast<const float*>(p.sa_ptrs[walk.problem]);
+      const float* sb = reinterpret_cast<const float*>(p.sb_ptrs[walk.problem]);
+      const void* cmap = nullptr;
+      if constexpr (!SWAP) cmap = out_map_for(p, out_tmpl, walk.problem, c_built, lane);
+      if constexpr (SWAP) {
+        // Lane l owns weight row n0 + 128 c + 32 quarter + l of each chunk c;
+        // acc[c][t] is its output for token m0 + t.
+        float acc[kChunks][TM];
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+#pragma unroll
+          for (int i = 0; i < TM; ++i) acc[c][i] = 0.0f;
+        }
+        const int64_t ta = m0 + lane, tb = m0 + lane + 32;  // tokens whose scales this lane fetches
+        auto fetch = [&](int64_t kb, float& s_a0, float& s_a1, float (&s_b)[kChunks]) {
+          s_a0 = (lane < TM && ta < q.m) ? sa[ta * kblocks + kb] : 0.0f;
+          s_a1 = (lane + 32 < TM && tb < q.m) ? sa[tb * kblocks + kb] : 0.0f;
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) {
+            const int64_t nblk = (n0 + c * 128) / kFp8Block;
+            s_b[c] = n0 + c * 128 < q.n ? sb[nblk * kblocks + kb] : 0.0f;
+          }
+        };
+        float na0 = 0.0f, na1 = 0.0f, nb[kChunks];
+        if (kblocks > 0) fetch(0, na0, na1, nb);
+        for (int64_t kb = 0; kb < kblocks; ++kb) {
+          const float ca0 = na0, ca1 = na1;
+          float cb[kChunks];
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) cb[c] = nb[c];
+          if (kb + 1 < kblocks) fetch(kb + 1, na0, na1, nb);  // next block's scales in flight
+          const int pb = static_cast<int>(pit & 1u);
+          if (!mbar_wait_warp(&part_full[pb], (pit >> 1) & 1u, budget, abort)) {
+            if (lane == 0) raise_error(p, kErrWaitAccFull, abort);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                 static_cast<uint32_t>(pb * Cfg::kPartCols);
+#pragma unroll
+          for (int c = 0; c < kChunks; ++c) {
+            uint32_t r[TM / 16][16];
+#pragma unroll
+            for (int j = 0; j < TM / 16; ++j) tmem_ld16(taddr + c * TM + j * 16, r[j]);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < TM; ++i) {
+              const float s_tok = i < 32 ? __shfl_sync(0xffffffffu, ca0, i) : __shfl_sync(0xffffffffu, ca1, i - 32);
+              acc[c][i] = fmaf(__uint_as_float(r[i / 16][i % 16]), s_tok * cb[c], acc[c][i]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&part_empty[pb]);
+          ++pit;
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+          const int64_t col = n0 + c * 128 + quarter * 32 + lane;
+          if (col < q.n) {
+#pragma unroll
+            for (int i = 0; i < TM; ++i) {
+              const int64_t row = m0 + i;
+              if (row < q.m) store_scalar<__nv_bfloat16>(q.c, row * q.n + col, acc[c][i]);
+            }
+          }
+        }
+      } else {
+        // Lane l owns token row m0 + 32 quarter + l and the tile's 128 columns.
+        float acc[128];
+#pragma unroll
+        for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+        const int64_t row = m0 + quarter * 32 + lane;
+        const int64_t nblk = n0 / kFp8Block;
+        auto fetch = [&](int64_t kb) -> float {
+          const float s_a = row < q.m ? sa[row * kblocks + kb] : 0.0f;
+          return s_a * sb[nblk * kblocks + kb];
+        };
+        float next = kblocks > 0 ? fetch(0) : 0.0f;
+        for (int64_t kb = 0; kb < kblocks; ++kb) {
+          const float f = next;
+          if (kb + 1 < kblocks) next = fetch(kb + 1);
+          const int pb = static_cast<int>(pit & 1u);
+          if (!mbar_wait_warp(&part_full[pb], (pit >> 1) & 1u, budget, abort)) {
+            if (lane == 0) raise_error(p, kErrWaitAccFull, abort);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                 static_cast<uint32_t>(pb * Cfg::kPartCols);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t r0[32], r1[32];
+            tmem_ld32(taddr + h * 64, r0);
+            tmem_ld32(taddr + h * 64 + 32, r1);
+            tmem_ld_wait();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              acc[h * 64 + i] = fmaf(__uint_as_float(r0[i]), f, acc[h * 64 + i]);
+              acc[h * 64 + 32 + i] = fmaf(__uint_as_float(r1[i]), f, acc[h * 64 + 32 + i]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&part_empty[pb]);
+          ++pit;
+        }
+        if (!ok) break;
+        if (cmap != nullptr) {
+          store_acc_rows_tma(q, cmap, acc, static_cast<int32_t>(m0 + quarter * 32), static_cast<int32_t>(n0),
+                             my_blocks, lane, chunk_seq, pol_out, p.error_word);
+        }
+      }
+    }
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+}  // namespace mgb

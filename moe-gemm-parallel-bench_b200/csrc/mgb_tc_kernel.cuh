@@ -438,6 +438,36 @@ __device__ __forceinline__ const void* out_map_for(const GroupedParams& p, const
   return g;
 }
 
+// The extra block of a heterogeneous launch's map builder (one warp):
+// unit_start[e] = units of problems [0, e) for the walk's tile shape and unit
+// size (empty or invalid problems have none), lane l summing a contiguous run
+// of problems, then a warp-wide exclusive scan.
+__device__ __forceinline__ void write_unit_prefix(const GroupedParams& p, int lane) {
+  const int per = (p.problem_count + 31) / 32;
+  const int lo = lane * per;
+  const int hi = lo + per < p.problem_count ? lo + per : p.problem_count;
+  const int64_t unit = p.unit_tiles > 0 ? p.unit_tiles : 1;
+  auto units_of = [&](int i) -> int64_t {
+    const Problem q = load_problem(p, i);
+    if (q.m <= 0 || q.n <= 0 || q.k < 0) return 0;
+    return ceil_div64(ceil_div64(q.m, p.walk_tm) * ceil_div64(q.n, p.walk_tn), unit);
+  };
+  int64_t sum = 0;
+  for (int i = lo; i < hi; ++i) sum += units_of(i);
+  int64_t incl = sum;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    const int64_t v = __shfl_up_sync(0xffffffffu, incl, d);
+    if (lane >= d) incl += v;
+  }
+  int64_t run = incl - sum;
+  for (int i = lo; i < hi; ++i) {
+    p.unit_start[i] = run;
+    run += units_of(i);
+  }
+  if (lane == 31) p.unit_start[p.problem_count] = incl;
+}
+
 // Builds the tensor maps of every problem of a grouped launch, one warp per
 // problem: lane 0 copies the three templates (box shape, swizzle and element
 // type final) into shared memory and rewrites the base addresses -- and, for
@@ -454,36 +484,7 @@ __global__ void __launch_bounds__(32)
   const int e = blockIdx.x;
   const int lane = threadIdx.x;
   if (e == p.problem_count && p.unit_start != nullptr) {
-    // The extra block of a heterogeneous launch: exclusive prefix sum of the
-    // walk's units per problem (the tile walk's rules: empty or invalid
-    // problems have none), lane l summing a contiguous run of problems.
-    const int per = (p.problem_count + 31) / 32;
-    const int lo = lane * per;
-    const int hi = lo + per < p.problem_count ? lo + per : p.problem_count;
-    const int64_t unit = p.unit_tiles > 0 ? p.unit_tiles : 1;
-    int64_t sum = 0;
-    for (int i = lo; i < hi; ++i) {
-      const Problem q = load_problem(p, i);
-      if (q.m > 0 && q.n > 0 && q.k >= 0) {
-        const int64_t tiles = ceil_div64(q.m, p.walk_tm) * ceil_div64(q.n, p.walk_tn);
-        sum += ceil_div64(tiles, unit);
-      }
-    }
-    int64_t incl = sum;
-#pragma unroll
-    for (int d = 1; d < 32; d <<= 1) {
-      const int64_t v = __shfl_up_sync(0xffffffffu, incl, d);
-      if (lane >= d) incl += v;
-    }
-    int64_t run = incl - sum;
-    for (int i = lo; i < hi; ++i) {
-      p.unit_start[i] = run;
-      const Problem q = load_problem(p, i);
-      if (q.m > 0 && q.n > 0 && q.k >= 0) {
-        run += ceil_div64(ceil_div64(q.m, p.walk_tm) * ceil_div64(q.n, p.walk_tn), unit);
-      }
-    }
-    if (lane == 31) p.unit_start[p.problem_count] = incl;
+    write_unit_prefix(p, lane);
     return;
   }
   if (e >= p.problem_count) return;

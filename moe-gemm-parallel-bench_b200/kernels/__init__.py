@@ -17,6 +17,14 @@ from .grouped_gemm import (
     launch_grouped,
     workspace_from_tensors,
 )
+from .fp8 import (
+    Fp8GroupedWorkspace,
+    build_fp8_workspace,
+    fp8_workspace_from_tensors,
+    launch_grouped_fp8,
+    quantize_activations,
+    quantize_weight,
+)
 from .matmul import (
     KernelConfig,
     last_matmul_config,
@@ -27,7 +35,13 @@ from .matmul import (
 )
 
 __all__ = [
+    "Fp8GroupedWorkspace",
     "GroupedWorkspace",
+    "build_fp8_workspace",
+    "fp8_workspace_from_tensors",
+    "launch_grouped_fp8",
+    "quantize_activations",
+    "quantize_weight",
     "KernelConfig",
     "build_fused_gate_up_workspace",
     "build_fused_swiglu_workspace",

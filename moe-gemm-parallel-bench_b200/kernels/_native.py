@@ -31,6 +31,7 @@ EXPORTED_SYMBOLS = (
     "grouped_gemm_launch",
     "grouped_gemm_swiglu_launch",
     "grouped_gemm_offsets_launch",
+    "grouped_gemm_fp8_launch",
     "grouped_gemm_launch_noalloc",
     "matmul_launch",
     "matrix_repack",
@@ -127,6 +128,12 @@ def _declare(lib) -> None:
         ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
     ]
     lib.grouped_gemm_offsets_launch.restype = ctypes.c_int
+    lib.grouped_gemm_fp8_launch.argtypes = [
+        c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(TileConfig), ctypes.c_void_p, ctypes.c_size_t,
+        ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
+    ]
+    lib.grouped_gemm_fp8_launch.restype = ctypes.c_int
     lib.matmul_launch.argtypes = [
         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
         ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
@@ -232,6 +239,21 @@ def offsets_launch(
         ctypes.byref(cfg), scratch, int(scratch_nbytes), stream, ctypes.byref(info),
     )
     _check(status, "grouped_gemm_offsets_launch")
+    return info
+
+
+def fp8_launch(
+    a_ptrs: int, b_ptrs: int, c_ptrs: int, sa_ptrs: int, sb_ptrs: int, dims: int, problem_count: int,
+    homogeneous: bool, m: int, n: int, k: int, config, scratch: int, scratch_nbytes: int, stream: int,
+) -> LaunchInfo:
+    """grouped_gemm_fp8_launch: e4m3 A [M, K] / B [N, K] with fp32 block scales, bf16 C."""
+    info = LaunchInfo()
+    cfg = tile_config(config)
+    status = load().grouped_gemm_fp8_launch(
+        a_ptrs, b_ptrs, c_ptrs, sa_ptrs, sb_ptrs, dims, int(problem_count), int(bool(homogeneous)), int(m), int(n),
+        int(k), ctypes.byref(cfg), scratch, int(scratch_nbytes), stream, ctypes.byref(info),
+    )
+    _check(status, "grouped_gemm_fp8_launch")
     return info
 
 

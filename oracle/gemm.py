@@ -89,6 +89,21 @@ def swiglu(a: np.ndarray, packed_b: np.ndarray, dtype: str) -> np.ndarray:
     return round_to_dtype(gate / (1.0 + np.exp(-gate)) * up, dtype)
 
 
+def fp8_block_scaled(a_q: np.ndarray, sa: np.ndarray, b_q: np.ndarray, sb: np.ndarray, block: int = 128) -> np.ndarray:
+    """FP8 block-scaled product, bf16 output: dequantize A (per row and
+    `block`-deep K block) and B [N, K] (per block x block tile), float64
+    C = A B^T, one rounding.  The quantization is DeepSeek-V3's
+    (model_configs/deepseek-v3.json:37-44), which the reference does not
+    emulate (README.md:298); a_q / b_q hold the e4m3 values as floats."""
+    a_q = np.asarray(a_q, np.float64)
+    b_q = np.asarray(b_q, np.float64)
+    m, k = a_q.shape
+    n = b_q.shape[0]
+    sa_full = np.repeat(np.asarray(sa, np.float64), block, axis=1)[:, :k]
+    sb_full = np.repeat(np.repeat(np.asarray(sb, np.float64), block, axis=0)[:n], block, axis=1)[:, :k]
+    return round_to_dtype((a_q * sa_full) @ (b_q * sb_full).T, "bf16")
+
+
 def exact_integer_outputs(shape: tuple[int, int, int], problems: int) -> list[np.ndarray]:
     """Known answer of tests/test_gpu.py:127-154: A = 1, B_e = e + 1 gives C_e = K * (e + 1)."""
     m, k, n = shape

@@ -577,6 +577,68 @@ def test_aggregate_layout_graph_replay_follows_device_offsets():
     del graph
 
 
+# ------------------------------------------------- FP8 block-scaled experts
+def _fp8_check(ws, rows=None):
+    from oracle import gemm as oracle
+
+    for a, sa, b, sb, c in ws.problem_tensors():
+        if rows is not None:
+            idx = rows(a.shape[0])
+            a, sa, c = a.index_select(0, idx), sa.index_select(0, idx), c.index_select(0, idx)
+        expected = oracle.fp8_block_scaled(_host(a), _host(sa), _host(b), _host(sb))
+        got = _host(c)
+        assert np.isfinite(got).all(), "output has non-finite values (unwritten)"
+        err = oracle.relative_frobenius(got, expected)
+        assert err <= REL_FRO["bf16"], f"relative Frobenius error {err:.3e}"
+        np.testing.assert_allclose(got, expected, rtol=ASSERT_CLOSE["bf16"], atol=ASSERT_CLOSE["bf16"])
+
+
+def test_fp8_block_scaled_every_tile_ragged_group():
+    """e4m3 A [M, K] / B [N, K] with DeepSeek-V3 block scales on every native
+    FP8 tile, over a heterogeneous group with partial K, N and M blocks."""
+    torch = _torch()
+    from kernels import KernelConfig, build_fp8_workspace, check_device_errors, launch_grouped_fp8
+
+    shapes = [(16, 256, 256), (40, 320, 200), (130, 128, 384), (1, 64, 136), (300, 512, 256)]
+    ws = build_fp8_workspace(shapes, seed=13)
+    assert not ws.homogeneous
+    for bm in (16, 32, 64, 128):
+        for c in ws.c:
+            c.fill_(float("nan"))
+        launch_grouped_fp8(ws, config=KernelConfig(bm, 256, 128, 4, 8, 4))
+        torch.cuda.synchronize()
+        check_device_errors()
+        assert ws.launch_info["path"] == "tcgen05_tma" and ws.launch_info["tile_m"] == bm, ws.launch_info
+        _fp8_check(ws)
+
+
+@pytest.mark.parametrize("m_e,k,n", [(16, 7168, 4096), (64, 2048, 7168), (128, 7168, 512), (1024, 256, 7168)])
+def test_fp8_block_scaled_deepseek_rank_shapes(m_e, k, n):
+    """DeepSeek-V3 W13 / W2 expert shapes (3 experts, the FP8 tile policy);
+    oracle on sampled rows."""
+    torch = _torch()
+    from kernels import build_fp8_workspace, check_device_errors, launch_grouped_fp8
+
+    ws = build_fp8_workspace([(m_e, k, n)] * 3, seed=m_e + k)
+    assert ws.homogeneous
+    launch_grouped_fp8(ws)
+    torch.cuda.synchronize()
+    check_device_errors()
+    rng = np.random.default_rng(k)
+    rows = lambda m: torch.as_tensor(np.unique(np.concatenate([[0, m - 1], rng.integers(0, m, 12)])), device="cuda")
+    _fp8_check(ws, rows=rows)
+
+
+def test_fp8_refuses_unaddressable_rows():
+    torch = _torch()
+    from kernels import build_fp8_workspace, launch_grouped_fp8
+    from kernels._native import NativeLaunchError
+
+    ws = build_fp8_workspace([(8, 24, 64)] * 2, seed=1)  # 24-byte rows: not TMA-addressable
+    with pytest.raises(NativeLaunchError, match="unsupported"):
+        launch_grouped_fp8(ws)
+
+
 def test_one_problem_group_dispatches_standard_matmul():
     """tests/test_gpu.py:190-195."""
     torch = _torch()

@@ -140,3 +140,24 @@ def test_native_tile_policy():
     assert native_candidates(256, 256) == (mm.TILE_PAIR_256x512,)
     assert native_candidates(512, 7168) == (mm.TILE_PAIR_256x512,)
     assert native_candidates(1024) == (mm.TILE_PAIR_256x512,)
+
+
+def test_fp8_quantization_round_trip_and_tiles():
+    """Block quantization helpers (CPU tensors): scales per token x 128-deep K
+    block and per 128 x 128 weight block; dequantized values within e4m3
+    precision; the tile policy by tokens per expert."""
+    torch = pytest.importorskip("torch")
+    from kernels import fp8
+
+    gen = torch.Generator().manual_seed(0)
+    x = torch.randn((5, 300), generator=gen)
+    q, s = fp8.quantize_activations(x)
+    assert q.dtype == torch.float8_e4m3fn and tuple(s.shape) == (5, 3)
+    back = fp8.dequantize_activations(q, s)
+    assert float((back - x).norm() / x.norm()) < 0.05
+    w = torch.randn((200, 300), generator=gen)
+    qw, sw = fp8.quantize_weight(w)
+    assert tuple(sw.shape) == (2, 3)
+    assert float((fp8.dequantize_weight(qw, sw) - w).norm() / w.norm()) < 0.05
+    assert fp8.fp8_tile_for(16).block_m == 16 and fp8.fp8_tile_for(40).block_m == 64
+    assert fp8.fp8_tile_for(1024).block_m == 128

@@ -134,3 +134,20 @@ def test_swiglu_known_answer():
     # silu(0) = 0 whatever up is; large negative gates vanish
     assert np.all(oracle.swiglu(np.zeros((2, 3)), np.ones((3, 4)), "bf16") == 0)
     assert abs(oracle.swiglu(np.full((1, 1), -50.0), np.ones((1, 2)), "fp32")[0, 0]) < 1e-15
+
+
+def test_fp8_block_scaled_oracle_is_dequantized_product():
+    rng = np.random.default_rng(5)
+    m, k, n = 3, 200, 130  # partial K and N blocks
+    a_q = rng.integers(-8, 8, (m, k)).astype(float)
+    b_q = rng.integers(-8, 8, (n, k)).astype(float)
+    sa = rng.uniform(0.5, 2.0, (m, 2))
+    sb = rng.uniform(0.5, 2.0, (2, 2))
+    got = oracle.fp8_block_scaled(a_q, sa, b_q, sb)
+    a = a_q * np.concatenate([np.repeat(sa[:, :1], 128, 1), np.repeat(sa[:, 1:], k - 128, 1)], axis=1)
+    b = b_q.copy()
+    for i in range(2):
+        for j in range(2):
+            b[i * 128:(i + 1) * 128, j * 128:(j + 1) * 128] *= sb[i, j]
+    expected = oracle.round_to_dtype(a @ b.T, "bf16")
+    np.testing.assert_array_equal(got, expected)
