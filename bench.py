@@ -70,6 +70,8 @@ def parse_args(argv=None):
     p.add_argument("--layout", choices=("tables", "aggregate"), default="tables",
                    help="W1: per-expert pointer tables (the reference's workspaces) or the expert-sorted "
                         "aggregate layout (launch_grouped_mm: A [E*M_e, K], B [E, K, N], int32 offsets)")
+    p.add_argument("--fp8", action="store_true",
+                   help="W1: e4m3 experts with DeepSeek-V3 block scales (grouped_gemm_fp8_launch, bf16 output)")
     p.add_argument("--fused-swiglu", action="store_true",
                    help="W1 only: launch with the fused SwiGLU epilogue (C = silu(gate) * up, [M_e, F_local])")
     p.add_argument("--cache-mode", choices=("hot", "cold"), default="hot",
@@ -121,15 +123,29 @@ def step_shapes(m_values, projection: str = "W1") -> list[tuple[str, int, tuple[
     return out
 
 
+def fp8_launch_bytes(m: int, k: int, n: int) -> int:
+    """One read of e4m3 A and B, their fp32 block scales, one bf16 write of C."""
+    kb, nb = -(-k // 128), -(-n // 128)
+    return m * k + n * k + 4 * (m * kb + nb * kb) + 2 * m * n
+
+
 def roofline_ms(m: int, k: int, n: int, count: int, peaks: dict, sustained: bool = True,
-                out_cols: int | None = None) -> tuple[float, str]:
+                out_cols: int | None = None, fp8: bool = False) -> tuple[float, str]:
     """Roofline time of one launch; `out_cols` is C's width when it is not N
-    (the fused SwiGLU epilogue writes N/2 columns)."""
+    (the fused SwiGLU epilogue writes N/2 columns).  FP8 launches count their
+    e4m3 / scale / bf16 bytes and twice the bf16 tensor peak (the dense e4m3
+    rate of the tensor cores is twice the bf16 one)."""
     from moe_parallel import gemm_flops, ideal_bytes
 
     flops = gemm_flops(m, k, n) * count
-    nbytes = ideal_bytes(m, k, n, 2) * count if out_cols is None else 2 * (m * k + k * n + m * out_cols) * count
-    tc = flops / ((peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]) * 1e12) * 1e3
+    if fp8:
+        nbytes = fp8_launch_bytes(m, k, n) * count
+    elif out_cols is None:
+        nbytes = ideal_bytes(m, k, n, 2) * count
+    else:
+        nbytes = 2 * (m * k + k * n + m * out_cols) * count
+    peak = peaks["bf16_tflops_sustained"] if sustained else peaks["bf16_tflops"]
+    tc = flops / ((2 * peak if fp8 else peak) * 1e12) * 1e3
     hbm = nbytes / (peaks["hbm_gbs"] * 1e9) * 1e3
     return (tc, "tensor") if tc >= hbm else (hbm, "hbm")
 
@@ -428,6 +444,79 @@ def build_rank_aggregate(rank: int, m_values, device, parallel=("EP", "TP"), exp
     return ep, tp, activations, outputs, launches
 
 
+def build_rank_fp8(rank: int, m_values, device, parallel=("EP", "TP"), expert_limit=None):
+    """W13 rank tensors quantized to e4m3 with DeepSeek-V3 block scales: each
+    expert's packed weight (the EP weight or the TP [gate_r | up_r] slice) is
+    stored [N, K] and quantized per 128 x 128 block; the activations per token
+    and 128-deep K block.  Outputs are bf16 [M_e, N]."""
+    import torch
+
+    from kernels import fp8_workspace_from_tensors, quantize_activations, quantize_weight
+    from moe_parallel import rank_plan, shard_weight
+
+    ep = rank_plan("W1", "EP", rank, PARALLEL, EXPERTS, FFN, HIDDEN)
+    tp = rank_plan("W1", "TP", rank, PARALLEL, EXPERTS, FFN, HIDDEN)
+    ep_experts = ep.experts[:expert_limit] if expert_limit else ep.experts
+    tp_experts = tp.experts[:expert_limit] if expert_limit else tp.experts
+    weights = {"EP": {}, "TP": {}}
+    for e in range(EXPERTS):
+        use_ep, use_tp = e in ep_experts and "EP" in parallel, e in tp_experts and "TP" in parallel
+        if not (use_ep or use_tp):
+            continue
+        w = expert_weight(e, device)
+        if use_ep:
+            weights["EP"][e] = quantize_weight(w.t())
+        if use_tp:
+            weights["TP"][e] = quantize_weight(shard_weight(w, tp).t())
+        del w
+    activations, outputs, workspaces = {}, {}, []
+    for m in m_values:
+        gen = torch.Generator(device=device).manual_seed(7919 * m)
+        a_all = torch.randn((EXPERTS, m, HIDDEN), device=device, generator=gen).to(torch.bfloat16)
+        qa, sa = quantize_activations(a_all.view(-1, HIDDEN))
+        qa, sa = qa.view(EXPERTS, m, HIDDEN), sa.view(EXPERTS, m, -1)
+        activations[m] = [qa, sa]
+        c_ep = torch.empty((len(ep_experts), m, 2 * FFN), device=device, dtype=torch.bfloat16)
+        c_tp = torch.empty((len(tp_experts), m, 2 * tp.local_ffn), device=device, dtype=torch.bfloat16)
+        outputs[m] = (c_ep, c_tp)
+        for par, experts, c in (("EP", ep_experts, c_ep), ("TP", tp_experts, c_tp)):
+            if par not in parallel:
+                continue
+            ws = fp8_workspace_from_tensors([qa[e] for e in experts], [weights[par][e][0] for e in experts],
+                                            [sa[e] for e in experts], [weights[par][e][1] for e in experts], list(c))
+            workspaces.append((par, m, ws))
+    return ep, tp, activations, outputs, workspaces
+
+
+def verify_fp8_outputs(world, workspaces, m_values, device) -> dict:
+    """After timing: every rank checks sampled experts and rows of its FP8
+    launches against the float64 product of the dequantized operands; the
+    worst relative error is max-reduced over the ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from kernels.fp8 import dequantize_activations, dequantize_weight
+
+    worst = 0.0
+    checks = {m_values[0], m_values[-1]}
+    for par, m, ws in workspaces:
+        if m not in checks:
+            continue
+        for e in sorted({0, ws.problem_count - 1}):
+            rows = torch.tensor(sorted({0, m // 2, m - 1}), device=device)
+            a = dequantize_activations(ws.a[e].index_select(0, rows), ws.sa[e].index_select(0, rows)).double()
+            b = dequantize_weight(ws.b[e], ws.sb[e]).double()
+            ref = a @ b.t()
+            got = ws.c[e].index_select(0, rows).double()
+            worst = max(worst, float((got - ref).norm() / ref.norm()))
+    t = torch.tensor([worst], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    worst = float(t.item())
+    return {"checked_m": sorted(checks), "max_rel_frobenius": worst, "passed": worst <= 1e-2,
+            "reference": "float64 product of the dequantized e4m3 operands"}
+
+
 FIXED_CONFIG = None  # set by --config: launches use it instead of the autotuned winner
 CLASS_CONFIGS: dict[str, object] = {}  # set by --config-small / --config-large
 
@@ -438,6 +527,10 @@ def launch(ws) -> None:
     fixed = FIXED_CONFIG or CLASS_CONFIGS.get(ws.max_m) or CLASS_CONFIGS.get("small" if ws.max_m <= 128 else "large")
     if isinstance(ws, AggregateLaunch):
         ws.run(fixed)
+    elif getattr(ws, "operation", "") == "fp8_block_scaled":
+        from kernels import launch_grouped_fp8
+
+        launch_grouped_fp8(ws, config=fixed)
     elif fixed is None:
         launch_grouped(ws)
     else:
@@ -713,7 +806,13 @@ def main(argv=None) -> int:
         raise SystemExit("--fused-swiglu applies to the W1 (packed gate+up) projection")
     if args.layout == "aggregate" and (args.projection != "W1" or args.cache_mode != "hot"):
         raise SystemExit("--layout aggregate measures the hot W1 step")
-    if args.layout == "aggregate":
+    if args.fp8 and (args.projection != "W1" or args.layout != "tables" or args.fused_swiglu or
+                     args.cache_mode != "hot"):
+        raise SystemExit("--fp8 measures the hot W1 step with per-expert tables")
+    if args.fp8:
+        ep, tp, activations, outputs, workspaces = build_rank_fp8(rank, m_values, device, parallel,
+                                                                  args.expert_limit)
+    elif args.layout == "aggregate":
         ep, tp, activations, outputs, workspaces = build_rank_aggregate(rank, m_values, device, parallel,
                                                                         args.expert_limit, swiglu=args.fused_swiglu)
     elif args.projection == "W1":
@@ -790,7 +889,8 @@ def main(argv=None) -> int:
     for (par, m), times in per_launch.items():
         (mm, k, n), count = shapes[(par, m)]
         ms = statistics.median(times)
-        roof, bound = roofline_ms(mm, k, n, count, peaks, out_cols=n // 2 if args.fused_swiglu else None)
+        roof, bound = roofline_ms(mm, k, n, count, peaks, out_cols=n // 2 if args.fused_swiglu else None,
+                                  fp8=args.fp8)
         per_shape.append({"parallel": par, "M_e": m, "experts": count, "ms": round(ms, 4),
                           "tflops": round(gemm_flops(mm, k, n) * count / ms / 1e9, 1),
                           "roofline_frac": round(roof / ms, 3), "bound": bound})
@@ -798,20 +898,26 @@ def main(argv=None) -> int:
     dominant = max(per_shape, key=lambda r: r["ms"])
     (dm, dk, dn), dcount = shapes[(dominant["parallel"], dominant["M_e"])]
     d_flops = gemm_flops(dm, dk, dn) * dcount
-    d_bytes = 2 * (dm * dk + dk * dn + dm * (dn // 2 if args.fused_swiglu else dn)) * dcount
+    if args.fp8:
+        d_bytes = fp8_launch_bytes(dm, dk, dn) * dcount
+    else:
+        d_bytes = 2 * (dm * dk + dk * dn + dm * (dn // 2 if args.fused_swiglu else dn)) * dcount
     if dominant["bound"] == "tensor":
         achieved = d_flops / (dominant["ms"] * 1e-3) / 1e12
-        roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": peaks["bf16_tflops_sustained"],
-                    "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops_sustained"], 3)}
+        tc_peak = peaks["bf16_tflops_sustained"] * (2 if args.fp8 else 1)
+        roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": tc_peak,
+                    "unit": "TFLOP/s", "frac": round(achieved / tc_peak, 3)}
     else:
         achieved = d_bytes / (dominant["ms"] * 1e-3) / 1e9
         roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                     "frac": round(achieved / peaks["hbm_gbs"], 3)}
     roofline.update({"kernel": f"{'W13' if args.projection == 'W1' else 'W2'} {dominant['parallel']} M_e={dominant['M_e']}",
                      "time_share": round(dominant["ms"] / total_ms, 3), "peak_source": peak_source,
-                     "traffic": None if args.fused_swiglu else traffic_from_profiles(dominant, args.projection)})
+                     "traffic": None if (args.fused_swiglu or args.fp8 or args.layout != "tables")
+                     else traffic_from_profiles(dominant, args.projection)})
     step_roof_ms = sum(roofline_ms(*shapes[key][0], shapes[key][1], peaks,
-                                   out_cols=shapes[key][0][2] // 2 if args.fused_swiglu else None)[0] for key in shapes)
+                                   out_cols=shapes[key][0][2] // 2 if args.fused_swiglu else None,
+                                   fp8=args.fp8)[0] for key in shapes)
 
     # End to end through the public API with host buffers: per step, the
     # step's activations go host -> device from pinned memory, every launch
@@ -865,7 +971,9 @@ def main(argv=None) -> int:
     check_device_errors(local_rank)
 
     progress("verification")
-    if parallel == ("EP", "TP") and not args.expert_limit and args.projection == "W2":
+    if args.fp8:
+        verification = verify_fp8_outputs(world, workspaces, m_values, device)
+    elif parallel == ("EP", "TP") and not args.expert_limit and args.projection == "W2":
         verification = verify_w2_outputs(rank, world, ep, tp, outputs, device, m_values)
     elif parallel == ("EP", "TP") and not args.expert_limit:
         verification = verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_values,
@@ -890,11 +998,13 @@ def main(argv=None) -> int:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": "e4m3" if args.fp8 else "bf16", "data": "synthetic",
             "config": {"workload": (WORKLOAD if args.projection == "W1" else WORKLOAD_W2)
                        + ("; fused SwiGLU epilogue: C = silu(gate) * up, [M_e, F_local]" if args.fused_swiglu else "")
                        + ("; expert-sorted aggregate layout (launch_grouped_mm, int32 offsets)"
-                          if args.layout == "aggregate" else ""),
+                          if args.layout == "aggregate" else "")
+                       + ("; e4m3 experts with DeepSeek-V3 block scales (128x128 weight, 1x128 token), "
+                          "bf16 output; tensor peak = 2x the measured bf16 one" if args.fp8 else ""),
                        "parallelism": f"GPU r runs rank r of P=8 (EP and TP), {world} rank(s)",
                        "cache": ("hot; inputs larger than L2 (0.94-1.88 GB of weights per projection), no flush"
                                  if args.cache_mode == "hot" else

@@ -28,7 +28,7 @@ static int launch_fp8_variant(const CUtensorMap& act, const CUtensorMap& wgt, co
     if (e != cudaSuccess) return static_cast<int>(e);
     configured[dev] = true;
   }
-  fp8_grouped_kernel<SWAP, TM, TN><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(act, wgt, out, p);
+  fp8_grouped_kernel<SWAP, TM, TN><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(act, wgt, out, p);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -18,15 +18,17 @@
 // accumulators held in registers, while the MMA warp fills the other of two
 // partial buffers with the next K block.
 //
-// Roles (192 threads), as in tc_grouped_kernel:
+// Roles, as in tc_grouped_kernel:
 //   warp 0      TMA producer (per stage: TM token rows and TN weight rows of
 //               one 128-deep K block, 128 bytes per row, 128-byte swizzle)
 //   warp 1      TMEM allocator; lane 0 issues the MMAs
-//   warps 2..5  promotion and the output stores
+//   warps 2..   promotion and the output stores (4 warps for swap-AB tiles,
+//               8 for row tiles: warp w reads TMEM lanes 32 (w % 4) .. + 31)
 // Tiles: SWAP (narrow M): MMA M = 128 weight rows per chunk (TN / 128
 // chunks), MMA N = TM tokens; the lane owns a weight row, the registers hold
 // its TM token columns.  Row tiles: MMA M = 128 tokens, N = TN = 128 weight
-// rows (one scale block); the lane owns a token row and 128 columns.
+// rows (one scale block); eight promotion warps, two per TMEM lane quarter,
+// each own a token row per lane and 64 of the 128 columns.
 #pragma once
 
 #include "mgb_tc_kernel.cuh"
@@ -41,7 +43,17 @@ struct Fp8Cfg {
   static constexpr int kActBytes = TM * 128;
   static constexpr int kWgtBytes = TN * 128;
   static constexpr int kStageBytes = kActBytes + kWgtBytes;
-  static constexpr int kEpiBytes = SWAP ? 0 : kEpiBytesRowTile;
+  // Row tiles promote with 8 warps (two per TMEM lane quarter, 64 columns
+  // each): the promotion's FMAs are issued from every sub-partition twice
+  // over, which keeps up with the MMA; swap-AB tiles need 4.
+  // (10 warps put three on two sub-partitions, whose 16K registers then cap a
+  // thread at 168: enough for 64 accumulators, not for the 128 a 128 x 256
+  // row tile would need.)
+  static constexpr int kEpiWarps = SWAP ? 4 : 8;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kWarpCols = SWAP ? 0 : TN / 2;  // row tiles: columns one promotion warp owns
+  static constexpr int kBlocksPerWarp = 2;              // output staging blocks per warp
+  static constexpr int kEpiBytes = SWAP ? 0 : kEpiWarps * kBlocksPerWarp * kEpiWarpBytes;
   static constexpr int kStagesRaw = (kTcSmemBudget - kEpiBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
   static constexpr int kPartCols = SWAP ? (TN / 128) * TM : TN;  // TMEM columns of one partial
@@ -109,48 +121,49 @@ __global__ void __launch_bounds__(32)
   for (int i = 0; i < kMapsPerProblem; ++i) tmap_publish(&g[i], &staging[i]);
 }
 
-// Row-tile output: 32 rows (one per lane) x 128 fp32 accumulators in
-// registers -> bf16, staged per 64-column chunk like store_rows_tma and
-// written with one tensor store each (TMA clips rows / columns past C).
-__device__ __forceinline__ void store_acc_rows_tma(const Problem& q, const void* cmap, const float (&acc)[128],
-                                                   int32_t row0, int32_t n0, uint8_t* blocks, int lane,
+// Row-tile output of one warp: 32 rows (one per lane) x 64 fp32
+// accumulators in registers -> bf16, staged like store_rows_tma (in one of the
+// warp's kBlocks 4 KB blocks) and written with one tensor store (TMA clips
+// rows / columns past C).
+template <int kBlocks, int OFF, int W>
+__device__ __forceinline__ void store_acc_rows_tma(const Problem& q, const void* cmap, const float (&acc)[W],
+                                                   int32_t row0, int32_t x0, uint8_t* blocks, int lane,
                                                    uint32_t& seq, uint64_t policy, uint32_t* error_word) {
-  if (row0 >= q.m) return;
-#pragma unroll
-  for (int c = 0; c < 2; ++c) {
-    if (n0 + c * 64 >= q.n) break;
-    uint8_t* block = blocks + ((seq + static_cast<uint32_t>(c)) & 1u) * kEpiWarpBytes;
-    if (lane == 0) bulk_wait_group_read<1>();
-    __syncwarp();
-    uint8_t* my_row = block + lane * 128;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const float* v = acc + c * 64 + 8 * j;
-      const uint4 packed = make_uint4(
-          pack_pair<__nv_bfloat16>(__float_as_uint(v[0]), __float_as_uint(v[1])),
-          pack_pair<__nv_bfloat16>(__float_as_uint(v[2]), __float_as_uint(v[3])),
-          pack_pair<__nv_bfloat16>(__float_as_uint(v[4]), __float_as_uint(v[5])),
-          pack_pair<__nv_bfloat16>(__float_as_uint(v[6]), __float_as_uint(v[7])));
-      *reinterpret_cast<uint4*>(my_row + ((j ^ (lane & 7)) << 4)) = packed;
-    }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      const int32_t x = n0 + c * 64;
-      if (x >= 0 && row0 >= 0 && x < q.n && row0 < q.m) {
-        tma_store_2d(cmap, block, x, row0, policy);
-        bulk_commit_group();
-      } else {
-        atomicOr(error_word, kErrBadStore);
-      }
+  if (row0 >= q.m || x0 >= q.n) return;
+  uint8_t* block = blocks + (kBlocks == 2 ? (seq & 1u) * kEpiWarpBytes : 0u);
+  if (lane == 0) {
+    if constexpr (kBlocks == 2) {
+      bulk_wait_group_read<1>();  // the store issued from `block` two chunks ago has read it
+    } else {
+      bulk_wait_group_read<0>();  // the previous store from the single block has read it
     }
   }
-  const int chunks = q.n - n0 >= 128 ? 2 : static_cast<int>((q.n - n0 + 63) / 64);
-  seq += static_cast<uint32_t>(chunks);
+  __syncwarp();
+  uint8_t* my_row = block + lane * 128;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int o = OFF + 8 * j;  // compile-time after unrolling: acc stays in registers
+    const uint4 packed = make_uint4(pack_pair<__nv_bfloat16>(__float_as_uint(acc[o]), __float_as_uint(acc[o + 1])),
+                                    pack_pair<__nv_bfloat16>(__float_as_uint(acc[o + 2]), __float_as_uint(acc[o + 3])),
+                                    pack_pair<__nv_bfloat16>(__float_as_uint(acc[o + 4]), __float_as_uint(acc[o + 5])),
+                                    pack_pair<__nv_bfloat16>(__float_as_uint(acc[o + 6]), __float_as_uint(acc[o + 7])));
+    *reinterpret_cast<uint4*>(my_row + ((j ^ (lane & 7)) << 4)) = packed;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    if (x0 >= 0 && row0 >= 0) {
+      tma_store_2d(cmap, block, x0, row0, policy);
+      bulk_commit_group();
+    } else {
+      atomicOr(error_word, kErrBadStore);
+    }
+  }
+  seq += 1;
 }
 
 template <bool SWAP, int TM, int TN>
-__global__ void __launch_bounds__(kTcThreads, 1)
+__global__ void __launch_bounds__(Fp8Cfg<SWAP, TM, TN>::kThreads, 1)
     fp8_grouped_kernel(const __grid_constant__ CUtensorMap act_tmpl, const __grid_constant__ CUtensorMap wgt_tmpl,
                        const __grid_constant__ CUtensorMap out_tmpl, const GroupedParams p) {
   using Cfg = Fp8Cfg<SWAP, TM, TN>;
@@ -165,7 +178,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + Cfg::kEpiBytes);
   uint64_t* empty = full + S;
   uint64_t* part_full = empty + S;       // [2] MMA commit: a partial is ready
-  uint64_t* part_empty = part_full + 2;  // [2] 4 epilogue warps: a partial was read
+  uint64_t* part_empty = part_full + 2;  // [2] every epilogue warp: a partial was read
   uint64_t* drain_bar = part_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -181,7 +194,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&part_full[b], 1);
-      mbar_init(&part_empty[b], 4);
+      mbar_init(&part_empty[b], Cfg::kEpiWarps);
     }
     mbar_init(drain_bar, 1);
     *abort = 0;
@@ -316,9 +329,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   } else {
     // ------------------------------------------- promotion and the stores
     const int quarter = warp & 3;
+    const int ew = warp - 2;                 // epilogue warp index
+    const int half = SWAP ? 0 : ew / 4;      // row tiles: columns [TN/2 half, TN/2 half + TN/2)
     TileWalk<TM, TN> walk;
     uint32_t pit = 0;
-    uint8_t* my_blocks = epi_stage + quarter * 2 * kEpiWarpBytes;
+    uint8_t* my_blocks = epi_stage + ew * Cfg::kBlocksPerWarp * kEpiWarpBytes;
     int c_built = -1;
     const uint64_t pol_out = policy_evict_first();
     uint32_t chunk_seq = 0;
@@ -399,12 +414,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
         }
       } else {
-        // Lane l owns token row m0 + 32 quarter + l and the tile's 128 columns.
-        float acc[128];
+        // Lane l owns token row m0 + 32 quarter + l and columns
+        // [W half, W half + W) of the tile (W = TN / 2, inside one scale block).
+        constexpr int W = Cfg::kWarpCols;
+        float acc[W];
 #pragma unroll
-        for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+        for (int i = 0; i < W; ++i) acc[i] = 0.0f;
         const int64_t row = m0 + quarter * 32 + lane;
-        const int64_t nblk = n0 / kFp8Block;
+        const int64_t nblk = (n0 + half * W) / kFp8Block;
         auto fetch = [&](int64_t kb) -> float {
           const float s_a = row < q.m ? sa[row * kblocks + kb] : 0.0f;
           return s_a * sb[nblk * kblocks + kb];
@@ -421,17 +438,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           }
           tc_fence_after();
           const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
-                                 static_cast<uint32_t>(pb * Cfg::kPartCols);
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
+                                 static_cast<uint32_t>(pb * Cfg::kPartCols + half * W);
+          if constexpr (W == 64) {
             uint32_t r0[32], r1[32];
-            tmem_ld32(taddr + h * 64, r0);
-            tmem_ld32(taddr + h * 64 + 32, r1);
+            tmem_ld32(taddr, r0);
+            tmem_ld32(taddr + 32, r1);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) {
-              acc[h * 64 + i] = fmaf(__uint_as_float(r0[i]), f, acc[h * 64 + i]);
-              acc[h * 64 + 32 + i] = fmaf(__uint_as_float(r1[i]), f, acc[h * 64 + 32 + i]);
+              acc[i] = fmaf(__uint_as_float(r0[i]), f, acc[i]);
+              acc[32 + i] = fmaf(__uint_as_float(r1[i]), f, acc[32 + i]);
+            }
+          } else {
+            // 128 accumulators per lane: one 32-column load in flight at a time.
+#pragma unroll
+            for (int h = 0; h < W / 32; ++h) {
+              uint32_t r[32];
+              tmem_ld32(taddr + h * 32, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; ++i) acc[h * 32 + i] = fmaf(__uint_as_float(r[i]), f, acc[h * 32 + i]);
             }
           }
           tc_fence_before();
@@ -441,8 +467,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         if (!ok) break;
         if (cmap != nullptr) {
-          store_acc_rows_tma(q, cmap, acc, static_cast<int32_t>(m0 + quarter * 32), static_cast<int32_t>(n0),
-                             my_blocks, lane, chunk_seq, pol_out, p.error_word);
+          const int32_t row0 = static_cast<int32_t>(m0 + quarter * 32);
+          const int32_t x0 = static_cast<int32_t>(n0 + half * W);
+          store_acc_rows_tma<Cfg::kBlocksPerWarp, 0>(q, cmap, acc, row0, x0, my_blocks, lane, chunk_seq, pol_out,
+                                                     p.error_word);
+          if constexpr (W == 128) {
+            store_acc_rows_tma<Cfg::kBlocksPerWarp, 64>(q, cmap, acc, row0, x0 + 64, my_blocks, lane, chunk_seq,
+                                                        pol_out, p.error_word);
+          }
         }
       }
     }

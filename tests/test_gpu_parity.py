@@ -602,13 +602,14 @@ def test_fp8_block_scaled_every_tile_ragged_group():
     shapes = [(16, 256, 256), (40, 320, 200), (130, 128, 384), (1, 64, 136), (300, 512, 256)]
     ws = build_fp8_workspace(shapes, seed=13)
     assert not ws.homogeneous
-    for bm in (16, 32, 64, 128):
+    for bm, bn in ((16, 256), (32, 256), (64, 256), (128, 128)):
         for c in ws.c:
             c.fill_(float("nan"))
-        launch_grouped_fp8(ws, config=KernelConfig(bm, 256, 128, 4, 8, 4))
+        launch_grouped_fp8(ws, config=KernelConfig(bm, bn, 128, 4, 8, 4))
         torch.cuda.synchronize()
         check_device_errors()
         assert ws.launch_info["path"] == "tcgen05_tma" and ws.launch_info["tile_m"] == bm, ws.launch_info
+        assert ws.launch_info["tile_n"] == bn, ws.launch_info
         _fp8_check(ws)
 
 
