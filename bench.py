@@ -88,6 +88,9 @@ def parse_args(argv=None):
                    help="per-M_e configs, e.g. '16:16,256;128:128,256;1024:256,128' (overrides autotuning)")
     p.add_argument("--expert-limit", type=int, default=None,
                    help="at most this many experts per workspace (smaller cases for ncu captures)")
+    p.add_argument("--moe-layer", action="store_true",
+                   help="time the whole expert-parallel MoE layer (route, dispatch, W13 SwiGLU, W2, combine)")
+    p.add_argument("--layer-tokens", type=int, default=4096, help="tokens per rank for --moe-layer")
     p.add_argument("--tile-sweep", action="store_true",
                    help="time every native tile per shape, alone and right after a heavy launch (diagnosis)")
     return p.parse_args(argv)
@@ -760,6 +763,176 @@ def tile_sweep(args, device) -> None:
 
 
 # ------------------------------------------------------------- main
+LAYER_WORKLOAD = ("DeepSeek-V3 MoE expert layer bf16 (H=7168, F=2048, E=256 experts split over the ranks, top-8): "
+                  "per rank T tokens routed uniformly at random; one step = route + count exchange + dispatch "
+                  "(peer stores) + W13 grouped GEMM with fused SwiGLU + W2 grouped GEMM + weighted combine "
+                  "(peer loads)")
+
+
+def layer_reference(x, ids, weights, device):
+    """fp32 reference of the layer for a few tokens from regenerated global
+    expert weights (bf16 intermediates as the layer stores them)."""
+    import torch
+
+    out = torch.zeros((x.shape[0], HIDDEN), dtype=torch.float32, device=device)
+    for t in range(x.shape[0]):
+        for j in range(ids.shape[1]):
+            e = int(ids[t, j])
+            w13 = expert_weight(e, device).float()
+            w2 = expert_down_weight(e, device).float()
+            xt = x[t:t + 1].float()
+            gate, up = xt @ w13[:, :FFN], xt @ w13[:, FFN:]
+            h = (torch.nn.functional.silu(gate) * up).to(torch.bfloat16).float()
+            out[t] += float(weights[t, j]) * (h @ w2).to(torch.bfloat16).float()[0]
+    return out.to(torch.bfloat16).float()
+
+
+def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> None:
+    """--moe-layer: the whole EP layer per step, one JSON line on rank 0."""
+    import torch
+    import torch.distributed as dist
+
+    from expert_parallel import ExpertParallelMoE
+    from kernels import check_device_errors
+
+    peaks, peak_source = load_peaks()
+    tokens, top_k = args.layer_tokens, TOPK
+    local = EXPERTS // world
+    progress(f"building {local} local experts")
+    w13 = torch.empty((local, HIDDEN, 2 * FFN), dtype=torch.bfloat16, device=device)
+    w2 = torch.empty((local, FFN, HIDDEN), dtype=torch.bfloat16, device=device)
+    for i in range(local):
+        w13[i] = expert_weight(rank * local + i, device)
+        w2[i] = expert_down_weight(rank * local + i, device)
+    gen = torch.Generator(device=device).manual_seed(31337 + rank)
+    x = torch.randn((tokens, HIDDEN), device=device, generator=gen).to(torch.bfloat16)
+    scores = torch.rand((tokens, EXPERTS), device=device, generator=gen)
+    top = scores.topk(top_k, dim=1)
+    ids = top.indices.to(torch.int32).contiguous()
+    weights = torch.softmax(top.values, dim=1).float().contiguous()
+    out = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device=device)
+    layer = ExpertParallelMoE(w13, w2, EXPERTS, max_tokens=tokens, top_k=top_k)
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    progress(f"tiles {layer.tile_configs(tokens)}")
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            layer(x, ids, weights, out)
+    stream.synchronize()
+    check_device_errors(local_rank)
+
+    gpu_index = os.environ.get("CUDA_VISIBLE_DEVICES", str(local_rank)).split(",")[local_rank] \
+        if "CUDA_VISIBLE_DEVICES" in os.environ else str(local_rank)
+    sampler = ClockSampler(gpu_index)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    sampler.start()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall_begin = time.time()
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(args.steps):
+            layer(x, ids, weights, out)
+        end.record(stream)
+    torch.cuda.synchronize(device)
+    sampler.mark(wall_begin, time.time())
+    clocks = sampler.stop()
+    elapsed = torch.tensor([start.elapsed_time(end)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(elapsed, op=dist.ReduceOp.MAX)
+    max_ms = float(elapsed.item())
+    check_device_errors(local_rank)
+
+    # Phase split from a few more steps (dispatch incl. route and exchange,
+    # W13, W2, combine incl. its barrier).
+    phases = {"dispatch": [], "w13": [], "w2": [], "combine": []}
+    with torch.cuda.stream(stream):
+        for _ in range(5):
+            begin = torch.cuda.Event(enable_timing=True)
+            marks = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            begin.record(stream)
+            layer(x, ids, weights, out, phase_events=marks)
+            stream.synchronize()
+            prev = begin
+            for name, ev in zip(phases, marks):
+                phases[name].append(prev.elapsed_time(ev))
+                prev = ev
+    phase_ms = {k: round(statistics.median(v), 4) for k, v in phases.items()}
+
+    progress("end-to-end pass")
+    host_x = torch.empty(x.shape, dtype=x.dtype, pin_memory=True).copy_(x)
+    host_ids = torch.empty(ids.shape, dtype=ids.dtype, pin_memory=True).copy_(ids)
+    host_w = torch.empty(weights.shape, dtype=weights.dtype, pin_memory=True).copy_(weights)
+    host_out = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    e2e_steps = max(1, args.e2e_steps)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(device)
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e_start.record(stream)
+        for _ in range(e2e_steps):
+            x.copy_(host_x, non_blocking=True)
+            ids.copy_(host_ids, non_blocking=True)
+            weights.copy_(host_w, non_blocking=True)
+            layer(x, ids, weights, out)
+            host_out.copy_(out, non_blocking=True)
+        e_end.record(stream)
+    torch.cuda.synchronize(device)
+    e2e_t = torch.tensor([e_start.elapsed_time(e_end)], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(e2e_t.item())
+    check_device_errors(local_rank)
+
+    progress("verification")
+    sample = torch.arange(0, tokens, max(1, tokens // 8), device=device)[:8]
+    expected = layer_reference(x[sample], ids[sample].cpu(), weights[sample].cpu(), device)
+    got = out[sample].float()
+    err = torch.tensor([float((got - expected).norm() / expected.norm().clamp_min(1e-30))], device=device,
+                       dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    launches = layer.launches_per_forward() * args.steps
+    layer.close()
+
+    if rank == 0:
+        slots = tokens * top_k
+        step_flops = world * slots * 2 * (HIDDEN * 2 * FFN + FFN * HIDDEN)
+        value = step_flops * args.steps / (max_ms * 1e-3) / 1e12
+        ms_step = max_ms / args.steps
+        gemm_ms = phase_ms["w13"] + phase_ms["w2"]
+        tc_peak = peaks["bf16_tflops_sustained"]
+        achieved = step_flops / world / (gemm_ms * 1e-3) / 1e12
+        moved = slots * HIDDEN * 2
+        line = {
+            "metric": "MoE expert layer TFLOP/s (route + dispatch + W13 SwiGLU + W2 + combine), whole job",
+            "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded tokens, uniform "
+            "random top-8 routing, random-init expert weights)",
+            "config": {"workload": LAYER_WORKLOAD, "tokens_per_rank": tokens, "experts_per_rank": local,
+                       "rows_per_expert_avg": slots / local, "parallelism": f"ep{world}",
+                       "l2": "weights (2.8 GB per 32 experts) exceed L2; no flush"},
+            "phases_ms": phase_ms,
+            "roofline": {"bound": "tensor", "kernel": "W13 + W2 grouped GEMMs", "achieved": round(achieved, 1),
+                         "peak": tc_peak, "unit": "TFLOP/s", "frac": round(achieved / tc_peak, 3),
+                         "peak_source": peak_source, "traffic": None,
+                         "gemm_share": round(gemm_ms / sum(phase_ms.values()), 3)},
+            "exchange": {"dispatch_gbs": round(moved / (phase_ms["dispatch"] * 1e-3) / 1e9, 1),
+                         "combine_gbs": round(moved / (phase_ms["combine"] * 1e-3) / 1e9, 1),
+                         "bytes_per_rank": moved},
+            "e2e": {"value": round(step_flops * e2e_steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "h2d_bytes_per_step": host_x.numel() * 2 + host_ids.numel() * 4 + host_w.numel() * 4,
+                    "d2h_bytes_per_step": host_out.numel() * 2},
+            "gpu_launches": launches, "clocks": clocks,
+            "verify": {"sampled_tokens": int(sample.numel()), "max_rel_err": float(err.item()), "tol": 1e-2,
+                       "ok": float(err.item()) < 1e-2},
+        }
+        print(json.dumps(line), flush=True)
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
     if args.warmup < 3:
@@ -781,6 +954,11 @@ def main(argv=None) -> int:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    if args.moe_layer:
+        moe_layer_bench(args, rank, world, local_rank, device)
+        if world > 1:
+            dist.destroy_process_group()
+        return 0
     m_values = [int(v) for v in args.m_values.split(",")]
     peaks, peak_source = load_peaks()
 

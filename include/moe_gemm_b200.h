@@ -154,6 +154,110 @@ int grouped_gemm_fp8_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const 
                             const mgb_tile_config* config, void* scratch, size_t scratch_bytes, void* stream,
                             mgb_launch_info* info);
 
+/* grouped_gemm_offsets_launch where several row segments share one B: with
+ * b_count > 0, segment e multiplies B[e % b_count] (b_count = 0 is the plain
+ * call).  An expert-parallel rank that received P senders' tokens, each sender's
+ * block sorted by the rank's b_count local experts, runs its experts over the
+ * received buffer as P * b_count segments without re-sorting it. */
+int grouped_gemm_offsets_launch_ex(const void* a, const void* b, void* c, const int32_t* offs,
+                                   int32_t problem_count, int32_t b_count, int64_t total_rows, int64_t n, int64_t k,
+                                   int64_t stride_am, int64_t stride_be, int64_t stride_bk, int64_t stride_cm,
+                                   int32_t dtype, int32_t precision, int32_t swiglu, const mgb_tile_config* config,
+                                   void* scratch, size_t scratch_bytes, void* stream, mgb_launch_info* info);
+
+/* MoE routing, permutation and combine (an expert-parallel layer around the
+ * grouped GEMMs; the reference excludes routing and all-to-all, README.md:14,
+ * README.md:35).  topk_ids: int32 [tokens, top_k] global expert ids in
+ * [0, num_experts) (others are dropped).  All device pointers, `stream` the
+ * caller's.
+ *
+ * moe_route_layout: counts [num_experts] (int32, zeroed by the call) = slots
+ * per expert; position [tokens * top_k] = the slot's index inside its expert
+ * (-1 for a dropped slot).  Slots of one expert keep no particular order. */
+int moe_route_layout(const int32_t* topk_ids, int64_t tokens, int32_t top_k, int32_t num_experts, int32_t* counts,
+                     int32_t* position, void* stream);
+
+/* moe_permute: sorted[offsets[e] + position[i], :] = x[i / top_k, :] for every
+ * kept slot i (offsets = exclusive prefix sum of counts, int32
+ * [num_experts]); rows of `hidden` elements of elem_bytes (2 or 4), row
+ * pitches in elements. */
+int moe_permute(const void* x, int64_t x_pitch, const int32_t* topk_ids, const int32_t* position,
+                const int32_t* offsets, int64_t tokens, int32_t top_k, int32_t num_experts, int64_t hidden,
+                void* sorted, int64_t sorted_pitch, int32_t elem_bytes, void* stream);
+
+/* moe_combine: out[t, :] = sum_j weights[t, j] * y[offsets[e_tj] + position[t*top_k + j], :]
+ * over the kept slots of token t (fp32 accumulate, bf16 in and out; a token
+ * with no kept slot gets zeros). */
+int moe_combine(const void* y, int64_t y_pitch, const int32_t* topk_ids, const float* weights,
+                const int32_t* position, const int32_t* offsets, int64_t tokens, int32_t top_k,
+                int32_t num_experts, int64_t hidden, void* out, int64_t out_pitch, void* stream);
+
+/* Expert-parallel dispatch and combine over peer memory.  No reference
+ * counterpart: the reference stops at the expert GEMMs and leaves routing and
+ * the all-to-all out (README.md:14, README.md:35).  Rank r of `world` owns
+ * experts [r * E / world, (r + 1) * E / world).  Each rank allocates one
+ * region (moe_ep_shared_alloc), sends its IPC handle to the others (any host
+ * channel), maps theirs (moe_ep_peer_open) and keeps a device int64 [world]
+ * table of every rank's region base as mapped in its own process.  A forward
+ * is, on one stream and without host synchronisation:
+ *   moe_route_layout -> moe_ep_exchange_counts -> moe_ep_dispatch ->
+ *   grouped GEMMs on the region's recv rows (offs = recv_offs, one segment per
+ *   local expert) writing its out rows -> moe_ep_combine.
+ * Every rank must run every step of every forward (with zero tokens too);
+ * barrier waits are bounded by `timeout_ns` (<= 0: 10 s) and report
+ * expiry as error bit 9, rows beyond `capacity` as bit 10 (dropped). */
+#define MGB_EP_MAX_WORLD 16
+#define MGB_EP_HANDLE_BYTES 64
+
+typedef struct mgb_ep_config {
+  int32_t rank;
+  int32_t world;       /* 1 .. MGB_EP_MAX_WORLD */
+  int32_t num_experts; /* global experts E, a multiple of world */
+  int32_t elem_bytes;  /* 2: bf16 token rows */
+  int64_t hidden;      /* row width H in elements */
+  int64_t capacity;    /* receive rows per rank (world * tokens * top_k never drops) */
+  int64_t timeout_ns;
+} mgb_ep_config;
+
+/* Byte offsets inside one rank's region (all ranks share the layout):
+ * counts int32 [2][world][E], send_base int32 [E], recv_offs int32 [E / world]
+ * (cumulative row ends of the local experts: the grouped GEMM's offs), recv and
+ * out rows [capacity][hidden]. */
+typedef struct mgb_ep_region {
+  int64_t counts;
+  int64_t send_base;
+  int64_t recv_offs;
+  int64_t recv;
+  int64_t out;
+  int64_t bytes;
+} mgb_ep_region;
+
+int moe_ep_region_layout(int32_t world, int32_t num_experts, int64_t hidden, int64_t capacity, int32_t elem_bytes,
+                         mgb_ep_region* layout);
+/* Zero-filled device allocation of `bytes` on the current device; writes its
+ * MGB_EP_HANDLE_BYTES-byte CUDA IPC handle when `ipc_handle` is non-null. */
+int moe_ep_shared_alloc(size_t bytes, void** region, void* ipc_handle);
+int moe_ep_shared_free(void* region);
+/* Maps a peer's region (peer access enabled on demand). */
+int moe_ep_peer_open(const void* ipc_handle, void** region);
+int moe_ep_peer_close(void* region);
+/* counts: this rank's moe_route_layout counts [E].  Publishes them to every
+ * rank, waits for all ranks, then writes send_base and recv_offs. */
+int moe_ep_exchange_counts(const int32_t* counts, const int64_t* peer_regions, const mgb_ep_config* config,
+                           void* stream);
+/* Copies row i / top_k of x (pitch in elements) to the owner of expert
+ * topk_ids[i], at send_base[e] + position[i] of its recv rows; returns after
+ * every rank's rows have arrived. */
+int moe_ep_dispatch(const void* x, int64_t x_pitch, const int32_t* topk_ids, const int32_t* position,
+                    int64_t tokens, int32_t top_k, const int64_t* peer_regions, const mgb_ep_config* config,
+                    void* stream);
+/* Waits until every rank's out rows are complete, then
+ * out[t, :] = sum_j topk_weights[t, j] * (owner's out row of slot t * top_k + j)
+ * (fp32 accumulate, bf16 out; dropped slots add nothing). */
+int moe_ep_combine(const int32_t* topk_ids, const float* topk_weights, const int32_t* position, int64_t tokens,
+                   int32_t top_k, const int64_t* peer_regions, const mgb_ep_config* config, void* out,
+                   int64_t out_pitch, void* stream);
+
 /* Masked single GEMM C[m, n] = A[m, k] @ B[k, n] with arbitrary element strides.
  * Replaces the Triton launch of launch_matmul (kernels/matmul.py:332-392,
  * kernel _matmul_kernel_impl :223-273).  Operands that satisfy the TMA rules

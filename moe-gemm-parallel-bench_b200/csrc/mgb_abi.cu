@@ -384,6 +384,13 @@ int grouped_launch_impl(const int64_t* a_ptrs, const int64_t* b_ptrs, const int6
 
 }  // namespace
 
+namespace mgb {
+uint32_t* current_error_word() {
+  DeviceState ds;
+  return device_state(&ds) == MGB_OK ? ds.error_word : nullptr;
+}
+}  // namespace mgb
+
 extern "C" {
 
 int grouped_gemm_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs, const int32_t* dims,
@@ -409,6 +416,17 @@ int grouped_gemm_offsets_launch(const void* a, const void* b, void* c, const int
                                 int64_t stride_bk, int64_t stride_cm, int32_t dtype, int32_t precision,
                                 int32_t swiglu, const mgb_tile_config* config, void* scratch, size_t scratch_bytes,
                                 void* stream, mgb_launch_info* info) {
+  return grouped_gemm_offsets_launch_ex(a, b, c, offs, problem_count, 0, total_rows, n, k, stride_am, stride_be,
+                                        stride_bk, stride_cm, dtype, precision, swiglu, config, scratch,
+                                        scratch_bytes, stream, info);
+}
+
+int grouped_gemm_offsets_launch_ex(const void* a, const void* b, void* c, const int32_t* offs,
+                                   int32_t problem_count, int32_t b_count, int64_t total_rows, int64_t n, int64_t k,
+                                   int64_t stride_am, int64_t stride_be, int64_t stride_bk, int64_t stride_cm,
+                                   int32_t dtype, int32_t precision, int32_t swiglu, const mgb_tile_config* config,
+                                   void* scratch, size_t scratch_bytes, void* stream, mgb_launch_info* info) {
+  if (b_count < 0) return MGB_ERR_INVALID;
   if (!valid_dtype(dtype, precision) || problem_count <= 0 || offs == nullptr || total_rows < 0 || n <= 0 ||
       k < 0 || stride_am < k || stride_bk < n || stride_be < k * n || stride_cm < (swiglu ? n / 2 : n)) {
     return MGB_ERR_INVALID;
@@ -435,6 +453,7 @@ int grouped_gemm_offsets_launch(const void* a, const void* b, void* c, const int
   p.scm = stride_cm;
   p.scn = 1;
   p.sbe = stride_be;
+  p.b_count = b_count;
   p.elem_bytes = es;
   p.problem_count = problem_count;
   p.homogeneous = 0;

@@ -42,6 +42,7 @@ struct GroupedParams {
   // experts, C [T, N]; pointers in a / b / c, row strides sam / sbk / scm.
   const int32_t* offs;
   int64_t sbe;
+  int32_t b_count;  // > 0: problem e uses B[e % b_count] (segments of several senders share an expert)
   int32_t elem_bytes;
   int32_t unit_tiles;     // tensor-core kernels: consecutive tiles of one problem a CTA takes at a time
   // Heterogeneous tensor-core launches: unit_start[e] = units of problems
@@ -86,7 +87,7 @@ __device__ __forceinline__ Problem load_problem(const GroupedParams& p, int e) {
     q.n = p.n;
     q.k = p.k;
     q.a = static_cast<const char*>(p.a) + start * p.sam * es;
-    q.b = static_cast<const char*>(p.b) + e * p.sbe * es;
+    q.b = static_cast<const char*>(p.b) + (p.b_count > 0 ? e % p.b_count : e) * p.sbe * es;
     q.c = static_cast<char*>(p.c) + start * p.scm * es;
     q.sam = p.sam; q.sak = 1; q.sbk = p.sbk; q.sbn = 1; q.scm = p.scm; q.scn = 1;
     return q;

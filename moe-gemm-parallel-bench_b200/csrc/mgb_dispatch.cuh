@@ -54,6 +54,11 @@ int fp8_launch(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wg
 int fp8_maps_launch(const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out, const GroupedParams& p,
                     cudaStream_t stream);
 
+// The current device's error word (device pointer), or nullptr when the CUDA
+// runtime cannot resolve it; kernels outside the GEMM families OR their
+// kErr* bits into it.
+uint32_t* current_error_word();
+
 // Launches simt_grouped_kernel<T>; returns a cudaError_t value.
 template <typename T>
 int simt_launch(const GroupedParams& p, int grid, cudaStream_t stream);

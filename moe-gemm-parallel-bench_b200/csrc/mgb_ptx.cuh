@@ -21,6 +21,8 @@ enum ErrorBits : uint32_t {
   kErrBadDims = 1u << 6,        // a problem has negative dims; problem skipped
   kErrTestWait = 1u << 7,       // the test-only never-arrived barrier timed out (expected)
   kErrBadStore = 1u << 8,       // an output tile store fell outside C (not issued; a kernel bug)
+  kErrPeerWait = 1u << 9,       // an expert-parallel barrier gave up waiting for a peer rank
+  kErrCapacity = 1u << 10,      // expert-parallel rows beyond a rank's receive capacity were dropped
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {

@@ -31,6 +31,18 @@ EXPORTED_SYMBOLS = (
     "grouped_gemm_launch",
     "grouped_gemm_swiglu_launch",
     "grouped_gemm_offsets_launch",
+    "grouped_gemm_offsets_launch_ex",
+    "moe_route_layout",
+    "moe_permute",
+    "moe_combine",
+    "moe_ep_region_layout",
+    "moe_ep_shared_alloc",
+    "moe_ep_shared_free",
+    "moe_ep_peer_open",
+    "moe_ep_peer_close",
+    "moe_ep_exchange_counts",
+    "moe_ep_dispatch",
+    "moe_ep_combine",
     "grouped_gemm_fp8_launch",
     "grouped_gemm_launch_noalloc",
     "matmul_launch",
@@ -52,7 +64,11 @@ ERROR_BITS = {
     1 << 6: "a problem had invalid dimensions and was skipped",
     1 << 7: "test-only barrier wait timed out",
     1 << 8: "an output tile store fell outside C and was not issued (kernel bug)",
+    1 << 9: "an expert-parallel barrier timed out waiting for a peer rank",
+    1 << 10: "expert-parallel rows beyond a rank's receive capacity were dropped",
 }
+EP_HANDLE_BYTES = 64
+EP_MAX_WORLD = 16
 TEST_WAIT_BIT = 1 << 7
 
 
@@ -89,6 +105,33 @@ class LaunchInfo(ctypes.Structure):
             "stages": int(self.stages),
             "grid": int(self.grid),
         }
+
+
+class EpConfig(ctypes.Structure):
+    """mgb_ep_config: one rank's view of an expert-parallel layer."""
+
+    _fields_ = [
+        ("rank", ctypes.c_int32),
+        ("world", ctypes.c_int32),
+        ("num_experts", ctypes.c_int32),
+        ("elem_bytes", ctypes.c_int32),
+        ("hidden", ctypes.c_int64),
+        ("capacity", ctypes.c_int64),
+        ("timeout_ns", ctypes.c_int64),
+    ]
+
+
+class EpRegion(ctypes.Structure):
+    """mgb_ep_region: byte offsets inside one rank's shared region."""
+
+    _fields_ = [
+        ("counts", ctypes.c_int64),
+        ("send_base", ctypes.c_int64),
+        ("recv_offs", ctypes.c_int64),
+        ("recv", ctypes.c_int64),
+        ("out", ctypes.c_int64),
+        ("bytes", ctypes.c_int64),
+    ]
 
 
 class NativeLaunchError(RuntimeError):
@@ -128,6 +171,44 @@ def _declare(lib) -> None:
         ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
     ]
     lib.grouped_gemm_offsets_launch.restype = ctypes.c_int
+    lib.grouped_gemm_offsets_launch_ex.argtypes = [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32,
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int32, ctypes.POINTER(TileConfig),
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
+    ]
+    lib.grouped_gemm_offsets_launch_ex.restype = ctypes.c_int
+    lib.moe_route_layout.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+                                     ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    lib.moe_route_layout.restype = ctypes.c_int
+    lib.moe_permute.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p,
+                                ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p]
+    lib.moe_permute.restype = ctypes.c_int
+    lib.moe_combine.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
+                                ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
+    lib.moe_combine.restype = ctypes.c_int
+    lib.moe_ep_region_layout.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
+                                         ctypes.c_int32, ctypes.POINTER(EpRegion)]
+    lib.moe_ep_region_layout.restype = ctypes.c_int
+    lib.moe_ep_shared_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
+    lib.moe_ep_shared_alloc.restype = ctypes.c_int
+    lib.moe_ep_shared_free.argtypes = [ctypes.c_void_p]
+    lib.moe_ep_shared_free.restype = ctypes.c_int
+    lib.moe_ep_peer_open.argtypes = [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]
+    lib.moe_ep_peer_open.restype = ctypes.c_int
+    lib.moe_ep_peer_close.argtypes = [ctypes.c_void_p]
+    lib.moe_ep_peer_close.restype = ctypes.c_int
+    lib.moe_ep_exchange_counts.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(EpConfig), ctypes.c_void_p]
+    lib.moe_ep_exchange_counts.restype = ctypes.c_int
+    lib.moe_ep_dispatch.argtypes = [ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                    ctypes.c_int32, ctypes.c_void_p, ctypes.POINTER(EpConfig), ctypes.c_void_p]
+    lib.moe_ep_dispatch.restype = ctypes.c_int
+    lib.moe_ep_combine.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
+                                   ctypes.c_void_p, ctypes.POINTER(EpConfig), ctypes.c_void_p, ctypes.c_int64,
+                                   ctypes.c_void_p]
+    lib.moe_ep_combine.restype = ctypes.c_int
     lib.grouped_gemm_fp8_launch.argtypes = [
         c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
         ctypes.c_int64, ctypes.c_int64, ctypes.POINTER(TileConfig), ctypes.c_void_p, ctypes.c_size_t,
@@ -228,18 +309,86 @@ def grouped_launch(
 def offsets_launch(
     a: int, b: int, c: int, offs: int, problem_count: int, total_rows: int, n: int, k: int, stride_am: int,
     stride_be: int, stride_bk: int, stride_cm: int, dtype: str, precision: str, swiglu: bool, config, scratch: int,
-    scratch_nbytes: int, stream: int,
+    scratch_nbytes: int, stream: int, b_count: int = 0,
 ) -> LaunchInfo:
-    """grouped_gemm_offsets_launch: the expert-sorted aggregate layout."""
+    """grouped_gemm_offsets_launch_ex: the expert-sorted aggregate layout
+    (segment e multiplies B[e % b_count] when b_count > 0)."""
     info = LaunchInfo()
     cfg = tile_config(config)
-    status = load().grouped_gemm_offsets_launch(
-        a, b, c, offs, int(problem_count), int(total_rows), int(n), int(k), int(stride_am), int(stride_be),
-        int(stride_bk), int(stride_cm), DTYPE_CODES[dtype], PRECISION_CODES[precision], int(bool(swiglu)),
-        ctypes.byref(cfg), scratch, int(scratch_nbytes), stream, ctypes.byref(info),
+    status = load().grouped_gemm_offsets_launch_ex(
+        a, b, c, offs, int(problem_count), int(b_count), int(total_rows), int(n), int(k), int(stride_am),
+        int(stride_be), int(stride_bk), int(stride_cm), DTYPE_CODES[dtype], PRECISION_CODES[precision],
+        int(bool(swiglu)), ctypes.byref(cfg), scratch, int(scratch_nbytes), stream, ctypes.byref(info),
     )
-    _check(status, "grouped_gemm_offsets_launch")
+    _check(status, "grouped_gemm_offsets_launch_ex")
     return info
+
+
+def route_layout(topk_ids: int, tokens: int, top_k: int, num_experts: int, counts: int, position: int,
+                 stream: int) -> None:
+    _check(load().moe_route_layout(topk_ids, int(tokens), int(top_k), int(num_experts), counts, position, stream),
+           "moe_route_layout")
+
+
+def permute(x: int, x_pitch: int, topk_ids: int, position: int, offsets: int, tokens: int, top_k: int,
+            num_experts: int, hidden: int, sorted_rows: int, sorted_pitch: int, elem_bytes: int, stream: int) -> None:
+    _check(load().moe_permute(x, int(x_pitch), topk_ids, position, offsets, int(tokens), int(top_k), int(num_experts),
+                              int(hidden), sorted_rows, int(sorted_pitch), int(elem_bytes), stream), "moe_permute")
+
+
+def combine(y: int, y_pitch: int, topk_ids: int, weights: int, position: int, offsets: int, tokens: int, top_k: int,
+            num_experts: int, hidden: int, out: int, out_pitch: int, stream: int) -> None:
+    _check(load().moe_combine(y, int(y_pitch), topk_ids, weights, position, offsets, int(tokens), int(top_k),
+                              int(num_experts), int(hidden), out, int(out_pitch), stream), "moe_combine")
+
+
+def ep_region_layout(world: int, num_experts: int, hidden: int, capacity: int, elem_bytes: int) -> EpRegion:
+    region = EpRegion()
+    _check(load().moe_ep_region_layout(int(world), int(num_experts), int(hidden), int(capacity), int(elem_bytes),
+                                       ctypes.byref(region)), "moe_ep_region_layout")
+    return region
+
+
+def ep_shared_alloc(nbytes: int, with_handle: bool = True) -> tuple[int, bytes]:
+    """Zero-filled device region on the current device and its IPC handle
+    (empty without ``with_handle``)."""
+    ptr = ctypes.c_void_p()
+    handle = ctypes.create_string_buffer(EP_HANDLE_BYTES) if with_handle else None
+    _check(load().moe_ep_shared_alloc(int(nbytes), ctypes.byref(ptr), handle), "moe_ep_shared_alloc")
+    return int(ptr.value), (handle.raw if with_handle else b"")
+
+
+def ep_shared_free(ptr: int) -> None:
+    _check(load().moe_ep_shared_free(ptr), "moe_ep_shared_free")
+
+
+def ep_peer_open(handle: bytes) -> int:
+    if len(handle) != EP_HANDLE_BYTES:
+        raise ValueError(f"an IPC handle has {EP_HANDLE_BYTES} bytes, got {len(handle)}")
+    ptr = ctypes.c_void_p()
+    _check(load().moe_ep_peer_open(ctypes.create_string_buffer(handle, EP_HANDLE_BYTES), ctypes.byref(ptr)),
+           "moe_ep_peer_open")
+    return int(ptr.value)
+
+
+def ep_peer_close(ptr: int) -> None:
+    _check(load().moe_ep_peer_close(ptr), "moe_ep_peer_close")
+
+
+def ep_exchange_counts(counts: int, peers: int, config: EpConfig, stream: int) -> None:
+    _check(load().moe_ep_exchange_counts(counts, peers, ctypes.byref(config), stream), "moe_ep_exchange_counts")
+
+
+def ep_dispatch(x: int, x_pitch: int, topk_ids: int, position: int, tokens: int, top_k: int, peers: int,
+                config: EpConfig, stream: int) -> None:
+    _check(load().moe_ep_dispatch(x, int(x_pitch), topk_ids, position, int(tokens), int(top_k), peers,
+                                  ctypes.byref(config), stream), "moe_ep_dispatch")
+
+
+def ep_combine(topk_ids: int, weights: int, position: int, tokens: int, top_k: int, peers: int, config: EpConfig,
+               out: int, out_pitch: int, stream: int) -> None:
+    _check(load().moe_ep_combine(topk_ids, weights, position, int(tokens), int(top_k), peers, ctypes.byref(config),
+                                 out, int(out_pitch), stream), "moe_ep_combine")
 
 
 def fp8_launch(

@@ -461,7 +461,10 @@ def launch_grouped_mm(mat_a, mat_b, offs, out=None, *, config: KernelConfig | No
     142-158): ``mat_a`` [T, K] with tokens sorted by expert, ``mat_b`` [E, K, N],
     ``offs`` int32 [E] cumulative row ends on the same device (read by the
     kernel, so no host synchronisation and CUDA-graph capturable once the
-    scratch exists: make the first call for a group size eagerly).  Rows of
+    scratch exists: make the first call for a group size eagerly).  ``offs``
+    may also hold S = P * E segments (P senders' blocks, each sorted by the E
+    experts, as an expert-parallel rank receives them): segment s multiplies
+    ``mat_b[s % E]``.  Rows of
     ``mat_a`` / ``mat_b`` / ``out`` may be padded (row strides ≥ the logical
     width); columns must be contiguous.  With ``swiglu`` each ``mat_b[e]`` is a
     packed [gate | up] weight and ``out`` is [T, N/2] =
@@ -475,7 +478,8 @@ def launch_grouped_mm(mat_a, mat_b, offs, out=None, *, config: KernelConfig | No
         raise ValueError("expected mat_a [T, K], mat_b [E, K, N] and offs [E]")
     total, k = mat_a.shape
     experts, kb, n = mat_b.shape
-    if kb != k or offs.shape[0] != experts or experts == 0:
+    segments = offs.shape[0]
+    if kb != k or experts == 0 or segments == 0 or segments % experts:
         raise ValueError(f"shape mismatch: mat_a={tuple(mat_a.shape)}, mat_b={tuple(mat_b.shape)}, offs={tuple(offs.shape)}")
     if offs.dtype != torch.int32:
         raise ValueError("offs must be int32 cumulative row ends")
@@ -494,19 +498,19 @@ def launch_grouped_mm(mat_a, mat_b, offs, out=None, *, config: KernelConfig | No
         raise ValueError("columns of mat_a, mat_b and out must be contiguous (row padding is allowed)")
     if input_precision not in _native.PRECISION_CODES:
         raise ValueError(f"input_precision must be 'ieee' or 'tf32', got {input_precision!r}")
-    key = (mat_a.device.index or 0, experts)
+    key = (mat_a.device.index or 0, segments)
     scratch = _AGGREGATE_SCRATCH.get(key)
     if scratch is None:
-        scratch = torch.empty(_native.scratch_bytes(experts, 0), dtype=torch.uint8, device=mat_a.device)
+        scratch = torch.empty(_native.scratch_bytes(segments, 0), dtype=torch.uint8, device=mat_a.device)
         _AGGREGATE_SCRATCH[key] = scratch
     global _last_aggregate_info
-    cfg = config or native_candidates(max(1, -(-total // experts)), k)[0]
+    cfg = config or native_candidates(max(1, -(-total // segments)), k)[0]
     with torch.cuda.device(mat_a.device):
         info = _native.offsets_launch(
-            mat_a.data_ptr(), mat_b.data_ptr(), out.data_ptr(), offs.data_ptr(), experts, total, n, k,
+            mat_a.data_ptr(), mat_b.data_ptr(), out.data_ptr(), offs.data_ptr(), segments, total, n, k,
             mat_a.stride(0), mat_b.stride(0), mat_b.stride(1), out.stride(0), dtype_name(mat_a.dtype),
             input_precision, swiglu, cfg, scratch.data_ptr(), scratch.numel(),
-            torch.cuda.current_stream(mat_a.device).cuda_stream,
+            torch.cuda.current_stream(mat_a.device).cuda_stream, b_count=experts if segments != experts else 0,
         )
     _last_aggregate_info = info.as_dict()
     return out
