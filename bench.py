@@ -904,7 +904,18 @@ def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> Non
         ms_step = max_ms / args.steps
         gemm_ms = phase_ms["w13"] + phase_ms["w2"]
         tc_peak = peaks["bf16_tflops_sustained"]
-        achieved = step_flops / world / (gemm_ms * 1e-3) / 1e12
+        # Per rank and GEMM: FLOPs on the tensor cores, or the expert weights
+        # plus input and output rows through HBM, whichever takes longer.
+        rows = slots  # rows a rank receives under uniform routing
+        gemm_flops = rows * 2 * (HIDDEN * 2 * FFN + FFN * HIDDEN)
+        gemm_bytes = 2 * (local * (HIDDEN * 2 * FFN + FFN * HIDDEN) + rows * (HIDDEN + FFN) * 2)
+        t_tensor = gemm_flops / (tc_peak * 1e12)
+        t_hbm = gemm_bytes / (peaks["hbm_gbs"] * 1e9)
+        bound = "tensor" if t_tensor >= t_hbm else "hbm"
+        if bound == "tensor":
+            achieved, peak, unit = gemm_flops / (gemm_ms * 1e-3) / 1e12, tc_peak, "TFLOP/s"
+        else:
+            achieved, peak, unit = gemm_bytes / (gemm_ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
         moved = slots * HIDDEN * 2
         line = {
             "metric": "MoE expert layer TFLOP/s (route + dispatch + W13 SwiGLU + W2 + combine), whole job",
@@ -916,10 +927,11 @@ def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> Non
                        "rows_per_expert_avg": slots / local, "parallelism": f"ep{world}",
                        "l2": "weights (2.8 GB per 32 experts) exceed L2; no flush"},
             "phases_ms": phase_ms,
-            "roofline": {"bound": "tensor", "kernel": "W13 + W2 grouped GEMMs", "achieved": round(achieved, 1),
-                         "peak": tc_peak, "unit": "TFLOP/s", "frac": round(achieved / tc_peak, 3),
+            "roofline": {"bound": bound, "kernel": "W13 + W2 grouped GEMMs", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": unit, "frac": round(achieved / peak, 3),
                          "peak_source": peak_source, "traffic": None,
-                         "gemm_share": round(gemm_ms / sum(phase_ms.values()), 3)},
+                         "gemm_share": round(gemm_ms / sum(phase_ms.values()), 3),
+                         "gemm_roofline_ms": round(max(t_tensor, t_hbm) * 1e3, 4)},
             "exchange": {"dispatch_gbs": round(moved / (phase_ms["dispatch"] * 1e-3) / 1e9, 1),
                          "combine_gbs": round(moved / (phase_ms["combine"] * 1e-3) / 1e9, 1),
                          "bytes_per_rank": moved},

@@ -46,7 +46,8 @@ struct Tc2Cfg {
   static constexpr int kHalfWgtBytes = kHalf * 128;  // one CTA's weight columns of one MMA half
   static constexpr int kWgtBytes = NH * kHalfWgtBytes;
   static constexpr int kStageBytes = kActBytes + kWgtBytes;
-  static constexpr int kEpiBytes = kEpiBytesRowTile;  // staging blocks of the 4 epilogue warps
+  static constexpr int kEpiBlocks = 4;
+  static constexpr int kEpiBytes = epi_bytes_row_tile(kEpiBlocks);  // staging blocks of the 4 epilogue warps
   static constexpr int kStagesRaw = (kTcSmemBudget - kEpiBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
   static constexpr int kAccCols = kTileN;
@@ -256,7 +257,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     }
     TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
     uint32_t acc_it = 0;
-    uint8_t* my_blocks = epi_stage + quarter * 2 * kEpiWarpBytes;
+    uint8_t* my_blocks = epi_stage + quarter * Cfg::kEpiBlocks * kEpiWarpBytes;
     int c_built = -1;
     const uint64_t pol_out = policy_evict_first();
     uint32_t chunk_seq = 0;
@@ -287,14 +288,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
                              static_cast<uint32_t>(buf * Cfg::kAccCols);
       if (p.swiglu) {
         if (cmap != nullptr) {
-          store_rows_tma_swiglu<T, Cfg::kTileN / 2>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
+          store_rows_tma_swiglu<T, Cfg::kTileN / 2, Cfg::kEpiBlocks>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
                                                     static_cast<int32_t>(n0), my_blocks, lane, chunk_seq, pol_out,
                                                     p.error_word);
         } else {
           store_rows_scalar_swiglu<T, Cfg::kTileN / 2>(q, taddr, m0 + quarter * 32, n0, lane);
         }
       } else if (cmap != nullptr) {
-        store_rows_tma<T, Cfg::kTileN>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
+        store_rows_tma<T, Cfg::kTileN, Cfg::kEpiBlocks>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
                                        static_cast<int32_t>(n0), my_blocks, lane, chunk_seq, pol_out, p.error_word);
       } else {
         store_rows_staged<T, Cfg::kTileN>(q, taddr, m0 + quarter * 32, n0, my_blocks, lane);

@@ -40,7 +40,12 @@ constexpr int kTcThreads = 192;
 // alignment of the ring.
 constexpr int kTcSmemBudget = 232448 - 3072;
 constexpr int kEpiWarpBytes = 32 * 128;  // one staging block: 32 rows x 128 bytes
-constexpr int kEpiBytesRowTile = 4 * 2 * kEpiWarpBytes;  // 4 epilogue warps x 2 blocks (double-buffered)
+// Staging blocks per epilogue warp (NB): a block is reused once the tensor
+// store issued from it NB chunks earlier has read it, so NB stores of a warp
+// can be in flight.  One-CTA row tiles keep 2 (their operand ring needs the
+// shared memory: 4 stages of 128 x 256 tiles); CTA-pair tiles take 4, which
+// measured faster on the large-M W13 shapes.
+constexpr int epi_bytes_row_tile(int blocks) { return 4 * blocks * kEpiWarpBytes; }  // 4 epilogue warps
 // Tensor maps of a grouped launch: build_maps_kernel writes A, B and C maps of
 // every problem into the scratch buffer before the GEMM kernel runs.
 constexpr int kMapsPerProblem = 3;
@@ -64,7 +69,8 @@ struct TcCfg {
   // Row tiles stage their epilogue through shared memory and store it with
   // TMA (store_rows_tma); swap-AB tiles store column-per-lane, already
   // contiguous across the warp.
-  static constexpr int kEpiBytes = SWAP ? 0 : kEpiBytesRowTile;
+  static constexpr int kEpiBlocks = 2;
+  static constexpr int kEpiBytes = SWAP ? 0 : epi_bytes_row_tile(kEpiBlocks);
   static constexpr int kStagesRaw = (kTcSmemBudget - kEpiBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
 
@@ -252,7 +258,7 @@ __device__ __forceinline__ void write_unit_smem(const uint32_t (&v)[32], uint8_t
 // other) and written by one tensor store of 32 rows x 128 bytes; rows and
 // columns past C's extents are clipped by the tensor map.  `seq` counts the
 // warp's chunks across tiles and picks the block.
-template <typename T, int TN>
+template <typename T, int TN, int NB>
 __device__ __forceinline__ void store_rows_tma(const Problem& q, const void* cmap, uint32_t taddr, int32_t row0,
                                                int32_t n0, uint8_t* blocks, int lane, uint32_t& seq,
                                                uint64_t policy, uint32_t* error_word) {
@@ -271,9 +277,9 @@ __device__ __forceinline__ void store_rows_tma(const Problem& q, const void* cma
     if (g >= units) break;
     const int c = g / kUnits;
     const int u = g % kUnits;
-    uint8_t* block = blocks + ((seq + static_cast<uint32_t>(c)) & 1u) * kEpiWarpBytes;
+    uint8_t* block = blocks + ((seq + static_cast<uint32_t>(c)) % NB) * kEpiWarpBytes;
     if (u == 0) {
-      if (lane == 0) bulk_wait_group_read<1>();  // the store issued from `block` two chunks ago has read it
+      if (lane == 0) bulk_wait_group_read<NB - 1>();  // the store last issued from `block` has read it
       __syncwarp();
     }
     tmem_ld_wait();  // unit g has landed
@@ -302,7 +308,7 @@ __device__ __forceinline__ void store_rows_tma(const Problem& q, const void* cma
 // TMEM columns [0, TO), up columns [TO, 2 TO); each 32-column output unit
 // loads both, computes silu(gate) * up in fp32 and is staged and stored like
 // store_rows_tma.
-template <typename T, int TO>
+template <typename T, int TO, int NB>
 __device__ __forceinline__ void store_rows_tma_swiglu(const Problem& qo, const void* cmap, uint32_t taddr,
                                                       int32_t row0, int32_t o0, uint8_t* blocks, int lane,
                                                       uint32_t& seq, uint64_t policy, uint32_t* error_word) {
@@ -317,9 +323,9 @@ __device__ __forceinline__ void store_rows_tma_swiglu(const Problem& qo, const v
   for (int g = 0; g < units; ++g) {
     const int c = g / kUnits;
     const int u = g % kUnits;
-    uint8_t* block = blocks + ((seq + static_cast<uint32_t>(c)) & 1u) * kEpiWarpBytes;
+    uint8_t* block = blocks + ((seq + static_cast<uint32_t>(c)) % NB) * kEpiWarpBytes;
     if (u == 0) {
-      if (lane == 0) bulk_wait_group_read<1>();
+      if (lane == 0) bulk_wait_group_read<NB - 1>();
       __syncwarp();
     }
     uint32_t gate[32], up[32];
@@ -731,7 +737,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     TileWalk<TM, TN> walk;
     uint32_t acc_it = 0;
-    uint8_t* my_blocks = epi_stage + quarter * 2 * kEpiWarpBytes;
+    uint8_t* my_blocks = epi_stage + quarter * Cfg::kEpiBlocks * kEpiWarpBytes;
     int c_built = -1;
     const uint64_t pol_out = policy_evict_first();
     uint32_t chunk_seq = 0;
@@ -814,7 +820,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if constexpr (TN >= 128) {
           if (p.swiglu) {
             if (cmap != nullptr) {
-              store_rows_tma_swiglu<T, TN / 2>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
+              store_rows_tma_swiglu<T, TN / 2, Cfg::kEpiBlocks>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
                                                static_cast<int32_t>(n0), my_blocks, lane, chunk_seq, pol_out,
                                                p.error_word);
             } else {
@@ -825,7 +831,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         if (!done) {
           if (cmap != nullptr) {
-            store_rows_tma<T, TN>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32), static_cast<int32_t>(n0),
+            store_rows_tma<T, TN, Cfg::kEpiBlocks>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32), static_cast<int32_t>(n0),
                                   my_blocks, lane, chunk_seq, pol_out, p.error_word);
           } else {
             store_rows_staged<T, TN>(q, taddr, m0 + quarter * 32, n0, my_blocks, lane);
