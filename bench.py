@@ -91,6 +91,8 @@ def parse_args(argv=None):
     p.add_argument("--moe-layer", action="store_true",
                    help="time the whole expert-parallel MoE layer (route, dispatch, W13 SwiGLU, W2, combine)")
     p.add_argument("--layer-tokens", type=int, default=4096, help="tokens per rank for --moe-layer")
+    p.add_argument("--ep-transport", choices=("peer", "nccl"), default="peer",
+                   help="--moe-layer exchange: peer-memory kernels, or the NCCL all_to_all_single baseline")
     p.add_argument("--tile-sweep", action="store_true",
                    help="time every native tile per shape, alone and right after a heavy launch (diagnosis)")
     return p.parse_args(argv)
@@ -792,7 +794,7 @@ def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> Non
     import torch
     import torch.distributed as dist
 
-    from expert_parallel import ExpertParallelMoE
+    from expert_parallel import ExpertParallelMoE, NcclAllToAllMoE
     from kernels import check_device_errors
 
     peaks, peak_source = load_peaks()
@@ -811,7 +813,8 @@ def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> Non
     ids = top.indices.to(torch.int32).contiguous()
     weights = torch.softmax(top.values, dim=1).float().contiguous()
     out = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device=device)
-    layer = ExpertParallelMoE(w13, w2, EXPERTS, max_tokens=tokens, top_k=top_k)
+    layer_cls = ExpertParallelMoE if args.ep_transport == "peer" else NcclAllToAllMoE
+    layer = layer_cls(w13, w2, EXPERTS, max_tokens=tokens, top_k=top_k)
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
     progress(f"tiles {layer.tile_configs(tokens)}")
@@ -894,7 +897,9 @@ def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> Non
                        dtype=torch.float64)
     if world > 1:
         dist.all_reduce(err, op=dist.ReduceOp.MAX)
-    launches = layer.launches_per_forward() * args.steps
+    # Native kernels per forward; the NCCL baseline adds torch and NCCL kernels
+    # (cumsum, index gather / scatter, all-to-alls) that are not counted.
+    launches = (layer.launches_per_forward() if args.ep_transport == "peer" else 7) * args.steps
     layer.close()
 
     if rank == 0:
@@ -924,6 +929,9 @@ def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> Non
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded tokens, uniform "
             "random top-8 routing, random-init expert weights)",
             "config": {"workload": LAYER_WORKLOAD, "tokens_per_rank": tokens, "experts_per_rank": local,
+                       "exchange": ("peer-memory dispatch / combine kernels (NVLink loads and stores)"
+                                    if args.ep_transport == "peer" else
+                                    "NCCL all_to_all_single (baseline; host sync for split sizes)"),
                        "rows_per_expert_avg": slots / local, "parallelism": f"ep{world}",
                        "l2": "weights (2.8 GB per 32 experts) exceed L2; no flush"},
             "phases_ms": phase_ms,

@@ -236,3 +236,121 @@ class ExpertParallelMoE:
 
     def __exit__(self, *exc):
         self.close()
+
+
+class NcclAllToAllMoE:
+    """The same layer with the exchange done by NCCL ``all_to_all_single`` --
+    the library baseline the peer-memory path is measured against.
+
+    Per forward: route and permute the slots into expert order (native
+    kernels), all-to-all the per-expert counts, copy the split sizes to the
+    host (the variable-split all-to-all needs them there), all-to-all the
+    rows, regroup them from source-major to expert-major (one gather), the
+    same two grouped GEMMs, the reverse gather and all-to-all, and the native
+    weighted combine.  Same arguments and results as ExpertParallelMoE.
+    """
+
+    def __init__(self, w13, w2, num_experts: int, *, max_tokens: int, top_k: int, group=None):
+        if torch is None or not torch.cuda.is_available():
+            raise RuntimeError("CUDA PyTorch and the native sm_100a library are required")
+        _native.load()
+        local, hidden, two_f = w13.shape
+        if w2.shape != (local, two_f // 2, hidden) or two_f % 2 or w13.dtype != torch.bfloat16:
+            raise ValueError("expected bf16 w13 [E_l, H, 2F] and w2 [E_l, F, H]")
+        if dist is not None and dist.is_available() and dist.is_initialized():
+            self.rank, self.world = dist.get_rank(group), dist.get_world_size(group)
+        else:
+            self.rank, self.world = 0, 1
+        if num_experts != local * self.world:
+            raise ValueError(f"num_experts {num_experts} != {self.world} ranks x {local} local experts")
+        self.group, self.device = group, w13.device
+        self.w13, self.w2 = w13.contiguous(), w2.contiguous()
+        self.num_experts, self.local_experts = num_experts, local
+        self.hidden, self.ffn, self.top_k, self.max_tokens = hidden, two_f // 2, top_k, max_tokens
+        self.counts = torch.zeros(num_experts, dtype=torch.int32, device=self.device)
+        self.position = torch.empty(max(1, max_tokens * top_k), dtype=torch.int32, device=self.device)
+        self.sorted_rows = torch.empty((max(1, max_tokens * top_k), hidden), dtype=torch.bfloat16, device=self.device)
+        self.returned = torch.empty_like(self.sorted_rows)
+
+    def tile_configs(self, tokens: int) -> tuple[KernelConfig, KernelConfig]:
+        rows = expected_rows_per_expert(tokens, self.top_k, self.local_experts)
+        return native_candidates(rows, self.hidden)[0], native_candidates(rows, self.ffn)[0]
+
+    def _all_to_all(self, out, inp, out_splits=None, in_splits=None):
+        if self.world == 1:
+            out.copy_(inp)
+        else:
+            dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def forward(self, x, topk_ids, topk_weights, out=None, *, configs=None, phase_events=None):
+        tokens, k, E, El, P = x.shape[0], self.top_k, self.num_experts, self.local_experts, self.world
+        if tokens > self.max_tokens or tuple(topk_ids.shape) != (tokens, k) or topk_ids.dtype != torch.int32:
+            raise ValueError("x / topk_ids do not match the layer")
+        if out is None:
+            out = torch.empty((tokens, self.hidden), dtype=torch.bfloat16, device=self.device)
+        cfg13, cfg2 = configs or self.tile_configs(tokens)
+        marks = list(phase_events or ())
+        with torch.cuda.device(self.device):
+            stream = torch.cuda.current_stream(self.device).cuda_stream
+            _native.route_layout(topk_ids.data_ptr(), tokens, k, E, self.counts.data_ptr(),
+                                 self.position.data_ptr(), stream)
+            starts = torch.cumsum(self.counts, 0, dtype=torch.int32) - self.counts
+            _native.permute(x.data_ptr(), x.stride(0) if tokens else self.hidden, topk_ids.data_ptr(),
+                            self.position.data_ptr(), starts.data_ptr(), tokens, k, E, self.hidden,
+                            self.sorted_rows.data_ptr(), self.hidden, 2, stream)
+            recv_counts = torch.empty_like(self.counts)
+            self._all_to_all(recv_counts, self.counts)
+            splits = torch.stack((self.counts.view(P, El).sum(1), recv_counts.view(P, El).sum(1))).cpu()
+            send_splits, recv_splits = splits[0].tolist(), splits[1].tolist()
+            received = sum(recv_splits)
+            recv_rows = torch.empty((received, self.hidden), dtype=torch.bfloat16, device=self.device)
+            self._all_to_all(recv_rows, self.sorted_rows[: sum(send_splits)], recv_splits, send_splits)
+            # Source-major [src][expert] segments -> expert-major rows.
+            per = recv_counts.view(P, El).to(torch.int64)
+            expert_start = torch.cumsum(per.sum(0), 0) - per.sum(0)
+            src_before = torch.cumsum(per, 0) - per
+            seg_dest = (expert_start[None, :] + src_before).reshape(-1)
+            seg_src = (torch.cumsum(per.reshape(-1), 0) - per.reshape(-1))
+            seg_len = per.reshape(-1)
+            seg_of_row = torch.repeat_interleave(torch.arange(P * El, device=self.device), seg_len,
+                                                 output_size=received)
+            dest = seg_dest[seg_of_row] + torch.arange(received, device=self.device) - seg_src[seg_of_row]
+            grouped = torch.empty_like(recv_rows)
+            grouped.index_copy_(0, dest, recv_rows)
+            offs = torch.cumsum(per.sum(0), 0).to(torch.int32)
+            if marks:
+                marks.pop(0).record()
+            if received:
+                h = launch_grouped_mm(grouped, self.w13, offs, swiglu=True, config=cfg13)
+                if marks:
+                    marks.pop(0).record()
+                y = launch_grouped_mm(h, self.w2, offs, config=cfg2)
+                if marks:
+                    marks.pop(0).record()
+                back = y.index_select(0, dest)
+            else:
+                for _ in range(2):
+                    if marks:
+                        marks.pop(0).record()
+                back = recv_rows
+            self._all_to_all(self.returned[: sum(send_splits)], back, send_splits, recv_splits)
+            _native.combine(self.returned.data_ptr(), self.hidden, topk_ids.data_ptr(), topk_weights.data_ptr(),
+                            self.position.data_ptr(), starts.data_ptr(), tokens, k, E, self.hidden,
+                            out.data_ptr(), out.stride(0) if tokens else self.hidden, stream)
+            if marks:
+                marks.pop(0).record()
+        return out
+
+    __call__ = forward
+
+    def check_errors(self) -> None:
+        check_device_errors(self.device)
+
+    def close(self) -> None:
+        pass
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()

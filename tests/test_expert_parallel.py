@@ -204,6 +204,22 @@ def test_single_rank_layer_matches_oracle(tokens, experts, hidden, ffn, top_k, r
 
 @pytest.mark.gpu
 @pytest.mark.skipif(not cuda_ready(), reason="needs a CUDA GPU")
+def test_nccl_baseline_layer_single_rank_matches_oracle():
+    _setup_paths()
+    from expert_parallel import NcclAllToAllMoE
+
+    tokens, experts, hidden, ffn, top_k = 150, 16, 512, 256, 4
+    x, w13, w2, ids, w = _layer_case(9, tokens, experts, hidden, ffn, top_k, drop=0.1)
+    gx, g13, g2, gids, gw = _to_gpu(x, w13, w2, ids, w)
+    layer = NcclAllToAllMoE(g13, g2, experts, max_tokens=tokens, top_k=top_k)
+    out = layer(gx, gids, gw)
+    layer.check_errors()
+    err = relative_frobenius(out.float().cpu().numpy(), oracle_moe.moe_layer(x, ids, w, w13, w2))
+    assert err < BF16_TOL, err
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(not cuda_ready(), reason="needs a CUDA GPU")
 def test_repeated_forwards_zero_tokens_and_graph_replay():
     _setup_paths()
     from expert_parallel import ExpertParallelMoE
@@ -315,7 +331,7 @@ def _two_rank_worker(rank, world, port, result_dir):
     _setup_paths()
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
-    from expert_parallel import ExpertParallelMoE
+    from expert_parallel import ExpertParallelMoE, NcclAllToAllMoE
 
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
@@ -328,19 +344,20 @@ def _two_rank_worker(rank, world, port, result_dir):
     g13 = torch.from_numpy(w13[mine]).cuda().to(torch.bfloat16)
     g2 = torch.from_numpy(w2[mine]).cuda().to(torch.bfloat16)
     worst, lines = 0.0, []
-    with ExpertParallelMoE(g13, g2, experts, max_tokens=max_tokens, top_k=top_k) as layer:
-        for step, (tokens, routing) in enumerate(((120, {}), (160, {"skew": True}), (0 if rank else 33, {}),
-                                                  (77, {"drop": 0.2}))):
-            trng = np.random.default_rng(1000 * step + rank)
-            x = _tokens(trng, tokens, hidden)
-            ids, w = _routing(trng, tokens, experts, top_k, **routing)
-            out = layer(torch.from_numpy(x).cuda().to(torch.bfloat16), torch.from_numpy(ids).cuda(),
-                        torch.from_numpy(w).cuda())
-            layer.check_errors()
-            if tokens:
-                err = relative_frobenius(out.float().cpu().numpy(), oracle_moe.moe_layer(x, ids, w, w13, w2))
-                worst = max(worst, err)
-                lines.append(f"step {step} tokens {tokens} err {err:.3e}")
+    for cls in (ExpertParallelMoE, NcclAllToAllMoE):
+        with cls(g13, g2, experts, max_tokens=max_tokens, top_k=top_k) as layer:
+            for step, (tokens, routing) in enumerate(((120, {}), (160, {"skew": True}), (0 if rank else 33, {}),
+                                                      (77, {"drop": 0.2}))):
+                trng = np.random.default_rng(1000 * step + rank)
+                x = _tokens(trng, tokens, hidden)
+                ids, w = _routing(trng, tokens, experts, top_k, **routing)
+                out = layer(torch.from_numpy(x).cuda().to(torch.bfloat16), torch.from_numpy(ids).cuda(),
+                            torch.from_numpy(w).cuda())
+                layer.check_errors()
+                if tokens:
+                    err = relative_frobenius(out.float().cpu().numpy(), oracle_moe.moe_layer(x, ids, w, w13, w2))
+                    worst = max(worst, err)
+                    lines.append(f"{cls.__name__} step {step} tokens {tokens} err {err:.3e}")
     dist.destroy_process_group()
     Path(result_dir, f"rank{rank}.txt").write_text(f"{worst}\n" + "\n".join(lines))
 
