@@ -91,8 +91,11 @@ def parse_args(argv=None):
     p.add_argument("--moe-layer", action="store_true",
                    help="time the whole expert-parallel MoE layer (route, dispatch, W13 SwiGLU, W2, combine)")
     p.add_argument("--layer-tokens", type=int, default=4096, help="tokens per rank for --moe-layer")
-    p.add_argument("--ep-transport", choices=("peer", "nccl"), default="peer",
-                   help="--moe-layer exchange: peer-memory kernels, or the NCCL all_to_all_single baseline")
+    p.add_argument("--layer-experts", type=int, default=EXPERTS,
+                   help="global experts for --moe-layer (fewer: a smaller case for profiling)")
+    p.add_argument("--ep-transport", choices=("peer", "peer-pull", "nccl"), default="peer",
+                   help="--moe-layer exchange: peer-memory kernels with W2 returning rows from its epilogue, "
+                        "peer-memory kernels with the combine pulling rows, or the NCCL all_to_all_single baseline")
     p.add_argument("--tile-sweep", action="store_true",
                    help="time every native tile per shape, alone and right after a heavy launch (diagnosis)")
     return p.parse_args(argv)
@@ -798,8 +801,10 @@ def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> Non
     from kernels import check_device_errors
 
     peaks, peak_source = load_peaks()
-    tokens, top_k = args.layer_tokens, TOPK
-    local = EXPERTS // world
+    tokens, top_k, experts = args.layer_tokens, TOPK, args.layer_experts
+    if experts % world or experts < top_k:
+        raise SystemExit("--layer-experts must be a multiple of the ranks and at least top-k")
+    local = experts // world
     progress(f"building {local} local experts")
     w13 = torch.empty((local, HIDDEN, 2 * FFN), dtype=torch.bfloat16, device=device)
     w2 = torch.empty((local, FFN, HIDDEN), dtype=torch.bfloat16, device=device)
@@ -808,13 +813,16 @@ def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> Non
         w2[i] = expert_down_weight(rank * local + i, device)
     gen = torch.Generator(device=device).manual_seed(31337 + rank)
     x = torch.randn((tokens, HIDDEN), device=device, generator=gen).to(torch.bfloat16)
-    scores = torch.rand((tokens, EXPERTS), device=device, generator=gen)
+    scores = torch.rand((tokens, experts), device=device, generator=gen)
     top = scores.topk(top_k, dim=1)
     ids = top.indices.to(torch.int32).contiguous()
     weights = torch.softmax(top.values, dim=1).float().contiguous()
     out = torch.empty((tokens, HIDDEN), dtype=torch.bfloat16, device=device)
-    layer_cls = ExpertParallelMoE if args.ep_transport == "peer" else NcclAllToAllMoE
-    layer = layer_cls(w13, w2, EXPERTS, max_tokens=tokens, top_k=top_k)
+    if args.ep_transport == "nccl":
+        layer = NcclAllToAllMoE(w13, w2, experts, max_tokens=tokens, top_k=top_k)
+    else:
+        layer = ExpertParallelMoE(w13, w2, experts, max_tokens=tokens, top_k=top_k,
+                                  fused_return=args.ep_transport == "peer")
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
     progress(f"tiles {layer.tile_configs(tokens)}")
@@ -899,7 +907,7 @@ def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> Non
         dist.all_reduce(err, op=dist.ReduceOp.MAX)
     # Native kernels per forward; the NCCL baseline adds torch and NCCL kernels
     # (cumsum, index gather / scatter, all-to-alls) that are not counted.
-    launches = (layer.launches_per_forward() if args.ep_transport == "peer" else 7) * args.steps
+    launches = (7 if args.ep_transport == "nccl" else layer.launches_per_forward()) * args.steps
     layer.close()
 
     if rank == 0:
@@ -928,10 +936,14 @@ def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> Non
             "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded tokens, uniform "
             "random top-8 routing, random-init expert weights)",
-            "config": {"workload": LAYER_WORKLOAD, "tokens_per_rank": tokens, "experts_per_rank": local,
-                       "exchange": ("peer-memory dispatch / combine kernels (NVLink loads and stores)"
-                                    if args.ep_transport == "peer" else
-                                    "NCCL all_to_all_single (baseline; host sync for split sizes)"),
+            "config": {"workload": LAYER_WORKLOAD, "tokens_per_rank": tokens, "experts": experts,
+                       "experts_per_rank": local,
+                       "exchange": {"peer": "peer-memory dispatch kernel; W2 epilogue stores rows back to the "
+                                            "source ranks (NVLink stores); local combine",
+                                    "peer-pull": "peer-memory dispatch kernel; combine loads rows from the owners "
+                                                 "(NVLink loads)",
+                                    "nccl": "NCCL all_to_all_single (baseline; host sync for split sizes)"}[
+                                        args.ep_transport],
                        "rows_per_expert_avg": slots / local, "parallelism": f"ep{world}",
                        "l2": "weights (2.8 GB per 32 experts) exceed L2; no flush"},
             "phases_ms": phase_ms,

@@ -217,23 +217,28 @@ typedef struct mgb_ep_config {
   int64_t hidden;      /* row width H in elements */
   int64_t capacity;    /* receive rows per rank (world * tokens * top_k never drops) */
   int64_t timeout_ns;
+  int64_t max_slots;   /* tokens * top_k bound of one forward: rows of the return buffer */
 } mgb_ep_config;
 
 /* Byte offsets inside one rank's region (all ranks share the layout):
  * counts int32 [2][world][E], send_base int32 [E], recv_offs int32 [E / world]
  * (cumulative row ends of the local experts: the grouped GEMM's offs), recv and
- * out rows [capacity][hidden]. */
+ * out rows [capacity][hidden], origin int64 [capacity] (receive row -> source
+ * rank << 40 | source slot, written by the dispatch), ret rows
+ * [max_slots][hidden] (expert outputs returned to this rank, by slot). */
 typedef struct mgb_ep_region {
   int64_t counts;
   int64_t send_base;
   int64_t recv_offs;
   int64_t recv;
   int64_t out;
+  int64_t origin;
+  int64_t ret;
   int64_t bytes;
 } mgb_ep_region;
 
-int moe_ep_region_layout(int32_t world, int32_t num_experts, int64_t hidden, int64_t capacity, int32_t elem_bytes,
-                         mgb_ep_region* layout);
+int moe_ep_region_layout(int32_t world, int32_t num_experts, int64_t hidden, int64_t capacity, int64_t max_slots,
+                         int32_t elem_bytes, mgb_ep_region* layout);
 /* Zero-filled device allocation of `bytes` on the current device; writes its
  * MGB_EP_HANDLE_BYTES-byte CUDA IPC handle when `ipc_handle` is non-null. */
 int moe_ep_shared_alloc(size_t bytes, void** region, void* ipc_handle);
@@ -253,10 +258,31 @@ int moe_ep_dispatch(const void* x, int64_t x_pitch, const int32_t* topk_ids, con
                     void* stream);
 /* Waits until every rank's out rows are complete, then
  * out[t, :] = sum_j topk_weights[t, j] * (owner's out row of slot t * top_k + j)
- * (fp32 accumulate, bf16 out; dropped slots add nothing). */
+ * (fp32 accumulate, bf16 out; dropped slots add nothing).  With `returned`
+ * nonzero the rows are read from this rank's own ret rows instead (row
+ * t * top_k + j), where the owners' W2 launches stored them
+ * (grouped_gemm_offsets_scatter_launch over the origin table). */
 int moe_ep_combine(const int32_t* topk_ids, const float* topk_weights, const int32_t* position, int64_t tokens,
-                   int32_t top_k, const int64_t* peer_regions, const mgb_ep_config* config, void* out,
-                   int64_t out_pitch, void* stream);
+                   int32_t top_k, const int64_t* peer_regions, const mgb_ep_config* config, int32_t returned,
+                   void* out, int64_t out_pitch, void* stream);
+
+/* Aggregate-layout grouped GEMM whose output rows are scattered: row R of the
+ * product (rows of segment e = [offs[e-1], offs[e]), weights B[e % b_count]
+ * or B[e]) is stored at byte dst_offset + (row_origin[R] & 0xFFFFFFFFFF) *
+ * dst_pitch_bytes of rank (row_origin[R] >> 40)'s region, whose base in this
+ * process is peer_regions[rank] (device int64 table of peer_count entries; a
+ * negative origin drops the row, a rank >= peer_count drops it and sets error
+ * bit 8).  The expert-parallel layer's W2 uses it to return each output row
+ * straight to the rank that sent the token, from the GEMM epilogue.
+ * Tensor-core path only (16-byte aligned operands; N * element size a multiple
+ * of 16 bytes); no SwiGLU. */
+int grouped_gemm_offsets_scatter_launch(const void* a, const void* b, const int32_t* offs, int32_t problem_count,
+                                        int32_t b_count, int64_t total_rows, int64_t n, int64_t k, int64_t stride_am,
+                                        int64_t stride_be, int64_t stride_bk, const int64_t* row_origin,
+                                        const int64_t* peer_regions, int32_t peer_count, int64_t dst_offset,
+                                        int64_t dst_pitch_bytes, int32_t dtype, int32_t precision,
+                                        const mgb_tile_config* config, void* scratch, size_t scratch_bytes,
+                                        void* stream, mgb_launch_info* info);
 
 /* Masked single GEMM C[m, n] = A[m, k] @ B[k, n] with arbitrary element strides.
  * Replaces the Triton launch of launch_matmul (kernels/matmul.py:332-392,

@@ -472,6 +472,65 @@ int grouped_gemm_offsets_launch_ex(const void* a, const void* b, void* c, const 
                                tma, config, scratch, scratch_bytes, static_cast<cudaStream_t>(stream), info);
 }
 
+int grouped_gemm_offsets_scatter_launch(const void* a, const void* b, const int32_t* offs, int32_t problem_count,
+                                        int32_t b_count, int64_t total_rows, int64_t n, int64_t k, int64_t stride_am,
+                                        int64_t stride_be, int64_t stride_bk, const int64_t* row_origin,
+                                        const int64_t* peer_regions, int32_t peer_count, int64_t dst_offset,
+                                        int64_t dst_pitch_bytes, int32_t dtype, int32_t precision,
+                                        const mgb_tile_config* config, void* scratch, size_t scratch_bytes,
+                                        void* stream, mgb_launch_info* info) {
+  if (b_count < 0 || !valid_dtype(dtype, precision) || problem_count <= 0 || offs == nullptr || total_rows < 0 ||
+      n <= 0 || k < 0 || stride_am < k || stride_bk < n || stride_be < k * n || row_origin == nullptr ||
+      peer_regions == nullptr || peer_count <= 0 || dst_offset < 0 || dst_offset % 16 != 0 ||
+      dst_pitch_bytes % 16 != 0) {
+    return MGB_ERR_INVALID;
+  }
+  const int es = elem_size(dtype);
+  if ((n * es) % 16 != 0 || dst_pitch_bytes < n * es) return MGB_ERR_INVALID;
+  if (total_rows > 0 && (a == nullptr || b == nullptr)) return MGB_ERR_INVALID;
+  DeviceState ds;
+  if (int st = device_state(&ds)) return st;
+  const auto aligned16 = [](const void* ptr) { return reinterpret_cast<uintptr_t>(ptr) % 16 == 0; };
+  const bool tma = aligned16(a) && aligned16(b) && (stride_am * es) % 16 == 0 && (stride_bk * es) % 16 == 0 &&
+                   (stride_be * es) % 16 == 0 && k < (1ll << 31) && n < (1ll << 31) && total_rows < (1ll << 31);
+  // The scatter epilogue exists on the tensor-core kernels only.
+  if (!tma || k == 0 || (dtype == MGB_FP32 && precision != MGB_TF32)) return MGB_ERR_UNSUPPORTED;
+
+  GroupedParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.offs = offs;
+  p.a = a;
+  p.b = b;
+  p.c = nullptr;  // rows go to their scatter destinations; no C is written
+  p.sam = stride_am;
+  p.sak = 1;
+  p.sbk = stride_bk;
+  p.sbn = 1;
+  p.scm = n;
+  p.scn = 1;
+  p.sbe = stride_be;
+  p.b_count = b_count;
+  p.elem_bytes = es;
+  p.problem_count = problem_count;
+  p.m = total_rows;
+  p.n = n;
+  p.k = k;
+  p.wait_budget = g_wait_budget;
+  p.test_flags = g_test_flags;
+  p.error_word = ds.error_word;
+  p.scatter_origin = row_origin;
+  p.scatter_peers = peer_regions;
+  p.scatter_ranks = peer_count;
+  p.scatter_offset = dst_offset;
+  p.scatter_pitch = dst_pitch_bytes;
+  if (total_rows == 0) {
+    fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0}, 0);
+    return MGB_OK;
+  }
+  return launch_grouped_params(p, ds, TileBound{1, total_rows, problem_count}, total_rows, n, k, dtype, precision,
+                               tma, config, scratch, scratch_bytes, static_cast<cudaStream_t>(stream), info);
+}
+
 int grouped_gemm_fp8_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs,
                             const int64_t* sa_ptrs, const int64_t* sb_ptrs, const int32_t* dims,
                             int32_t problem_count, int32_t homogeneous, int64_t m, int64_t n, int64_t k,

@@ -57,6 +57,17 @@ struct GroupedParams {
   const int64_t* sa_ptrs;
   const int64_t* sb_ptrs;
   int32_t swiglu;         // 1: fused SwiGLU epilogue, C_e[M, N/2] = silu(A_e B_e[:, :N/2]) * (A_e B_e[:, N/2:])
+  // Row-scatter epilogue (aggregate mode, tensor-core kernels, no SwiGLU):
+  // row R of the aggregate C is not written to C but to the region of rank
+  // scatter_origin[R] >> 40 (base scatter_peers[rank], this process's mapping)
+  // at byte scatter_offset + (scatter_origin[R] & 0xFFFFFFFFFF) *
+  // scatter_pitch; a negative origin drops the row.  The expert-parallel layer
+  // uses it to return W2 rows straight to the ranks that sent the tokens.
+  const int64_t* scatter_origin;
+  const int64_t* scatter_peers;
+  int32_t scatter_ranks;  // entries of scatter_peers; an origin naming another rank drops the row
+  int64_t scatter_offset;
+  int64_t scatter_pitch;
   long long wait_budget;  // SM clock cycles a barrier wait may take before the launch gives up
   int32_t test_flags;     // bit 0: make the epilogue wait on a barrier nothing arrives on
   uint32_t* error_word;   // where error bits are OR-ed (a __device__ word of this library)
@@ -64,6 +75,7 @@ struct GroupedParams {
 
 struct Problem {
   int64_t m, n, k;
+  int64_t row0;  // aggregate mode: row of the launch's A / C where the problem starts
   const char* a;
   const char* b;
   char* c;
@@ -72,6 +84,7 @@ struct Problem {
 
 __device__ __forceinline__ Problem load_problem(const GroupedParams& p, int e) {
   Problem q;
+  q.row0 = 0;
   if (p.single) {
     q.m = p.m; q.n = p.n; q.k = p.k;
     q.a = static_cast<const char*>(p.a);
@@ -89,6 +102,7 @@ __device__ __forceinline__ Problem load_problem(const GroupedParams& p, int e) {
     q.a = static_cast<const char*>(p.a) + start * p.sam * es;
     q.b = static_cast<const char*>(p.b) + (p.b_count > 0 ? e % p.b_count : e) * p.sbe * es;
     q.c = static_cast<char*>(p.c) + start * p.scm * es;
+    q.row0 = start;
     q.sam = p.sam; q.sak = 1; q.sbk = p.sbk; q.sbn = 1; q.scm = p.scm; q.scn = 1;
     return q;
   }

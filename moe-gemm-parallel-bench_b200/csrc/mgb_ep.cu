@@ -17,6 +17,10 @@
 //              by local expert, then by source rank, then by slot position
 //   out        rows [capacity][hidden]  the experts' outputs, same order;
 //              the source ranks read their rows back from here
+//   origin     int64 [capacity]  per receive row: source rank << 40 | the
+//              slot's index on the source (written by the dispatch)
+//   ret        rows [max_slots][hidden]  expert outputs returned to this rank
+//              by the owners' W2 epilogues, indexed by slot
 //
 // One forward (all on the caller's stream, no host synchronisation):
 //   moe_route_layout         counts[E], position[slot] (local)
@@ -24,13 +28,17 @@
 //                            send_base and recv_offs from the full table
 //   moe_ep_dispatch          x rows -> owners' recv rows (peer stores); the
 //                            last block signals barrier 1 and waits for it
-//   grouped GEMMs            recv -> (W13, SwiGLU) -> (W2) -> out, per expert
-//   moe_ep_combine           barrier 2; out[t] = sum_j w_tj * owner's out row
+//   grouped GEMMs            recv -> (W13, SwiGLU) -> (W2) -> out, per expert;
+//                            or W2 scattered from its epilogue to the source
+//                            ranks' ret rows (grouped_gemm_offsets_scatter_launch)
+//   moe_ep_combine           barrier 2; out[t] = sum_j w_tj * owner's out row,
+//                            or * this rank's ret row of the slot
 //
 // Reuse is safe without more barriers: a rank writes into a peer's recv rows
 // or counts only after barrier 0 of the next forward, which the peer passes
 // only after finishing its previous forward, and overwrites its own out rows
-// only after barrier 1, which every peer passes only after its combine.
+// (or a peer's ret rows) only after barrier 1, which every peer passes only
+// after its combine.
 // Every wait is bounded by a globaltimer deadline; on expiry the kernel ORs
 // kErrPeerWait into the device error word and returns.
 #include <cuda_bf16.h>
@@ -62,6 +70,7 @@ struct EpArgs {
   int32_t experts;
   int32_t local_experts;
   int64_t capacity;
+  int64_t max_slots;
   int64_t row_bytes;
   mgb_ep_region layout;
   unsigned long long timeout_ns;
@@ -168,34 +177,97 @@ __global__ void __launch_bounds__(1024) ep_exchange_kernel(const int32_t* __rest
   }
 }
 
-// One warp per slot: the token's row goes to the expert owner's receive rows.
-// The block that finishes last signals barrier 1 and waits for every rank.
+// Slots of one token handled together: their row addresses live in registers.
+constexpr int kFan = 8;
+
+// Receive row of slot i on its owner (-1: dropped slot; a slot past capacity
+// also reports when `report`).
+__device__ __forceinline__ int64_t slot_recv_row(const EpArgs& a, const int32_t* send_base, const int32_t* ids,
+                                                 const int32_t* position, int64_t i, bool report) {
+  const int32_t e = ids[i];
+  const int32_t pos = position[i];
+  if (e < 0 || e >= a.experts || pos < 0) return -1;
+  const int64_t row = static_cast<int64_t>(send_base[e]) + pos;
+  if (row >= a.capacity) {
+    if (report) atomicOr(a.err, mgb::kErrCapacity);
+    return -1;
+  }
+  return row;
+}
+
+// Address of slot i's row in its owner's region section `section` (recv or
+// out), or nullptr for a dropped slot.
+__device__ __forceinline__ uint8_t* slot_row(const EpArgs& a, const int32_t* send_base, const int32_t* ids,
+                                             const int32_t* position, int64_t i, int64_t section, int lane) {
+  const int64_t row = slot_recv_row(a, send_base, ids, position, i, lane == 0 && section == a.layout.recv);
+  if (row < 0) return nullptr;
+  return reinterpret_cast<uint8_t*>(region_of(a, ids[i] / a.local_experts) + section) + row * a.row_bytes;
+}
+
+// Where the expert output of kept slot i is read by the combine: the owner's
+// out row, or this rank's ret row i when the owners returned it.
+__device__ __forceinline__ const uint8_t* slot_result(const EpArgs& a, const int32_t* send_base, const int32_t* ids,
+                                                      const int32_t* position, int64_t i, bool returned) {
+  if (!returned) return slot_row(a, send_base, ids, position, i, a.layout.out, 1);
+  if (slot_recv_row(a, send_base, ids, position, i, false) < 0) return nullptr;
+  return reinterpret_cast<const uint8_t*>(region_of(a, a.rank) + a.layout.ret) + i * a.row_bytes;
+}
+
+// One warp per token: its row is read once per group of kFan slots and
+// stored to each slot's row in the expert owner's receive rows (peer stores
+// for remote owners), four 16-byte chunks per lane in flight.  The block
+// that finishes last signals barrier 1 and waits for every rank.
 __global__ void __launch_bounds__(kThreads)
     ep_dispatch_kernel(const uint8_t* __restrict__ x, int64_t x_pitch_bytes, const int32_t* __restrict__ ids,
-                       const int32_t* __restrict__ position, int64_t slots, int32_t top_k, bool vec16, EpArgs a) {
+                       const int32_t* __restrict__ position, int64_t tokens, int32_t top_k, bool vec16, EpArgs a) {
   char* self = region_of(a, a.rank);
   uint32_t* control = reinterpret_cast<uint32_t*>(self);
   const int32_t* send_base = reinterpret_cast<const int32_t*>(self + a.layout.send_base);
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + (threadIdx.x >> 5); i < slots; i += warps) {
-    const int32_t e = ids[i];
-    const int32_t pos = position[i];
-    if (e < 0 || e >= a.experts || pos < 0) continue;
-    const int64_t row = static_cast<int64_t>(send_base[e]) + pos;
-    if (row >= a.capacity) {
-      if (lane == 0) atomicOr(a.err, mgb::kErrCapacity);
-      continue;
-    }
-    const uint8_t* src = x + (i / top_k) * x_pitch_bytes;
-    uint8_t* dst = reinterpret_cast<uint8_t*>(region_of(a, e / a.local_experts) + a.layout.recv) + row * a.row_bytes;
-    if (vec16) {
-      for (int64_t b = lane * 16; b < a.row_bytes; b += 32 * 16) {
-        *reinterpret_cast<uint4*>(dst + b) = *reinterpret_cast<const uint4*>(src + b);
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + (threadIdx.x >> 5); t < tokens; t += warps) {
+    const uint8_t* src = x + t * x_pitch_bytes;
+    for (int j0 = 0; j0 < top_k; j0 += kFan) {
+      uint8_t* dst[kFan];
+#pragma unroll
+      for (int j = 0; j < kFan; ++j) {
+        const int64_t i = t * top_k + j0 + j;
+        const int64_t row = j0 + j < top_k ? slot_recv_row(a, send_base, ids, position, i, lane == 0) : -1;
+        dst[j] = nullptr;
+        if (row >= 0) {
+          char* owner = region_of(a, ids[i] / a.local_experts);
+          dst[j] = reinterpret_cast<uint8_t*>(owner + a.layout.recv) + row * a.row_bytes;
+          // The owner's W2 epilogue returns this row to (this rank, slot i).
+          if (lane == 0) reinterpret_cast<int64_t*>(owner + a.layout.origin)[row] = (static_cast<int64_t>(a.rank) << 40) | i;
+        }
       }
-    } else {
-      for (int64_t b = lane * 2; b < a.row_bytes; b += 32 * 2) {
-        *reinterpret_cast<uint16_t*>(dst + b) = *reinterpret_cast<const uint16_t*>(src + b);
+      if (vec16) {
+        constexpr int kBatch = 4;
+        for (int64_t b0 = lane * 16; b0 < a.row_bytes; b0 += kBatch * 32 * 16) {
+          uint4 v[kBatch];
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            const int64_t b = b0 + u * 32 * 16;
+            if (b < a.row_bytes) v[u] = *reinterpret_cast<const uint4*>(src + b);
+          }
+#pragma unroll
+          for (int j = 0; j < kFan; ++j) {
+            if (dst[j] == nullptr) continue;
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+              const int64_t b = b0 + u * 32 * 16;
+              if (b < a.row_bytes) *reinterpret_cast<uint4*>(dst[j] + b) = v[u];
+            }
+          }
+        }
+      } else {
+        for (int64_t b = lane * 2; b < a.row_bytes; b += 32 * 2) {
+          const uint16_t v = *reinterpret_cast<const uint16_t*>(src + b);
+#pragma unroll
+          for (int j = 0; j < kFan; ++j) {
+            if (dst[j] != nullptr) *reinterpret_cast<uint16_t*>(dst[j] + b) = v;
+          }
+        }
       }
     }
   }
@@ -219,37 +291,56 @@ __global__ void ep_barrier_kernel(EpArgs a, int phase) {
 }
 
 // One warp per token: fp32 weighted sum of the token's expert outputs, read
-// from the owners' out rows; bf16 result.
+// from the owners' out rows (peer loads for remote owners); bf16 result.
+// Each lane loads its 16-byte chunk of all the group's slots before summing,
+// so kFan loads per lane are in flight.
 __global__ void __launch_bounds__(kThreads)
     ep_combine_kernel(const int32_t* __restrict__ ids, const float* __restrict__ weights,
                       const int32_t* __restrict__ position, int64_t tokens, int32_t top_k,
-                      __nv_bfloat16* __restrict__ out, int64_t out_pitch, int64_t hidden, bool vec8, EpArgs a) {
+                      __nv_bfloat16* __restrict__ out, int64_t out_pitch, int64_t hidden, bool vec8, bool returned,
+                      EpArgs a) {
   const char* self = region_of(a, a.rank);
   const int32_t* send_base = reinterpret_cast<const int32_t*>(self + a.layout.send_base);
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + (threadIdx.x >> 5); t < tokens; t += warps) {
     __nv_bfloat16* dst = out + t * out_pitch;
+    const bool one_group = top_k <= kFan;
+    const uint8_t* src[kFan];
+    float w[kFan];
+    if (one_group) {
+#pragma unroll
+      for (int j = 0; j < kFan; ++j) {
+        src[j] = j < top_k ? slot_result(a, send_base, ids, position, t * top_k + j, returned) : nullptr;
+        w[j] = src[j] != nullptr ? weights[t * top_k + j] : 0.f;
+      }
+    }
     if (vec8) {
       for (int64_t c = lane * 8; c < hidden; c += 32 * 8) {
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int j = 0; j < top_k; ++j) {
-          const int64_t i = t * top_k + j;
-          const int32_t e = ids[i];
-          const int32_t pos = position[i];
-          if (e < 0 || e >= a.experts || pos < 0) continue;
-          const int64_t row = static_cast<int64_t>(send_base[e]) + pos;
-          if (row >= a.capacity) continue;
-          const __nv_bfloat16* y = reinterpret_cast<const __nv_bfloat16*>(
-              region_of(a, e / a.local_experts) + a.layout.out + row * a.row_bytes);
-          const uint4 raw = __ldcg(reinterpret_cast<const uint4*>(y + c));
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
-          const float w = weights[i];
+        for (int j0 = 0; j0 < top_k; j0 += kFan) {
+          if (!one_group) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 f = __bfloat1622float2(h[q]);
-            acc[2 * q] = fmaf(w, f.x, acc[2 * q]);
-            acc[2 * q + 1] = fmaf(w, f.y, acc[2 * q + 1]);
+            for (int j = 0; j < kFan; ++j) {
+              src[j] = j0 + j < top_k ? slot_result(a, send_base, ids, position, t * top_k + j0 + j, returned)
+                                      : nullptr;
+              w[j] = src[j] != nullptr ? weights[t * top_k + j0 + j] : 0.f;
+            }
+          }
+          uint4 raw[kFan];
+#pragma unroll
+          for (int j = 0; j < kFan; ++j) {
+            raw[j] = src[j] != nullptr ? __ldcg(reinterpret_cast<const uint4*>(src[j] + c * 2)) : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int j = 0; j < kFan; ++j) {
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float2 f = __bfloat1622float2(h[q]);
+              acc[2 * q] = fmaf(w[j], f.x, acc[2 * q]);
+              acc[2 * q + 1] = fmaf(w[j], f.y, acc[2 * q + 1]);
+            }
           }
         }
         uint4 packed;
@@ -262,15 +353,10 @@ __global__ void __launch_bounds__(kThreads)
       for (int64_t c = lane; c < hidden; c += 32) {
         float acc = 0.f;
         for (int j = 0; j < top_k; ++j) {
-          const int64_t i = t * top_k + j;
-          const int32_t e = ids[i];
-          const int32_t pos = position[i];
-          if (e < 0 || e >= a.experts || pos < 0) continue;
-          const int64_t row = static_cast<int64_t>(send_base[e]) + pos;
-          if (row >= a.capacity) continue;
-          const __nv_bfloat16* y = reinterpret_cast<const __nv_bfloat16*>(
-              region_of(a, e / a.local_experts) + a.layout.out + row * a.row_bytes);
-          acc = fmaf(weights[i], __bfloat162float(y[c]), acc);
+          const uint8_t* y = slot_result(a, send_base, ids, position, t * top_k + j, returned);
+          if (y != nullptr) {
+            acc = fmaf(weights[t * top_k + j], __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(y)[c]), acc);
+          }
         }
         dst[c] = __float2bfloat16_rn(acc);
       }
@@ -292,12 +378,13 @@ int make_args(const mgb_ep_config* cfg, const int64_t* peer_regions, EpArgs* a) 
   if (cfg == nullptr || peer_regions == nullptr) return MGB_ERR_INVALID;
   if (cfg->world <= 0 || cfg->world > MGB_EP_MAX_WORLD || cfg->rank < 0 || cfg->rank >= cfg->world ||
       cfg->num_experts <= 0 || cfg->num_experts > kMaxExperts || cfg->num_experts % cfg->world != 0 ||
-      cfg->hidden <= 0 || cfg->capacity < 0 || cfg->capacity >= (1ll << 31) || cfg->elem_bytes != 2) {
+      cfg->hidden <= 0 || cfg->capacity < 0 || cfg->capacity >= (1ll << 31) || cfg->elem_bytes != 2 ||
+      cfg->max_slots < 0 || cfg->max_slots >= (1ll << 40)) {
     return MGB_ERR_INVALID;
   }
   std::memset(a, 0, sizeof(*a));
-  if (moe_ep_region_layout(cfg->world, cfg->num_experts, cfg->hidden, cfg->capacity, cfg->elem_bytes, &a->layout) !=
-      MGB_OK) {
+  if (moe_ep_region_layout(cfg->world, cfg->num_experts, cfg->hidden, cfg->capacity, cfg->max_slots,
+                           cfg->elem_bytes, &a->layout) != MGB_OK) {
     return MGB_ERR_INVALID;
   }
   a->err = mgb::current_error_word();
@@ -308,6 +395,7 @@ int make_args(const mgb_ep_config* cfg, const int64_t* peer_regions, EpArgs* a) 
   a->experts = cfg->num_experts;
   a->local_experts = cfg->num_experts / cfg->world;
   a->capacity = cfg->capacity;
+  a->max_slots = cfg->max_slots;
   a->row_bytes = cfg->hidden * cfg->elem_bytes;
   a->timeout_ns = static_cast<unsigned long long>(cfg->timeout_ns > 0 ? cfg->timeout_ns : kDefaultTimeoutNs);
   return MGB_OK;
@@ -317,10 +405,10 @@ int make_args(const mgb_ep_config* cfg, const int64_t* peer_regions, EpArgs* a) 
 
 extern "C" {
 
-int moe_ep_region_layout(int32_t world, int32_t num_experts, int64_t hidden, int64_t capacity, int32_t elem_bytes,
-                         mgb_ep_region* layout) {
+int moe_ep_region_layout(int32_t world, int32_t num_experts, int64_t hidden, int64_t capacity, int64_t max_slots,
+                         int32_t elem_bytes, mgb_ep_region* layout) {
   if (layout == nullptr || world <= 0 || world > MGB_EP_MAX_WORLD || num_experts <= 0 ||
-      num_experts % world != 0 || hidden <= 0 || capacity < 0 || elem_bytes <= 0) {
+      num_experts % world != 0 || hidden <= 0 || capacity < 0 || max_slots < 0 || elem_bytes <= 0) {
     return MGB_ERR_INVALID;
   }
   mgb_ep_region r;
@@ -329,7 +417,9 @@ int moe_ep_region_layout(int32_t world, int32_t num_experts, int64_t hidden, int
   r.recv_offs = align_up(r.send_base + 4ll * num_experts, 256);
   r.recv = align_up(r.recv_offs + 4ll * (num_experts / world), 1024);
   r.out = align_up(r.recv + capacity * hidden * elem_bytes, 1024);
-  r.bytes = align_up(r.out + capacity * hidden * elem_bytes, 1024);
+  r.origin = align_up(r.out + capacity * hidden * elem_bytes, 1024);
+  r.ret = align_up(r.origin + capacity * 8, 1024);
+  r.bytes = align_up(r.ret + max_slots * hidden * elem_bytes, 1024);
   *layout = r;
   return MGB_OK;
 }
@@ -390,23 +480,26 @@ int moe_ep_dispatch(const void* x, int64_t x_pitch, const int32_t* topk_ids, con
                     void* stream) {
   EpArgs a;
   if (int st = make_args(config, peer_regions, &a)) return st;
-  if (tokens < 0 || top_k <= 0 || x_pitch < config->hidden) return MGB_ERR_INVALID;
+  if (tokens < 0 || top_k <= 0 || x_pitch < config->hidden || tokens * top_k > config->max_slots) {
+    return MGB_ERR_INVALID;
+  }
   if (tokens > 0 && (x == nullptr || topk_ids == nullptr || position == nullptr)) return MGB_ERR_INVALID;
-  const int64_t slots = tokens * top_k;
   const int64_t pitch_bytes = x_pitch * config->elem_bytes;
   const bool vec16 = aligned16(x) && a.row_bytes % 16 == 0 && pitch_bytes % 16 == 0;
   // Launched even without slots: every rank takes part in barrier 1.
-  ep_dispatch_kernel<<<grid_for(slots, kThreads / 32), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(x), pitch_bytes, topk_ids, position, slots, top_k, vec16, a);
+  ep_dispatch_kernel<<<grid_for(tokens, kThreads / 32), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(x), pitch_bytes, topk_ids, position, tokens, top_k, vec16, a);
   return cudaGetLastError() == cudaSuccess ? MGB_OK : MGB_ERR_CUDA;
 }
 
 int moe_ep_combine(const int32_t* topk_ids, const float* topk_weights, const int32_t* position, int64_t tokens,
-                   int32_t top_k, const int64_t* peer_regions, const mgb_ep_config* config, void* out,
-                   int64_t out_pitch, void* stream) {
+                   int32_t top_k, const int64_t* peer_regions, const mgb_ep_config* config, int32_t returned,
+                   void* out, int64_t out_pitch, void* stream) {
   EpArgs a;
   if (int st = make_args(config, peer_regions, &a)) return st;
-  if (tokens < 0 || top_k <= 0 || out_pitch < config->hidden) return MGB_ERR_INVALID;
+  if (tokens < 0 || top_k <= 0 || out_pitch < config->hidden || tokens * top_k > config->max_slots) {
+    return MGB_ERR_INVALID;
+  }
   if (tokens > 0 && (topk_ids == nullptr || topk_weights == nullptr || position == nullptr || out == nullptr)) {
     return MGB_ERR_INVALID;
   }
@@ -417,7 +510,7 @@ int moe_ep_combine(const int32_t* topk_ids, const float* topk_weights, const int
   const bool vec8 = aligned16(out) && config->hidden % 8 == 0 && out_pitch % 8 == 0;
   ep_combine_kernel<<<grid_for(tokens, kThreads / 32), kThreads, 0, s>>>(
       topk_ids, topk_weights, position, tokens, top_k, static_cast<__nv_bfloat16*>(out), out_pitch,
-      config->hidden, vec8, a);
+      config->hidden, vec8, returned != 0, a);
   return cudaGetLastError() == cudaSuccess ? MGB_OK : MGB_ERR_CUDA;
 }
 

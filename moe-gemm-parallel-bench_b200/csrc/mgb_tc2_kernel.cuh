@@ -272,7 +272,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       if (q.k <= 0) {
         for (int idx = ethread; idx < Cfg::kHalf * tile_out; idx += 128) {
           const int64_t row = m0 + idx / tile_out, col = n0 + idx % tile_out;
-          if (row < q.m && col < q.n) store_scalar<T>(q.c, row * q.scm + col * q.scn, 0.0f);
+          if (row < q.m && col < q.n) {
+            if (p.scatter_origin != nullptr) {
+              char* d = scatter_row(p, q, row);
+              if (d != nullptr) store_scalar<T>(d, col, 0.0f);
+            } else {
+              store_scalar<T>(q.c, row * q.scm + col * q.scn, 0.0f);
+            }
+          }
         }
         continue;
       }
@@ -294,6 +301,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         } else {
           store_rows_scalar_swiglu<T, Cfg::kTileN / 2>(q, taddr, m0 + quarter * 32, n0, lane);
         }
+      } else if (p.scatter_origin != nullptr) {
+        store_rows_scatter<T, Cfg::kTileN>(p, q, taddr, m0 + quarter * 32, n0, my_blocks, lane);
       } else if (cmap != nullptr) {
         store_rows_tma<T, Cfg::kTileN, Cfg::kEpiBlocks>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),
                                        static_cast<int32_t>(n0), my_blocks, lane, chunk_seq, pol_out, p.error_word);

@@ -193,6 +193,21 @@ __device__ __forceinline__ uint32_t pack_pair(uint32_t lo_bits, uint32_t hi_bits
   }
 }
 
+// Scatter-mode destination of row `row` of problem q (nullptr: dropped row or
+// past the problem's rows); see GroupedParams::scatter_origin.
+__device__ __forceinline__ char* scatter_row(const GroupedParams& p, const Problem& q, int64_t row) {
+  if (row < 0 || row >= q.m) return nullptr;
+  const int64_t origin = p.scatter_origin[q.row0 + row];
+  if (origin < 0) return nullptr;
+  const int64_t rank = origin >> 40;
+  if (rank >= p.scatter_ranks) {
+    atomicOr(p.error_word, kErrBadStore);
+    return nullptr;
+  }
+  return reinterpret_cast<char*>(static_cast<uintptr_t>(p.scatter_peers[rank])) + p.scatter_offset +
+         (origin & 0xFFFFFFFFFFll) * p.scatter_pitch;
+}
+
 // One 128-byte-per-row chunk of a warp's 32 accumulator rows (TMEM lanes):
 // loads columns [col0, col0 + 128 / sizeof(T)), converts them and writes row
 // `lane` of the 32 x 128-byte block `block` with its 16-byte units rotated by
@@ -302,6 +317,50 @@ __device__ __forceinline__ void store_rows_tma(const Problem& q, const void* cma
     }
   }
   seq += static_cast<uint32_t>(chunks);
+}
+
+// Row-tile epilogue of one warp in scatter mode: as store_rows_tma, but each
+// staged 32 x 128-byte chunk is written by the warp itself, row by row, to the
+// row's own destination (scatter_row; peer memory for rows returned to other
+// ranks): 8 lanes per 128-byte row segment, 4 rows per store instruction.
+// Columns must be a multiple of 8 elements (16 bytes).
+template <typename T, int TN>
+__device__ __forceinline__ void store_rows_scatter(const GroupedParams& p, const Problem& q, uint32_t taddr,
+                                                   int64_t row0, int64_t n0, uint8_t* block, int lane) {
+  constexpr int kChunkCols = 128 / static_cast<int>(sizeof(T));
+  constexpr int kUnits = kChunkCols / 32;
+  constexpr int kTotal = TN / 32;
+  if (row0 >= q.m) return;
+  const int64_t cols_left = q.n - n0;
+  const int chunks = cols_left >= TN ? TN / kChunkCols : static_cast<int>((cols_left + kChunkCols - 1) / kChunkCols);
+  const int units = chunks * kUnits;
+  char* my_dst = scatter_row(p, q, row0 + lane);
+  uint32_t v[2][32];
+  tmem_ld32(taddr, v[0]);
+#pragma unroll
+  for (int g = 0; g < kTotal; ++g) {
+    if (g >= units) break;
+    const int c = g / kUnits;
+    const int u = g % kUnits;
+    tmem_ld_wait();
+    if (g + 1 < units) tmem_ld32(taddr + (g + 1) * 32, v[(g + 1) & 1]);
+    write_unit_smem<T>(v[g & 1], block, lane, u);
+    if (u == kUnits - 1) {
+      __syncwarp();
+      const int piece = lane & 7;  // 16-byte piece of a 128-byte row segment
+      const int64_t col = n0 + c * kChunkCols + piece * (16 / static_cast<int>(sizeof(T)));
+#pragma unroll
+      for (int it = 0; it < 8; ++it) {
+        const int r = it * 4 + (lane >> 3);
+        const uint64_t d = __shfl_sync(0xffffffffu, reinterpret_cast<uint64_t>(my_dst), r);
+        if (d != 0 && col < q.n) {
+          const uint4 val = *reinterpret_cast<const uint4*>(block + r * 128 + ((piece ^ (r & 7)) << 4));
+          *reinterpret_cast<uint4*>(reinterpret_cast<char*>(d) + col * static_cast<int64_t>(sizeof(T))) = val;
+        }
+      }
+      __syncwarp();  // every lane has read the block before it is written again
+    }
+  }
 }
 
 // Row-tile SwiGLU epilogue of one warp through TMA: gate accumulators are
@@ -515,7 +574,7 @@ __global__ void __launch_bounds__(32)
         tmap_replace_stride1(&staging[1], static_cast<uint64_t>(q.sbk) * sizeof(T));
       }
     }
-    if (sane && c_tma_legal<T>(q, out_cols(p, q))) {
+    if (sane && p.scatter_origin == nullptr && c_tma_legal<T>(q, out_cols(p, q))) {
       tmap_replace_address(&staging[2], q.c);
       if (!p.homogeneous) {
         tmap_replace_dim(&staging[2], 0, static_cast<uint32_t>(out_cols(p, q)));
@@ -752,7 +811,14 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (q.k <= 0) {
         for (int idx = ethread; idx < TM * tile_out; idx += 128) {
           const int64_t row = m0 + idx / tile_out, col = n0 + idx % tile_out;
-          if (row < q.m && col < q.n) store_scalar<T>(q.c, row * q.scm + col * q.scn, 0.0f);
+          if (row < q.m && col < q.n) {
+            if (p.scatter_origin != nullptr) {
+              char* d = scatter_row(p, q, row);
+              if (d != nullptr) store_scalar<T>(d, col, 0.0f);
+            } else {
+              store_scalar<T>(q.c, row * q.scm + col * q.scn, 0.0f);
+            }
+          }
         }
         continue;
       }
@@ -806,7 +872,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             uint32_t r[16];
             tmem_ld16(taddr + c * TM + j * 16, r);
             tmem_ld_wait();
-            if (col < q.n) {
+            if (p.scatter_origin != nullptr) {
+              // Lane i of the warp resolves row j * 16 + i's destination once.
+              char* mine = lane < 16 ? scatter_row(p, q, m0 + j * 16 + lane) : nullptr;
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                const uint64_t d = __shfl_sync(0xffffffffu, reinterpret_cast<uint64_t>(mine), i);
+                if (d != 0 && col < q.n) store_scalar<T>(reinterpret_cast<char*>(d), col, __uint_as_float(r[i]));
+              }
+            } else if (col < q.n) {
 #pragma unroll
               for (int i = 0; i < 16; ++i) {
                 const int64_t row = m0 + j * 16 + i;
@@ -828,6 +902,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             done = true;
           }
+        }
+        if (!done && p.scatter_origin != nullptr) {
+          store_rows_scatter<T, TN>(p, q, taddr, m0 + quarter * 32, n0, my_blocks, lane);
+          done = true;
         }
         if (!done) {
           if (cmap != nullptr) {

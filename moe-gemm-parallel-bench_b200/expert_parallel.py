@@ -14,9 +14,13 @@ GPU:
     W13        grouped GEMM, fused SiLU(gate) * up epilogue, over the receive
                rows in the aggregate layout (offs = per-expert row ends on the
                device, so no host synchronisation)
-    W2         grouped GEMM into the region's out rows
-    combine    moe_ep_combine: every token reads its k expert outputs back
-               from the owners' out rows (peer loads) and sums them weighted
+    W2         grouped GEMM whose epilogue stores every output row straight
+               into the source rank's return rows (peer stores from the GEMM
+               epilogue, row destinations from the origin table the dispatch
+               wrote), so the return crosses NVLink while W2 still computes
+    combine    moe_ep_combine: every token sums its k returned rows
+               (local), weighted; with ``fused_return=False`` W2 writes the
+               owner's out rows and the combine reads them (peer loads)
 
 Rank r owns experts [r E / P, (r + 1) E / P) (utils/metrics.py:40-72 EP
 split).  Each rank's region is a plain device allocation mapped by its peers
@@ -36,7 +40,7 @@ except ImportError:  # pragma: no cover - host helpers stay importable
     dist = None
 
 from kernels import _native
-from kernels.grouped_gemm import check_device_errors, launch_grouped_mm
+from kernels.grouped_gemm import check_device_errors, launch_grouped_mm, launch_grouped_mm_scatter
 from kernels.matmul import KernelConfig, native_candidates
 
 
@@ -86,11 +90,13 @@ class ExpertParallelMoE:
     (receive rows, default ``ep_capacity``) may be set lower to save memory,
     in which case slots beyond it are dropped and reported.  ``group`` is the
     process group of the P ranks (None: the default group, or a single rank
-    when torch.distributed is not initialised).
+    when torch.distributed is not initialised).  ``fused_return`` selects the
+    W2 epilogue that returns rows to the source ranks (default) over the
+    combine that pulls them.
     """
 
     def __init__(self, w13, w2, num_experts: int, *, max_tokens: int, top_k: int, group=None,
-                 capacity: int | None = None, timeout_s: float = 10.0):
+                 capacity: int | None = None, timeout_s: float = 10.0, fused_return: bool = True):
         if torch is None or not torch.cuda.is_available():
             raise RuntimeError("CUDA PyTorch and the native sm_100a library are required")
         _native.load()
@@ -119,9 +125,11 @@ class ExpertParallelMoE:
         self.hidden, self.ffn = hidden, two_f // 2
         self.max_tokens, self.top_k = max_tokens, top_k
         self.capacity = ep_capacity(max_tokens, top_k, self.world) if capacity is None else int(capacity)
+        self.max_slots = max_tokens * top_k
+        self.fused_return = bool(fused_return)
         self.config = _native.EpConfig(self.rank, self.world, num_experts, 2, hidden, self.capacity,
-                                       int(timeout_s * 1e9))
-        self.region = _native.ep_region_layout(self.world, num_experts, hidden, self.capacity, 2)
+                                       int(timeout_s * 1e9), self.max_slots)
+        self.region = _native.ep_region_layout(self.world, num_experts, hidden, self.capacity, self.max_slots, 2)
         self._peer_ptrs: list[int] = []
         self._base = 0
         with torch.cuda.device(self.device):
@@ -139,6 +147,7 @@ class ExpertParallelMoE:
             self.out_rows = _view(self._base + self.region.out, (rows, hidden), "<i2", self.device).view(torch.bfloat16)
             self.recv_offs = _view(self._base + self.region.recv_offs, (local,), "<i4", self.device)
             self.send_base = _view(self._base + self.region.send_base, (num_experts,), "<i4", self.device)
+            self.origin = _view(self._base + self.region.origin, (rows,), "<i8", self.device)
             self.hidden_rows = torch.empty((rows, self.ffn), dtype=torch.bfloat16, device=self.device)
             self.counts = torch.zeros(num_experts, dtype=torch.int32, device=self.device)
             self.position = torch.empty(max(1, max_tokens * top_k), dtype=torch.int32, device=self.device)
@@ -191,14 +200,19 @@ class ExpertParallelMoE:
                 launch_grouped_mm(self.recv, self.w13, self.recv_offs, self.hidden_rows, swiglu=True, config=cfg13)
                 if marks:
                     marks.pop(0).record()
-                launch_grouped_mm(self.hidden_rows, self.w2, self.recv_offs, self.out_rows, config=cfg2)
+                if self.fused_return:
+                    launch_grouped_mm_scatter(self.hidden_rows, self.w2, self.recv_offs, self.origin, self.peers,
+                                              self.region.ret, self.hidden * 2, config=cfg2)
+                else:
+                    launch_grouped_mm(self.hidden_rows, self.w2, self.recv_offs, self.out_rows, config=cfg2)
             elif marks:
                 marks.pop(0).record()
             if marks:
                 marks.pop(0).record()
             _native.ep_combine(topk_ids.data_ptr(), topk_weights.data_ptr(), self.position.data_ptr(), tokens,
                                self.top_k, self.peers.data_ptr(), self.config, out.data_ptr(),
-                               out.stride(0) if tokens else self.hidden, stream)
+                               out.stride(0) if tokens else self.hidden, stream,
+                               returned=self.fused_return and self.capacity > 0)
             if marks:
                 marks.pop(0).record()
         return out
@@ -226,7 +240,7 @@ class ExpertParallelMoE:
                 if r != self.rank:
                     _native.ep_peer_close(ptr)
             self._peer_ptrs = []
-            for name in ("recv", "out_rows", "recv_offs", "send_base"):
+            for name in ("recv", "out_rows", "recv_offs", "send_base", "origin"):
                 self.__dict__.pop(name, None)
             _native.ep_shared_free(self._base)
             self._base = 0

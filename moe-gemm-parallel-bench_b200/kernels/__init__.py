@@ -12,6 +12,7 @@ from .grouped_gemm import (
     build_grouped_workspace,
     last_aggregate_launch_info,
     launch_grouped_mm,
+    launch_grouped_mm_scatter,
     check_device_errors,
     grouped_candidate_configs,
     launch_grouped,
@@ -47,6 +48,7 @@ __all__ = [
     "build_fused_swiglu_workspace",
     "last_aggregate_launch_info",
     "launch_grouped_mm",
+    "launch_grouped_mm_scatter",
     "build_grouped_workspace",
     "check_device_errors",
     "grouped_candidate_configs",

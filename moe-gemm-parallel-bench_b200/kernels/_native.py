@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "grouped_gemm_swiglu_launch",
     "grouped_gemm_offsets_launch",
     "grouped_gemm_offsets_launch_ex",
+    "grouped_gemm_offsets_scatter_launch",
     "moe_route_layout",
     "moe_permute",
     "moe_combine",
@@ -118,6 +119,7 @@ class EpConfig(ctypes.Structure):
         ("hidden", ctypes.c_int64),
         ("capacity", ctypes.c_int64),
         ("timeout_ns", ctypes.c_int64),
+        ("max_slots", ctypes.c_int64),
     ]
 
 
@@ -130,6 +132,8 @@ class EpRegion(ctypes.Structure):
         ("recv_offs", ctypes.c_int64),
         ("recv", ctypes.c_int64),
         ("out", ctypes.c_int64),
+        ("origin", ctypes.c_int64),
+        ("ret", ctypes.c_int64),
         ("bytes", ctypes.c_int64),
     ]
 
@@ -190,7 +194,7 @@ def _declare(lib) -> None:
                                 ctypes.c_void_p, ctypes.c_int64, ctypes.c_void_p]
     lib.moe_combine.restype = ctypes.c_int
     lib.moe_ep_region_layout.argtypes = [ctypes.c_int32, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64,
-                                         ctypes.c_int32, ctypes.POINTER(EpRegion)]
+                                         ctypes.c_int64, ctypes.c_int32, ctypes.POINTER(EpRegion)]
     lib.moe_ep_region_layout.restype = ctypes.c_int
     lib.moe_ep_shared_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p), ctypes.c_void_p]
     lib.moe_ep_shared_alloc.restype = ctypes.c_int
@@ -206,8 +210,16 @@ def _declare(lib) -> None:
                                     ctypes.c_int32, ctypes.c_void_p, ctypes.POINTER(EpConfig), ctypes.c_void_p]
     lib.moe_ep_dispatch.restype = ctypes.c_int
     lib.moe_ep_combine.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32,
-                                   ctypes.c_void_p, ctypes.POINTER(EpConfig), ctypes.c_void_p, ctypes.c_int64,
-                                   ctypes.c_void_p]
+                                   ctypes.c_void_p, ctypes.POINTER(EpConfig), ctypes.c_int32, ctypes.c_void_p,
+                                   ctypes.c_int64, ctypes.c_void_p]
+    lib.grouped_gemm_offsets_scatter_launch.argtypes = [
+        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+        ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64, ctypes.c_int32, ctypes.c_int32,
+        ctypes.POINTER(TileConfig),
+        ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p, ctypes.POINTER(LaunchInfo),
+    ]
+    lib.grouped_gemm_offsets_scatter_launch.restype = ctypes.c_int
     lib.moe_ep_combine.restype = ctypes.c_int
     lib.grouped_gemm_fp8_launch.argtypes = [
         c_i64p, c_i64p, c_i64p, c_i64p, c_i64p, ctypes.c_void_p, ctypes.c_int32, ctypes.c_int32, ctypes.c_int64,
@@ -342,10 +354,11 @@ def combine(y: int, y_pitch: int, topk_ids: int, weights: int, position: int, of
                               int(num_experts), int(hidden), out, int(out_pitch), stream), "moe_combine")
 
 
-def ep_region_layout(world: int, num_experts: int, hidden: int, capacity: int, elem_bytes: int) -> EpRegion:
+def ep_region_layout(world: int, num_experts: int, hidden: int, capacity: int, max_slots: int,
+                     elem_bytes: int) -> EpRegion:
     region = EpRegion()
-    _check(load().moe_ep_region_layout(int(world), int(num_experts), int(hidden), int(capacity), int(elem_bytes),
-                                       ctypes.byref(region)), "moe_ep_region_layout")
+    _check(load().moe_ep_region_layout(int(world), int(num_experts), int(hidden), int(capacity), int(max_slots),
+                                       int(elem_bytes), ctypes.byref(region)), "moe_ep_region_layout")
     return region
 
 
@@ -386,9 +399,28 @@ def ep_dispatch(x: int, x_pitch: int, topk_ids: int, position: int, tokens: int,
 
 
 def ep_combine(topk_ids: int, weights: int, position: int, tokens: int, top_k: int, peers: int, config: EpConfig,
-               out: int, out_pitch: int, stream: int) -> None:
+               out: int, out_pitch: int, stream: int, returned: bool = False) -> None:
     _check(load().moe_ep_combine(topk_ids, weights, position, int(tokens), int(top_k), peers, ctypes.byref(config),
-                                 out, int(out_pitch), stream), "moe_ep_combine")
+                                 int(bool(returned)), out, int(out_pitch), stream), "moe_ep_combine")
+
+
+def offsets_scatter_launch(
+    a: int, b: int, offs: int, problem_count: int, b_count: int, total_rows: int, n: int, k: int, stride_am: int,
+    stride_be: int, stride_bk: int, row_origin: int, peers: int, peer_count: int, dst_offset: int,
+    dst_pitch_bytes: int, dtype: str, precision: str, config, scratch: int, scratch_nbytes: int, stream: int,
+) -> LaunchInfo:
+    """grouped_gemm_offsets_scatter_launch: aggregate-layout GEMM whose rows
+    are stored at per-row destinations (see the C header)."""
+    info = LaunchInfo()
+    cfg = tile_config(config)
+    status = load().grouped_gemm_offsets_scatter_launch(
+        a, b, offs, int(problem_count), int(b_count), int(total_rows), int(n), int(k), int(stride_am),
+        int(stride_be), int(stride_bk), row_origin, peers, int(peer_count), int(dst_offset), int(dst_pitch_bytes),
+        DTYPE_CODES[dtype], PRECISION_CODES[precision], ctypes.byref(cfg), scratch, int(scratch_nbytes), stream,
+        ctypes.byref(info),
+    )
+    _check(status, "grouped_gemm_offsets_scatter_launch")
+    return info
 
 
 def fp8_launch(

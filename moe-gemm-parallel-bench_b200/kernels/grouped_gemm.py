@@ -516,6 +516,42 @@ def launch_grouped_mm(mat_a, mat_b, offs, out=None, *, config: KernelConfig | No
     return out
 
 
+def launch_grouped_mm_scatter(mat_a, mat_b, offs, row_origin, peer_regions, dst_offset: int, dst_pitch_bytes: int,
+                              *, config: KernelConfig | None = None, input_precision: str = "ieee") -> None:
+    """``launch_grouped_mm`` whose output rows are not written to an ``out``
+    matrix but each to its own destination: row R goes to byte ``dst_offset +
+    (row_origin[R] & (2**40 - 1)) * dst_pitch_bytes`` of the region whose base
+    is ``peer_regions[row_origin[R] >> 40]`` (int64 device tables; a negative
+    origin drops the row).  The expert-parallel layer returns W2 rows to the
+    ranks that sent the tokens this way, from the GEMM epilogue."""
+    if torch is None or not torch.cuda.is_available():
+        raise RuntimeError("CUDA PyTorch and the native sm_100a library are required")
+    _native.load()
+    total, k = mat_a.shape
+    experts, kb, n = mat_b.shape
+    segments = offs.shape[0]
+    if kb != k or experts == 0 or segments == 0 or segments % experts or offs.dtype != torch.int32:
+        raise ValueError(f"shape mismatch: mat_a={tuple(mat_a.shape)}, mat_b={tuple(mat_b.shape)}, offs={tuple(offs.shape)}")
+    if row_origin.dtype != torch.int64 or row_origin.numel() < total or peer_regions.dtype != torch.int64:
+        raise ValueError("row_origin must be int64 with a row per row of mat_a; peer_regions int64")
+    if mat_a.stride(1) != 1 or mat_b.stride(2) != 1 or mat_b.stride(0) < k * mat_b.stride(1):
+        raise ValueError("columns of mat_a and mat_b must be contiguous")
+    key = (mat_a.device.index or 0, segments)
+    scratch = _AGGREGATE_SCRATCH.get(key)
+    if scratch is None:
+        scratch = torch.empty(_native.scratch_bytes(segments, 0), dtype=torch.uint8, device=mat_a.device)
+        _AGGREGATE_SCRATCH[key] = scratch
+    cfg = config or native_candidates(max(1, -(-total // segments)), k)[0]
+    with torch.cuda.device(mat_a.device):
+        _native.offsets_scatter_launch(
+            mat_a.data_ptr(), mat_b.data_ptr(), offs.data_ptr(), segments,
+            experts if segments != experts else 0, total, n, k, mat_a.stride(0), mat_b.stride(0), mat_b.stride(1),
+            row_origin.data_ptr(), peer_regions.data_ptr(), peer_regions.numel(), dst_offset, dst_pitch_bytes,
+            dtype_name(mat_a.dtype),
+            input_precision, cfg, scratch.data_ptr(), scratch.numel(), torch.cuda.current_stream(mat_a.device).cuda_stream,
+        )
+
+
 def check_device_errors(device=None) -> None:
     """Synchronises ``device`` and raises RuntimeError if a native kernel
     reported a device-side failure (bounded wait expiry, skipped problem)."""

@@ -184,15 +184,16 @@ def _to_gpu(x, w13, w2, ids, w, device="cuda"):
     (64, 8, 256, 192, 2, {"drop": 0.25}),
     (300, 32, 1024, 512, 8, {}),
 ])
+@pytest.mark.parametrize("fused_return", [True, False])
 @pytest.mark.gpu
 @pytest.mark.skipif(not cuda_ready(), reason="needs a CUDA GPU")
-def test_single_rank_layer_matches_oracle(tokens, experts, hidden, ffn, top_k, routing):
+def test_single_rank_layer_matches_oracle(tokens, experts, hidden, ffn, top_k, routing, fused_return):
     _setup_paths()
     from expert_parallel import ExpertParallelMoE
 
     x, w13, w2, ids, w = _layer_case(1, tokens, experts, hidden, ffn, top_k, **routing)
     gx, g13, g2, gids, gw = _to_gpu(x, w13, w2, ids, w)
-    with ExpertParallelMoE(g13, g2, experts, max_tokens=tokens, top_k=top_k) as layer:
+    with ExpertParallelMoE(g13, g2, experts, max_tokens=tokens, top_k=top_k, fused_return=fused_return) as layer:
         out = layer(gx, gids, gw)
         layer.check_errors()
         expected = oracle_moe.moe_layer(x, ids, w, w13, w2)
@@ -200,6 +201,44 @@ def test_single_rank_layer_matches_oracle(tokens, experts, hidden, ffn, top_k, r
         assert err < BF16_TOL, err
         counts = oracle_moe.route_counts(ids, experts)
         assert layer.recv_offs.cpu().tolist() == np.cumsum(counts).tolist()
+
+
+@pytest.mark.parametrize("tile", ["swap16x256", "swap32x256", "swap64x256", "tok128x256", "tok128x64",
+                                  "pair256x256", "pair256x512"])
+@pytest.mark.gpu
+@pytest.mark.skipif(not cuda_ready(), reason="needs a CUDA GPU")
+def test_scatter_epilogue_every_tile_family(tile):
+    """W2-style aggregate GEMM whose rows go to per-row destinations: equal to
+    the plain launch's rows, permuted, with dropped rows left untouched."""
+    _setup_paths()
+    from kernels import KernelConfig, launch_grouped_mm, launch_grouped_mm_scatter
+
+    shapes = {"swap16x256": (16, 256), "swap32x256": (32, 256), "swap64x256": (64, 256), "tok128x256": (128, 256),
+              "tok128x64": (128, 64), "pair256x256": (256, 128), "pair256x512": (256, 256)}
+    bm, bn = shapes[tile]
+    cfg = KernelConfig(bm, bn, 64, 8, 4, 4)
+    rng = np.random.default_rng(4)
+    sizes = [0, 37, 300, 5, 129, 64]
+    k, n = 192, 776
+    total = sum(sizes)
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn((total, k), device="cuda", generator=gen).to(torch.bfloat16)
+    b = (torch.randn((len(sizes), k, n), device="cuda", generator=gen) * 0.1).to(torch.bfloat16)
+    offs = torch.tensor(np.cumsum(sizes), dtype=torch.int32, device="cuda")
+    ref = launch_grouped_mm(a, b, offs, config=cfg)
+    perm = rng.permutation(total)
+    origin_host = perm.astype(np.int64)
+    origin_host[rng.random(total) < 0.1] = -1  # dropped rows
+    pitch = n + 8  # padded destination rows
+    dst = torch.full((total, pitch), 7.0, dtype=torch.bfloat16, device="cuda")
+    peers = torch.tensor([dst.data_ptr()], dtype=torch.int64, device="cuda")
+    launch_grouped_mm_scatter(a, b, offs, torch.from_numpy(origin_host).cuda(), peers, 0, pitch * 2, config=cfg)
+    torch.cuda.synchronize()
+    host_dst, host_ref = dst.float().cpu().numpy(), ref.float().cpu().numpy()
+    kept = origin_host >= 0
+    assert np.array_equal(host_dst[origin_host[kept], :n], host_ref[kept])
+    untouched = np.setdiff1d(np.arange(total), origin_host[kept])
+    assert np.all(host_dst[untouched] == 7.0) and np.all(host_dst[:, n:] == 7.0)
 
 
 @pytest.mark.gpu
@@ -344,8 +383,10 @@ def _two_rank_worker(rank, world, port, result_dir):
     g13 = torch.from_numpy(w13[mine]).cuda().to(torch.bfloat16)
     g2 = torch.from_numpy(w2[mine]).cuda().to(torch.bfloat16)
     worst, lines = 0.0, []
-    for cls in (ExpertParallelMoE, NcclAllToAllMoE):
-        with cls(g13, g2, experts, max_tokens=max_tokens, top_k=top_k) as layer:
+    variants = ((ExpertParallelMoE, {"fused_return": True}), (ExpertParallelMoE, {"fused_return": False}),
+                (NcclAllToAllMoE, {}))
+    for cls, options in variants:
+        with cls(g13, g2, experts, max_tokens=max_tokens, top_k=top_k, **options) as layer:
             for step, (tokens, routing) in enumerate(((120, {}), (160, {"skew": True}), (0 if rank else 33, {}),
                                                       (77, {"drop": 0.2}))):
                 trng = np.random.default_rng(1000 * step + rank)
@@ -357,7 +398,7 @@ def _two_rank_worker(rank, world, port, result_dir):
                 if tokens:
                     err = relative_frobenius(out.float().cpu().numpy(), oracle_moe.moe_layer(x, ids, w, w13, w2))
                     worst = max(worst, err)
-                    lines.append(f"{cls.__name__} step {step} tokens {tokens} err {err:.3e}")
+                    lines.append(f"{cls.__name__} {options} step {step} tokens {tokens} err {err:.3e}")
     dist.destroy_process_group()
     Path(result_dir, f"rank{rank}.txt").write_text(f"{worst}\n" + "\n".join(lines))
 
