@@ -552,7 +552,8 @@ int grouped_gemm_fp8_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const 
   const TcVariant v = bm <= 16 ? TcVariant{true, 16, 256}
                       : bm <= 32 ? TcVariant{true, 32, 256}
                       : bm <= 64 ? TcVariant{true, 64, 256}
-                                 : TcVariant{false, 128, 128};
+                      : bm < 256 ? TcVariant{false, 128, 128}
+                                 : TcVariant{false, 256, 128, true};
   TcVariantInfo vi;
   if (!mgb::fp8_variant_info(v, &vi)) return MGB_ERR_UNSUPPORTED;
 
@@ -577,14 +578,15 @@ int grouped_gemm_fp8_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const 
   // (contiguous A [M, K], B [N, K], C [M, N]), so no stride table is read.
 
   const TileBound bound{problem_count, m, 0};
-  const int grid = grid_from(bound, v.tm, v.tn, n, ds.sm_count);
+  const int grid = v.pair ? 2 * grid_from(bound, v.tm, v.tn, n, std::max(1, vi.max_clusters))
+                          : grid_from(bound, v.tm, v.tn, n, ds.sm_count);
   const size_t maps_bytes = static_cast<size_t>(problem_count) * kMapsPerProblem * kMapBytes;
   const size_t need = maps_bytes + (static_cast<size_t>(problem_count) + 1) * sizeof(int64_t);
   if (scratch == nullptr || scratch_bytes < need || reinterpret_cast<uintptr_t>(scratch) % 128 != 0) {
     return MGB_ERR_SCRATCH;
   }
   p.desc_slots = static_cast<uint8_t*>(scratch);
-  p.unit_tiles = unit_tiles_for(bound.tiles(v.tm, v.tn, n), k, vi.bk, grid);
+  p.unit_tiles = unit_tiles_for(bound.tiles(v.tm, v.tn, n), k, vi.bk, v.pair ? grid / 2 : grid);
   if (!homogeneous) {
     p.unit_start = reinterpret_cast<int64_t*>(static_cast<uint8_t*>(scratch) + maps_bytes);
     p.walk_tm = v.tm;

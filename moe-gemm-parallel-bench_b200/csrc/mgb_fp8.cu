@@ -7,7 +7,8 @@
 
 namespace mgb {
 
-// swap-AB 16 / 32 / 64 tokens x 256 weight rows, and 128 x 128 row tiles.
+// swap-AB 16 / 32 / 64 tokens x 256 weight rows, and 128 x 128 row tiles;
+// the CTA-pair 256 x 128 tile (fp8_pair_kernel) is handled beside them.
 #define MGB_FOR_EACH_FP8_VARIANT(X) \
   X(true, 16, 256)                  \
   X(true, 32, 256)                  \
@@ -32,7 +33,40 @@ static int launch_fp8_variant(const CUtensorMap& act, const CUtensorMap& wgt, co
   return static_cast<int>(cudaGetLastError());
 }
 
+// Clusters of two the device keeps resident at once for the CTA-pair kernel
+// (queried once per device; SMs / 2 when the query is unavailable).
+static int fp8_pair_max_clusters() {
+  static int cached[128] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 0;
+  if (cached[dev] == 0) {
+    if (cudaFuncSetAttribute(fp8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Fp8PairCfg::kSmemBytes) != cudaSuccess) {
+      return 0;
+    }
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1), 1, 1);
+    cfg.blockDim = dim3(Fp8PairCfg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Fp8PairCfg::kSmemBytes;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, fp8_pair_kernel, &cfg) != cudaSuccess || clusters <= 0) {
+      cudaGetLastError();
+      clusters = sms / 2;
+    }
+    cached[dev] = clusters;
+  }
+  return cached[dev];
+}
+
 bool fp8_variant_info(const TcVariant& v, TcVariantInfo* info) {
+  if (v.pair) {
+    if (v.tm != Fp8PairCfg::kTileM || v.tn != Fp8PairCfg::kTileN) return false;
+    *info = TcVariantInfo{Fp8PairCfg::kBK, Fp8PairCfg::kStages, Fp8PairCfg::kSmemBytes, fp8_pair_max_clusters(),
+                          Fp8PairCfg::kHalfM, Fp8PairCfg::kHalfN};
+    return true;
+  }
 #define MGB_FP8_INFO(S, M, N)                                                         \
   if (v.swap == S && v.tm == M && v.tn == N) {                                        \
     using Cfg = Fp8Cfg<S, M, N>;                                                      \
@@ -46,6 +80,23 @@ bool fp8_variant_info(const TcVariant& v, TcVariantInfo* info) {
 
 int fp8_launch(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
                const GroupedParams& p, int grid, cudaStream_t stream) {
+  if (v.pair) {
+    if (v.tm != Fp8PairCfg::kTileM || v.tn != Fp8PairCfg::kTileN || grid % 2 != 0) {
+      return static_cast<int>(cudaErrorInvalidValue);
+    }
+    static bool configured[128] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 128) return static_cast<int>(cudaErrorInvalidDevice);
+    if (!configured[dev]) {
+      const cudaError_t e = cudaFuncSetAttribute(fp8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                 Fp8PairCfg::kSmemBytes);
+      if (e != cudaSuccess) return static_cast<int>(e);
+      configured[dev] = true;
+    }
+    fp8_pair_kernel<<<grid, Fp8PairCfg::kThreads, Fp8PairCfg::kSmemBytes, stream>>>(act, wgt, out, p);
+    return static_cast<int>(cudaGetLastError());
+  }
 #define MGB_FP8_LAUNCH(S, M, N) \
   if (v.swap == S && v.tm == M && v.tn == N) return launch_fp8_variant<S, M, N>(act, wgt, out, p, grid, stream);
   MGB_FOR_EACH_FP8_VARIANT(MGB_FP8_LAUNCH)

@@ -36,6 +36,7 @@
 namespace mgb {
 
 constexpr int kFp8Block = 128;  // scale block along K (and along N for the weights)
+constexpr int kScaleAhead = 4;  // row tiles: K blocks whose scales a promotion lane has in flight
 
 template <bool SWAP, int TM, int TN>
 struct Fp8Cfg {
@@ -52,19 +53,28 @@ struct Fp8Cfg {
   static constexpr int kEpiWarps = SWAP ? 4 : 8;
   static constexpr int kThreads = 64 + 32 * kEpiWarps;
   static constexpr int kWarpCols = SWAP ? 0 : TN / 2;  // row tiles: columns one promotion warp owns
-  static constexpr int kBlocksPerWarp = 2;              // output staging blocks per warp
+  // One output staging block per warp: a warp stores a tile once per 128-deep
+  // K loop, so double-buffering the stores buys nothing, while the shared
+  // memory it frees deepens the operand ring (the FP8 MMA drains a stage in
+  // half the time of a bf16 one, so the ring must hide twice as many stages
+  // of L2 latency).
+  static constexpr int kBlocksPerWarp = 1;
   static constexpr int kEpiBytes = SWAP ? 0 : kEpiWarps * kBlocksPerWarp * kEpiWarpBytes;
   static constexpr int kStagesRaw = (kTcSmemBudget - kEpiBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
   static constexpr int kPartCols = SWAP ? (TN / 128) * TM : TN;  // TMEM columns of one partial
-  static constexpr int kTmemCols = pow2_at_least(2 * kPartCols);
+  // Partials in flight: the MMA runs up to kPartBufs - 1 K blocks ahead of
+  // the promotion, whose per-block latency (barrier wake-up, TMEM load, FMAs)
+  // exceeds one block's MMA time; as many as fit in TMEM, at most 4.
+  static constexpr int kPartBufs = 512 / kPartCols >= 4 ? 4 : 2;
+  static constexpr int kTmemCols = pow2_at_least(kPartBufs * kPartCols);
   // E4M3 x E4M3 (format code 0 for both operands), both K-major, fp32 D.
   static constexpr uint32_t kIdesc = SWAP ? instr_desc(0, 0, 0, 128, TM) : instr_desc(0, 0, 0, TM, TN);
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 2048 + 1024;
   static_assert(TN % 128 == 0 && TN <= 256, "weight tile: whole 128-row scale blocks, one TMA box");
   static_assert(SWAP ? (TM % 16 == 0 && TM >= 16 && TM <= 64) : (TM == 128 && TN == 128), "token tile");
   static_assert(kStages >= 3, "operand ring depth");
-  static_assert(2 * kPartCols <= 512, "two partials fit in TMEM");
+  static_assert(kPartBufs * kPartCols <= 512, "the partials fit in TMEM");
   static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
@@ -177,9 +187,10 @@ __global__ void __launch_bounds__(Fp8Cfg<SWAP, TM, TN>::kThreads, 1)
   uint8_t* epi_stage = smem + S * Cfg::kStageBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + Cfg::kEpiBytes);
   uint64_t* empty = full + S;
-  uint64_t* part_full = empty + S;       // [2] MMA commit: a partial is ready
-  uint64_t* part_empty = part_full + 2;  // [2] every epilogue warp: a partial was read
-  uint64_t* drain_bar = part_empty + 2;
+  constexpr int NP = Cfg::kPartBufs;
+  uint64_t* part_full = empty + S;        // [NP] MMA commit: a partial is ready
+  uint64_t* part_empty = part_full + NP;  // [NP] every epilogue warp: a partial was read
+  uint64_t* drain_bar = part_empty + NP;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
   volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* never = abort + 1;
@@ -192,7 +203,7 @@ __global__ void __launch_bounds__(Fp8Cfg<SWAP, TM, TN>::kThreads, 1)
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < NP; ++b) {
       mbar_init(&part_full[b], 1);
       mbar_init(&part_empty[b], Cfg::kEpiWarps);
     }
@@ -284,8 +295,8 @@ __global__ void __launch_bounds__(Fp8Cfg<SWAP, TM, TN>::kThreads, 1)
         const int64_t kblocks = (q.k + BK - 1) / BK;
         for (int64_t kb = 0; kb < kblocks; ++kb) {
           const int s = static_cast<int>(it % S);
-          const int pb = static_cast<int>(pit & 1u);
-          if (!mbar_wait(&part_empty[pb], ((pit >> 1) & 1u) ^ 1u, budget, abort)) {
+          const int pb = static_cast<int>(pit % NP);
+          if (!mbar_wait(&part_empty[pb], ((pit / NP) & 1u) ^ 1u, budget, abort)) {
             raise_error(p, kErrWaitAccEmpty, abort);
             ok = false;
             break;
@@ -375,8 +386,8 @@ __global__ void __launch_bounds__(Fp8Cfg<SWAP, TM, TN>::kThreads, 1)
 #pragma unroll
           for (int c = 0; c < kChunks; ++c) cb[c] = nb[c];
           if (kb + 1 < kblocks) fetch(kb + 1, na0, na1, nb);  // next block's scales in flight
-          const int pb = static_cast<int>(pit & 1u);
-          if (!mbar_wait_warp(&part_full[pb], (pit >> 1) & 1u, budget, abort)) {
+          const int pb = static_cast<int>(pit % NP);
+          if (!mbar_wait_warp(&part_full[pb], (pit / NP) & 1u, budget, abort)) {
             if (lane == 0) raise_error(p, kErrWaitAccFull, abort);
             ok = false;
             break;
@@ -426,12 +437,21 @@ __global__ void __launch_bounds__(Fp8Cfg<SWAP, TM, TN>::kThreads, 1)
           const float s_a = row < q.m ? sa[row * kblocks + kb] : 0.0f;
           return s_a * sb[nblk * kblocks + kb];
         };
-        float next = kblocks > 0 ? fetch(0) : 0.0f;
-        for (int64_t kb = 0; kb < kblocks; ++kb) {
-          const float f = next;
-          if (kb + 1 < kblocks) next = fetch(kb + 1);
-          const int pb = static_cast<int>(pit & 1u);
-          if (!mbar_wait_warp(&part_full[pb], (pit >> 1) & 1u, budget, abort)) {
+        // The scales of the next kScaleAhead K blocks are in flight: a lane's
+        // token scales are kblocks * 4 bytes apart from its neighbours', so
+        // each fetch is one sector per lane with L2 latency to hide.
+        float ring[kScaleAhead];
+#pragma unroll
+        for (int j = 0; j < kScaleAhead; ++j) ring[j] = j < kblocks ? fetch(j) : 0.0f;
+        for (int64_t kb0 = 0; ok && kb0 < kblocks; kb0 += kScaleAhead) {
+#pragma unroll
+         for (int j = 0; j < kScaleAhead; ++j) {
+          const int64_t kb = kb0 + j;
+          if (kb >= kblocks) break;
+          const float f = ring[j];
+          if (kb + kScaleAhead < kblocks) ring[j] = fetch(kb + kScaleAhead);
+          const int pb = static_cast<int>(pit % NP);
+          if (!mbar_wait_warp(&part_full[pb], (pit / NP) & 1u, budget, abort)) {
             if (lane == 0) raise_error(p, kErrWaitAccFull, abort);
             ok = false;
             break;
@@ -464,6 +484,7 @@ __global__ void __launch_bounds__(Fp8Cfg<SWAP, TM, TN>::kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&part_empty[pb]);
           ++pit;
+         }
         }
         if (!ok) break;
         if (cmap != nullptr) {
@@ -487,6 +508,291 @@ __global__ void __launch_bounds__(Fp8Cfg<SWAP, TM, TN>::kThreads, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------------
+// CTA-pair FP8 tile for token-rich problems: a cluster of two CTAs owns a
+// 256-token x 128-weight-row output tile (one weight scale block).  CTA r
+// loads token rows [128 r, 128 r + 128) and weight rows [64 r, 64 r + 64) of
+// every 128-deep K block into its own shared memory; the even CTA issues
+// tcgen05.mma.cta_group::2.kind::f8f6f4 (M = 256, N = 128), which reads both
+// CTAs' halves and writes rows 0-127 / 128-255 of the partial into CTA 0 / 1's
+// TMEM.  Per CTA and K block that is 24 KB from L2 for 128 x 128 x 128 MACs
+// (175 FLOP per byte) instead of 32 KB for the one-CTA 128 x 128 tile (131).
+// Each CTA's eight promotion warps then work on their own 128 rows exactly as
+// in the one-CTA row tile.  Barriers as in tc2_grouped_kernel:
+//   full[s]         in CTA 0 only: both CTAs' TMA bytes for stage s land on it
+//   empty[s]        in each CTA: the MMA commit multicasts to both
+//   part_full[b]    in each CTA: the MMA commit multicasts to both
+//   part_empty[b]   in CTA 0 only: the 16 promotion warps of the pair arrive
+struct Fp8PairCfg {
+  static constexpr int kBK = kFp8Block;
+  static constexpr int kTileM = 256;  // tokens per cluster tile
+  static constexpr int kTileN = 128;  // weight rows per cluster tile (one scale block)
+  static constexpr int kHalfM = 128;  // token rows per CTA
+  static constexpr int kHalfN = 64;   // weight rows per CTA
+  static constexpr int kActBytes = kHalfM * 128;
+  static constexpr int kWgtBytes = kHalfN * 128;
+  static constexpr int kStageBytes = kActBytes + kWgtBytes;
+  static constexpr int kEpiWarps = 8;
+  static constexpr int kThreads = 64 + 32 * kEpiWarps;
+  static constexpr int kWarpCols = kTileN / 2;
+  static constexpr int kBlocksPerWarp = 1;  // as in Fp8Cfg: the freed shared memory deepens the ring
+  static constexpr int kEpiBytes = kEpiWarps * kBlocksPerWarp * kEpiWarpBytes;
+  static constexpr int kStagesRaw = (kTcSmemBudget - kEpiBytes) / kStageBytes;
+  static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
+  static constexpr int kPartCols = kTileN;  // TMEM columns of one partial (this CTA's 128 rows)
+  static constexpr int kPartBufs = 4;       // partials in flight (see Fp8Cfg)
+  static constexpr int kTmemCols = kPartBufs * kPartCols;
+  static constexpr uint32_t kIdesc = instr_desc(0, 0, 0, kTileM, kTileN);  // E4M3 x E4M3, both K-major
+  static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 2048 + 1024;
+  static_assert(kStages >= 3, "operand ring depth");
+  static_assert(kSmemBytes <= 232448, "shared memory");
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8PairCfg::kThreads, 1)
+    fp8_pair_kernel(const __grid_constant__ CUtensorMap act_tmpl, const __grid_constant__ CUtensorMap wgt_tmpl,
+                    const __grid_constant__ CUtensorMap out_tmpl, const GroupedParams p) {
+  using Cfg = Fp8PairCfg;
+  constexpr int S = Cfg::kStages;
+  constexpr int BK = Cfg::kBK;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* ring = smem;
+  uint8_t* epi_stage = smem + S * Cfg::kStageBytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(epi_stage + Cfg::kEpiBytes);
+  uint64_t* empty = full + S;
+  constexpr int NP = Cfg::kPartBufs;
+  uint64_t* part_full = empty + S;
+  uint64_t* part_empty = part_full + NP;
+  uint64_t* drain_bar = part_empty + NP;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* never = abort + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int64_t cluster = blockIdx.x >> 1;
+  const int64_t clusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < NP; ++b) {
+      mbar_init(&part_full[b], 1);
+      mbar_init(&part_empty[b], 2 * Cfg::kEpiWarps);
+    }
+    mbar_init(drain_bar, 1);
+    *abort = 0;
+    *never = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // the peer's barriers exist before anything lands on them
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const long long budget = p.wait_budget;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    const CUtensorMap* act_map = &act_tmpl;
+    const CUtensorMap* wgt_map = &wgt_tmpl;
+    const uint64_t pol_stream = policy_evict_first();
+    const uint64_t pol_shared = policy_evict_normal();
+    const uint64_t pol_act = policy_evict_last();
+    TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
+    uint32_t it = 0;
+    int built = -1;
+    bool ok = true;
+    for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
+      const Problem& q = walk.prob;
+      if (!fp8_legal(q)) {
+        if (lane == 0 && walk.problem != built) atomicOr(p.error_word, kErrMisaligned);
+        continue;
+      }
+      const int64_t kblocks = (q.k + BK - 1) / BK;
+      const uint64_t pol_wgt = walk.m_blocks > 1 ? pol_shared : pol_stream;
+      const int32_t m0 = static_cast<int32_t>(walk.m_block(t) * Cfg::kTileM + rank * Cfg::kHalfM);
+      const int32_t n0 = static_cast<int32_t>(walk.n_block(t) * Cfg::kTileN + rank * Cfg::kHalfN);
+      for (int64_t kb = 0; kb < kblocks; ++kb) {
+        const int s = static_cast<int>(it % S);
+        if (!mbar_wait_warp(&empty[s], ((it / S) & 1u) ^ 1u, budget, abort)) {
+          if (lane == 0) raise_error(p, kErrWaitEmpty, abort);
+          ok = false;
+          break;
+        }
+        if (kb == 0 && walk.problem != built) {
+          const CUtensorMap* g = problem_maps(p, walk.problem);  // built by build_fp8_maps_kernel
+          if (lane == 0) {
+            tmap_acquire(&g[0]);
+            tmap_acquire(&g[1]);
+          }
+          __syncwarp();
+          act_map = &g[0];
+          wgt_map = &g[1];
+          built = walk.problem;
+        }
+        if (lane == 0) {
+          uint8_t* st_act = ring + s * Cfg::kStageBytes;
+          uint8_t* st_wgt = st_act + Cfg::kActBytes;
+          const int32_t kx = static_cast<int32_t>(kb * BK);
+          const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
+          tma_load_2d_pair(act_map, bar, st_act, kx, m0, pol_act);
+          tma_load_2d_pair(wgt_map, bar, st_wgt, kx, n0, pol_wgt);
+        }
+        __syncwarp();
+        ++it;
+      }
+    }
+    if (*abort && leader && lane == 0) {
+      const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0u;
+      for (uint32_t j = first; j < it; ++j) {
+        if (!mbar_wait(&full[j % S], (j / S) & 1u, budget, never)) {
+          atomicOr(p.error_word, kErrWaitTeardown);
+          break;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------- MMA issuer (even CTA only)
+    if (lane == 0 && leader) {
+      TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
+      uint32_t it = 0;
+      uint32_t pit = 0;
+      bool ok = true;
+      for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
+        const Problem& q = walk.prob;
+        if (!fp8_legal(q)) continue;
+        const int64_t kblocks = (q.k + BK - 1) / BK;
+        for (int64_t kb = 0; kb < kblocks; ++kb) {
+          const int s = static_cast<int>(it % S);
+          const int pb = static_cast<int>(pit % NP);
+          if (!mbar_wait(&part_empty[pb], ((pit / NP) & 1u) ^ 1u, budget, abort)) {
+            raise_error(p, kErrWaitAccEmpty, abort);
+            ok = false;
+            break;
+          }
+          if (!mbar_wait(&full[s], (it / S) & 1u, budget, abort)) {
+            raise_error(p, kErrWaitFull, abort);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(pb * Cfg::kPartCols);
+          const uint32_t a_base = smem_u32(ring + s * Cfg::kStageBytes);
+          const uint32_t w_base = a_base + Cfg::kActBytes;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            const uint64_t act_desc = smem_desc(a_base + ks * 32, 16, 1024, kLayoutSw128);
+            const uint64_t wgt_desc = smem_desc(w_base + ks * 32, 16, 1024, kLayoutSw128);
+            mma_f8_pair(d_tmem, act_desc, wgt_desc, Cfg::kIdesc, ks > 0 ? 1u : 0u);
+          }
+          mma_commit_pair(&empty[s], 0x3);      // frees stage s in both CTAs
+          mma_commit_pair(&part_full[pb], 0x3);  // both CTAs' promotion warps may read
+          ++it;
+          ++pit;
+        }
+      }
+      if (*abort) {
+        mma_commit_pair(drain_bar, 0x1);
+        if (!mbar_wait(drain_bar, 0, budget, never)) atomicOr(p.error_word, kErrWaitTeardown);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------- promotion and the stores
+    constexpr int W = Cfg::kWarpCols;
+    const int quarter = warp & 3;
+    const int ew = warp - 2;
+    const int half = ew / 4;
+    TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
+    uint32_t pit = 0;
+    uint8_t* my_blocks = epi_stage + ew * Cfg::kBlocksPerWarp * kEpiWarpBytes;
+    int c_built = -1;
+    const uint64_t pol_out = policy_evict_first();
+    uint32_t chunk_seq = 0;
+    bool ok = true;
+    for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
+      const Problem& q = walk.prob;
+      if (!fp8_legal(q)) continue;
+      const int64_t kblocks = (q.k + BK - 1) / BK;
+      const int64_t m0 = walk.m_block(t) * Cfg::kTileM + rank * Cfg::kHalfM;
+      const int64_t n0 = walk.n_block(t) * Cfg::kTileN;
+      const float* sa = reinterpret_cast<const float*>(p.sa_ptrs[walk.problem]);
+      const float* sb = reinterpret_cast<const float*>(p.sb_ptrs[walk.problem]);
+      const void* cmap = out_map_for(p, out_tmpl, walk.problem, c_built, lane);
+      float acc[W];
+#pragma unroll
+      for (int i = 0; i < W; ++i) acc[i] = 0.0f;
+      const int64_t row = m0 + quarter * 32 + lane;
+      const int64_t nblk = n0 / kFp8Block;
+      auto fetch = [&](int64_t kb) -> float {
+        const float s_a = row < q.m ? sa[row * kblocks + kb] : 0.0f;
+        return s_a * sb[nblk * kblocks + kb];
+      };
+      float ring[kScaleAhead];  // scales of the next K blocks in flight, as in fp8_grouped_kernel
+#pragma unroll
+      for (int j = 0; j < kScaleAhead; ++j) ring[j] = j < kblocks ? fetch(j) : 0.0f;
+      for (int64_t kb0 = 0; ok && kb0 < kblocks; kb0 += kScaleAhead) {
+#pragma unroll
+       for (int j = 0; j < kScaleAhead; ++j) {
+        const int64_t kb = kb0 + j;
+        if (kb >= kblocks) break;
+        const float f = ring[j];
+        if (kb + kScaleAhead < kblocks) ring[j] = fetch(kb + kScaleAhead);
+        const int pb = static_cast<int>(pit % NP);
+        if (!mbar_wait_warp(&part_full[pb], (pit / NP) & 1u, budget, abort)) {
+          if (lane == 0) raise_error(p, kErrWaitAccFull, abort);
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                               static_cast<uint32_t>(pb * Cfg::kPartCols + half * W);
+        uint32_t r0[32], r1[32];
+        tmem_ld32(taddr, r0);
+        tmem_ld32(taddr + 32, r1);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          acc[i] = fmaf(__uint_as_float(r0[i]), f, acc[i]);
+          acc[32 + i] = fmaf(__uint_as_float(r1[i]), f, acc[32 + i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&part_empty[pb]), 0));
+        ++pit;
+       }
+      }
+      if (!ok) break;
+      if (cmap != nullptr) {
+        store_acc_rows_tma<Cfg::kBlocksPerWarp, 0>(q, cmap, acc, static_cast<int32_t>(m0 + quarter * 32),
+                                                   static_cast<int32_t>(n0 + half * W), my_blocks, lane, chunk_seq,
+                                                   pol_out, p.error_word);
+      }
+    }
+    if (lane == 0) bulk_wait_group_all();
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // neither CTA leaves while the pair may still touch its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
   }
 }
 

@@ -293,6 +293,14 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// Relaxed arrive on an mbarrier anywhere in the cluster: no release fence.  For
+// arrivals that only report finished TMEM reads (tcgen05.wait::ld has
+// completed them, and tcgen05.fence::before_thread_sync orders them), where a
+// release at cluster scope would stall the warp on every arrival.
+__device__ __forceinline__ void mbar_arrive_cluster_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 // TMA tile load issued by either CTA of a pair; the transaction bytes count on
 // the mbarrier at `mbar_cluster_addr` (the leader CTA's barrier).  No multicast.
 __device__ __forceinline__ void tma_load_2d_pair(const void* tmap, uint32_t mbar_cluster_addr, void* dst, int32_t x,
@@ -324,6 +332,18 @@ __device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t adesc, ui
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// CTA-pair kind::f8f6f4 MMA (E4M3 x E4M3 with format code 0 in both operand
+// fields of the instruction descriptor); K = 32 per MMA.
+__device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

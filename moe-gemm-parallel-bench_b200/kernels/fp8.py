@@ -36,6 +36,7 @@ FP8_TILE_SWAP_16 = KernelConfig(16, 256, 128, 4, 8, 4)
 FP8_TILE_SWAP_32 = KernelConfig(32, 256, 128, 4, 8, 4)
 FP8_TILE_SWAP_64 = KernelConfig(64, 256, 128, 8, 8, 4)
 FP8_TILE_ROWS_128 = KernelConfig(128, 128, 128, 8, 8, 4)
+FP8_TILE_PAIR_256 = KernelConfig(256, 128, 128, 8, 8, 4)  # CTA pair: 256 tokens x 128 weight rows
 
 
 def fp8_tile_for(max_m: int) -> KernelConfig:

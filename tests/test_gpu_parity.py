@@ -602,18 +602,20 @@ def test_fp8_block_scaled_every_tile_ragged_group():
     shapes = [(16, 256, 256), (40, 320, 200), (130, 128, 384), (1, 64, 136), (300, 512, 256)]
     ws = build_fp8_workspace(shapes, seed=13)
     assert not ws.homogeneous
-    for bm, bn in ((16, 256), (32, 256), (64, 256), (128, 128)):
+    for bm, bn in ((16, 256), (32, 256), (64, 256), (128, 128), (256, 128)):
         for c in ws.c:
             c.fill_(float("nan"))
         launch_grouped_fp8(ws, config=KernelConfig(bm, bn, 128, 4, 8, 4))
         torch.cuda.synchronize()
         check_device_errors()
-        assert ws.launch_info["path"] == "tcgen05_tma" and ws.launch_info["tile_m"] == bm, ws.launch_info
+        path = "tcgen05_tma_pair" if bm == 256 else "tcgen05_tma"
+        assert ws.launch_info["path"] == path and ws.launch_info["tile_m"] == bm, ws.launch_info
         assert ws.launch_info["tile_n"] == bn, ws.launch_info
         _fp8_check(ws)
 
 
-@pytest.mark.parametrize("m_e,k,n", [(16, 7168, 4096), (64, 2048, 7168), (128, 7168, 512), (1024, 256, 7168)])
+@pytest.mark.parametrize("m_e,k,n", [(16, 7168, 4096), (64, 2048, 7168), (128, 7168, 512), (1024, 256, 7168),
+                                     (512, 7168, 4096), (1024, 2048, 7168)])
 def test_fp8_block_scaled_deepseek_rank_shapes(m_e, k, n):
     """DeepSeek-V3 W13 / W2 expert shapes (3 experts, the FP8 tile policy);
     oracle on sampled rows."""
