@@ -61,7 +61,10 @@ def parse_args(argv=None):
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=200)
     p.add_argument("--warmup", type=int, default=5)
-    p.add_argument("--impl", choices=("native", "reference"), default="native")
+    p.add_argument("--impl", choices=("native", "reference", "reference-gpu"), default="native",
+                   help="reference: the reference's CPU path (the driver's reference arm); reference-gpu: the "
+                        "reference's own Triton grouped GEMM and torch grouped_mm provider on this GPU, per shape, "
+                        "next to the native kernels on identical inputs")
     p.add_argument("--e2e-steps", type=int, default=3)
     p.add_argument("--skip-cpu-baseline", action="store_true")
     p.add_argument("--m-values", type=str, default=",".join(map(str, M_VALUES)))
@@ -965,6 +968,125 @@ def moe_layer_bench(args, rank: int, world: int, local_rank: int, device) -> Non
         print(json.dumps(line), flush=True)
 
 
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def load_reference_package():
+    """The unmodified reference's `kernels` package from baseline/_ref,
+    imported as `refkernels` so it sits beside this package's `kernels`
+    (its modules import `utils.benchmark`, found on baseline/_ref)."""
+    import importlib.util
+
+    init = REF_DIR / "kernels" / "__init__.py"
+    if not init.exists():
+        raise FileNotFoundError(f"{init} is missing (install the reference into baseline/_ref)")
+    if str(REF_DIR) not in sys.path:
+        sys.path.append(str(REF_DIR))
+    spec = importlib.util.spec_from_file_location("refkernels", init, submodule_search_locations=[str(init.parent)])
+    module = importlib.util.module_from_spec(spec)
+    sys.modules["refkernels"] = module
+    spec.loader.exec_module(module)
+    return module
+
+
+def reference_gpu_arm(args, rank: int, world: int) -> None:
+    """--impl reference-gpu: per W13 (or W2) step shape, the reference's Triton
+    persistent grouped GEMM (its launch_grouped with its hot autotune,
+    kernels/grouped_gemm.py:618-760) and its torch.nn.functional.grouped_mm
+    provider (kernels/torch_grouped_gemm.py:121-176), both from the unmodified
+    reference in baseline/_ref, next to this package's native launch on the
+    same seeded inputs (the reference's build_grouped_workspace draw, restated
+    by kernels.build_grouped_workspace).  Native and Triton outputs are compared
+    (relative Frobenius).  Rank 0 only; one JSON line."""
+    if rank != 0:
+        return
+    import torch
+
+    torch.cuda.set_device(0)
+    try:
+        ref = load_reference_package()
+    except Exception as exc:  # the reference is not installed or does not import here
+        print(json.dumps({"impl": "reference-gpu", "unavailable": f"{type(exc).__name__}: {exc}"}))
+        return
+    from kernels import build_grouped_workspace, check_device_errors, launch_grouped
+
+    m_values = [int(v) for v in args.m_values.split(",")]
+    dims = projection_dims(args.projection)
+    parallel = [p for p in ("EP", "TP") if p in args.parallel.split(",")]
+    counts = {"EP": EXPERTS // PARALLEL, "TP": EXPERTS}
+
+    def median_ms(fn, reps: int = 10) -> float:
+        fn()
+        torch.cuda.synchronize()
+        times = []
+        for _ in range(reps):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            fn()
+            end.record()
+            end.synchronize()
+            times.append(start.elapsed_time(end))
+        return statistics.median(times)
+
+    rows = []
+    for m in m_values:
+        for par in parallel:
+            k, n = dims[par]
+            shapes = [(m, k, n)] * counts[par]
+            flops = 2 * m * k * n * counts[par]
+            row = {"parallel": par, "M_e": m, "experts": counts[par]}
+            progress(f"{par} M_e={m}: native")
+            ws = build_grouped_workspace(shapes, torch.bfloat16, seed=0)
+            launch_grouped(ws)
+            torch.cuda.synchronize()
+            check_device_errors(0)
+            row["native_ms"] = round(median_ms(lambda: launch_grouped(ws)), 4)
+            native_c = [c.clone() for c in ws.c[:4]]
+            del ws
+            progress(f"{par} M_e={m}: reference Triton (hot autotune)")
+            try:
+                rws = ref.build_grouped_workspace(shapes, torch.bfloat16, seed=0)
+                ref.launch_grouped(rws)
+                torch.cuda.synchronize()
+                row["triton_ms"] = round(median_ms(lambda: ref.launch_grouped(rws)), 4)
+                row["triton_config"] = str(getattr(rws, "config", None))
+                errs = []
+                for ours, theirs in zip(native_c, rws.c[:4]):
+                    diff = (ours.float() - theirs.float()).norm() / theirs.float().norm().clamp_min(1e-30)
+                    errs.append(float(diff))
+                row["rel_err_native_vs_triton"] = max(errs)
+                del rws
+            except Exception as exc:
+                row["triton_unavailable"] = f"{type(exc).__name__}: {str(exc)[:200]}"
+            torch.cuda.empty_cache()
+            progress(f"{par} M_e={m}: torch grouped_mm")
+            try:
+                tws = ref.build_torch_grouped_workspace(shapes, torch.bfloat16, seed=0)
+                row["torch_grouped_mm_ms"] = round(median_ms(lambda: ref.launch_torch_grouped(tws)), 4)
+                del tws
+            except Exception as exc:
+                row["torch_grouped_mm_unavailable"] = f"{type(exc).__name__}: {str(exc)[:200]}"
+            torch.cuda.empty_cache()
+            for key in ("native", "triton", "torch_grouped_mm"):
+                if f"{key}_ms" in row:
+                    row[f"{key}_tflops"] = round(flops / row[f"{key}_ms"] / 1e9, 1)
+            rows.append(row)
+            print(json.dumps(row), file=sys.stderr, flush=True)
+    totals = {key: round(sum(r.get(f"{key}_ms", float("nan")) for r in rows), 4)
+              for key in ("native", "triton", "torch_grouped_mm")}
+    print(json.dumps({
+        "impl": "reference-gpu", "metric": METRIC, "unit": "TFLOP/s", "n_gpus": 1, "dtype": "bf16",
+        "data": "synthetic (the reference's seeded build_grouped_workspace draw, N(0,1)*0.1)",
+        "config": {"workload": WORKLOAD if args.projection == "W1" else WORKLOAD_W2,
+                   "timing": "hot; median of 10 CUDA-event-timed launches per shape after the first call "
+                             "(the reference's autotune runs in that first call)"},
+        "providers": {"native": "this package (C ABI, native tile policy)",
+                      "triton": "reference kernels/grouped_gemm.py launch_grouped (Triton, hot autotune)",
+                      "torch_grouped_mm": "reference kernels/torch_grouped_gemm.py (torch.nn.functional.grouped_mm)"},
+        "step_ms": totals, "per_shape": rows,
+    }), flush=True)
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
     if args.warmup < 3:
@@ -972,6 +1094,9 @@ def main(argv=None) -> int:
     rank, world, local_rank = dist_env()
     if args.impl == "reference":
         reference_arm(args, rank, world)
+        return 0
+    if args.impl == "reference-gpu":
+        reference_gpu_arm(args, rank, world)
         return 0
 
     import torch
