@@ -3,8 +3,9 @@
 //
 //   moe_route_layout  per-expert slot counts and each slot's position inside
 //                     its expert (one atomic per slot)
-//   moe_permute       token rows -> expert-sorted rows, one warp per slot,
-//                     16-byte copies when rows allow it
+//   moe_permute       token rows -> expert-sorted rows, one warp per token
+//                     (the row is read once for its slots), 16-byte copies
+//                     when rows allow it
 //   moe_combine       expert-sorted results -> tokens, weighted sum over the
 //                     token's top-k slots in fp32, one warp per token
 #include <cuda_bf16.h>
@@ -36,37 +37,78 @@ __global__ void __launch_bounds__(kThreads) route_layout_kernel(const int32_t* _
   }
 }
 
-// One warp per slot: copies row i / top_k of x to row offsets[e] + position[i].
+// Slots of one token handled together: their row addresses live in registers.
+constexpr int kFan = 8;
+
+// One warp per token: its row is read once per group of kFan slots and
+// written to each kept slot's row offsets[e] + position[i] of `sorted`, four
+// 16-byte chunks per lane in flight.
 __global__ void __launch_bounds__(kThreads)
     permute_kernel(const uint8_t* __restrict__ x, int64_t x_pitch, const int32_t* __restrict__ ids,
-                   const int32_t* __restrict__ position, const int32_t* __restrict__ offsets, int64_t slots,
+                   const int32_t* __restrict__ position, const int32_t* __restrict__ offsets, int64_t tokens,
                    int32_t top_k, int32_t experts, int64_t row_bytes, uint8_t* __restrict__ sorted,
                    int64_t sorted_pitch, int32_t elem_bytes, bool vec16) {
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + (threadIdx.x >> 5); i < slots; i += warps) {
-    const int32_t e = ids[i];
-    if (e < 0 || e >= experts) continue;
-    const uint8_t* src = x + (i / top_k) * x_pitch;
-    uint8_t* dst = sorted + static_cast<int64_t>(offsets[e] + position[i]) * sorted_pitch;
-    if (vec16) {
-      for (int64_t b = lane * 16; b < row_bytes; b += 32 * 16) {
-        *reinterpret_cast<uint4*>(dst + b) = *reinterpret_cast<const uint4*>(src + b);
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + (threadIdx.x >> 5); t < tokens; t += warps) {
+    const uint8_t* src = x + t * x_pitch;
+    for (int j0 = 0; j0 < top_k; j0 += kFan) {
+      uint8_t* dst[kFan];
+#pragma unroll
+      for (int j = 0; j < kFan; ++j) {
+        dst[j] = nullptr;
+        if (j0 + j < top_k) {
+          const int64_t i = t * top_k + j0 + j;
+          const int32_t e = ids[i];
+          if (e >= 0 && e < experts && position[i] >= 0) {
+            dst[j] = sorted + static_cast<int64_t>(offsets[e] + position[i]) * sorted_pitch;
+          }
+        }
       }
-    } else if (elem_bytes == 4) {
-      for (int64_t b = lane * 4; b < row_bytes; b += 32 * 4) {
-        *reinterpret_cast<uint32_t*>(dst + b) = *reinterpret_cast<const uint32_t*>(src + b);
-      }
-    } else {
-      for (int64_t b = lane * 2; b < row_bytes; b += 32 * 2) {
-        *reinterpret_cast<uint16_t*>(dst + b) = *reinterpret_cast<const uint16_t*>(src + b);
+      if (vec16) {
+        constexpr int kBatch = 4;
+        for (int64_t b0 = lane * 16; b0 < row_bytes; b0 += kBatch * 32 * 16) {
+          uint4 v[kBatch];
+#pragma unroll
+          for (int u = 0; u < kBatch; ++u) {
+            const int64_t b = b0 + u * 32 * 16;
+            if (b < row_bytes) v[u] = *reinterpret_cast<const uint4*>(src + b);
+          }
+#pragma unroll
+          for (int j = 0; j < kFan; ++j) {
+            if (dst[j] == nullptr) continue;
+#pragma unroll
+            for (int u = 0; u < kBatch; ++u) {
+              const int64_t b = b0 + u * 32 * 16;
+              if (b < row_bytes) *reinterpret_cast<uint4*>(dst[j] + b) = v[u];
+            }
+          }
+        }
+      } else if (elem_bytes == 4) {
+        for (int64_t b = lane * 4; b < row_bytes; b += 32 * 4) {
+          const uint32_t v = *reinterpret_cast<const uint32_t*>(src + b);
+#pragma unroll
+          for (int j = 0; j < kFan; ++j) {
+            if (dst[j] != nullptr) *reinterpret_cast<uint32_t*>(dst[j] + b) = v;
+          }
+        }
+      } else {
+        for (int64_t b = lane * 2; b < row_bytes; b += 32 * 2) {
+          const uint16_t v = *reinterpret_cast<const uint16_t*>(src + b);
+#pragma unroll
+          for (int j = 0; j < kFan; ++j) {
+            if (dst[j] != nullptr) *reinterpret_cast<uint16_t*>(dst[j] + b) = v;
+          }
+        }
       }
     }
   }
 }
 
 // One warp per token: out[t] = sum_j w[t, j] y[offsets[e] + position[t k + j]]
-// in fp32, bf16 rows; 8 columns per lane step when rows are 16-byte aligned.
+// in fp32, bf16 rows.  A group's row addresses and weights are resolved once
+// per token; with 16-byte rows each lane loads its chunk of every slot of the
+// group before summing, so kFan loads per lane are in flight.
 __global__ void __launch_bounds__(kThreads)
     combine_kernel(const __nv_bfloat16* __restrict__ y, int64_t y_pitch, const int32_t* __restrict__ ids,
                    const float* __restrict__ weights, const int32_t* __restrict__ position,
@@ -76,21 +118,44 @@ __global__ void __launch_bounds__(kThreads)
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x / 32);
   for (int64_t t = blockIdx.x * static_cast<int64_t>(blockDim.x / 32) + (threadIdx.x >> 5); t < tokens; t += warps) {
     __nv_bfloat16* dst = out + t * out_pitch;
+    auto resolve = [&](int j0, const __nv_bfloat16* (&src)[kFan], float (&w)[kFan]) {
+#pragma unroll
+      for (int j = 0; j < kFan; ++j) {
+        src[j] = nullptr;
+        w[j] = 0.f;
+        if (j0 + j < top_k) {
+          const int64_t i = t * top_k + j0 + j;
+          const int32_t e = ids[i];
+          if (e >= 0 && e < experts && position[i] >= 0) {
+            src[j] = y + static_cast<int64_t>(offsets[e] + position[i]) * y_pitch;
+            w[j] = weights[i];
+          }
+        }
+      }
+    };
+    const __nv_bfloat16* src[kFan];
+    float w[kFan];
+    const bool one_group = top_k <= kFan;
+    if (one_group) resolve(0, src, w);
     if (vec8) {
       for (int64_t c = lane * 8; c < hidden; c += 32 * 8) {
         float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        for (int j = 0; j < top_k; ++j) {
-          const int64_t i = t * top_k + j;
-          const int32_t e = ids[i];
-          if (e < 0 || e >= experts) continue;
-          const float w = weights[i];
-          const uint4 raw = *reinterpret_cast<const uint4*>(y + (offsets[e] + position[i]) * y_pitch + c);
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        for (int j0 = 0; j0 < top_k; j0 += kFan) {
+          if (!one_group) resolve(j0, src, w);
+          uint4 raw[kFan];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 f = __bfloat1622float2(h[q]);
-            acc[2 * q] = fmaf(w, f.x, acc[2 * q]);
-            acc[2 * q + 1] = fmaf(w, f.y, acc[2 * q + 1]);
+          for (int j = 0; j < kFan; ++j) {
+            raw[j] = src[j] != nullptr ? *reinterpret_cast<const uint4*>(src[j] + c) : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int j = 0; j < kFan; ++j) {
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float2 f = __bfloat1622float2(h[q]);
+              acc[2 * q] = fmaf(w[j], f.x, acc[2 * q]);
+              acc[2 * q + 1] = fmaf(w[j], f.y, acc[2 * q + 1]);
+            }
           }
         }
         uint4 packed;
@@ -102,11 +167,12 @@ __global__ void __launch_bounds__(kThreads)
     } else {
       for (int64_t c = lane; c < hidden; c += 32) {
         float acc = 0.f;
-        for (int j = 0; j < top_k; ++j) {
-          const int64_t i = t * top_k + j;
-          const int32_t e = ids[i];
-          if (e < 0 || e >= experts) continue;
-          acc = fmaf(weights[i], __bfloat162float(y[(offsets[e] + position[i]) * y_pitch + c]), acc);
+        for (int j0 = 0; j0 < top_k; j0 += kFan) {
+          if (!one_group) resolve(j0, src, w);
+#pragma unroll
+          for (int j = 0; j < kFan; ++j) {
+            if (src[j] != nullptr) acc = fmaf(w[j], __bfloat162float(src[j][c]), acc);
+          }
         }
         dst[c] = __float2bfloat16_rn(acc);
       }
@@ -149,8 +215,8 @@ int moe_permute(const void* x, int64_t x_pitch, const int32_t* topk_ids, const i
   const int64_t row_bytes = hidden * elem_bytes;
   const bool vec16 = aligned16(x) && aligned16(sorted) && row_bytes % 16 == 0 && (x_pitch * elem_bytes) % 16 == 0 &&
                      (sorted_pitch * elem_bytes) % 16 == 0;
-  permute_kernel<<<grid_for(slots, kThreads / 32), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(x), x_pitch * elem_bytes, topk_ids, position, offsets, slots, top_k, num_experts,
+  permute_kernel<<<grid_for(tokens, kThreads / 32), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(x), x_pitch * elem_bytes, topk_ids, position, offsets, tokens, top_k, num_experts,
       row_bytes, static_cast<uint8_t*>(sorted), sorted_pitch * elem_bytes, elem_bytes, vec16);
   return cudaGetLastError() == cudaSuccess ? MGB_OK : MGB_ERR_CUDA;
 }
