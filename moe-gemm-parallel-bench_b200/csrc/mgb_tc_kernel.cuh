@@ -281,7 +281,10 @@ __device__ __forceinline__ void store_rows_tma(const Problem& q, const void* cma
   constexpr int kUnits = kChunkCols / 32;  // TMEM load units per chunk
   constexpr int kTotal = TN / 32;
   static_assert(TN % kChunkCols == 0, "tile width is a whole number of chunks");
-  if (row0 >= q.m) return;  // all 32 rows of this warp lie past C (a ragged last M block)
+  // All 32 rows lie past C (a ragged last M block), or every column does: no
+  // TMEM load may be issued then, since only the loop below waits for one (a
+  // tcgen05.ld left unwaited writes its registers after they were reused).
+  if (row0 >= q.m || n0 >= q.n) return;
   const int64_t cols_left = q.n - n0;
   const int chunks = cols_left >= TN ? TN / kChunkCols : static_cast<int>((cols_left + kChunkCols - 1) / kChunkCols);
   const int units = chunks * kUnits;
@@ -330,7 +333,7 @@ __device__ __forceinline__ void store_rows_scatter(const GroupedParams& p, const
   constexpr int kChunkCols = 128 / static_cast<int>(sizeof(T));
   constexpr int kUnits = kChunkCols / 32;
   constexpr int kTotal = TN / 32;
-  if (row0 >= q.m) return;
+  if (row0 >= q.m || n0 >= q.n) return;  // as in store_rows_tma: no unwaited TMEM load
   const int64_t cols_left = q.n - n0;
   const int chunks = cols_left >= TN ? TN / kChunkCols : static_cast<int>((cols_left + kChunkCols - 1) / kChunkCols);
   const int units = chunks * kUnits;
