@@ -93,3 +93,27 @@ def test_missing_library_fails_loudly(tmp_path, monkeypatch):
     with pytest.raises(RuntimeError, match="missing"):
         _native.load()
     assert not _native.available()
+
+
+def test_expert_parallel_region_layout_is_aligned_and_validated():
+    """moe_ep_region_layout is pure host arithmetic: sections in order, 256-byte
+    (tables) / 1024-byte (row blocks) aligned, sized for the arguments; bad
+    arguments are refused."""
+    world, experts, hidden, capacity, slots = 4, 256, 7168, 131072, 32768
+    r = _native.ep_region_layout(world, experts, hidden, capacity, slots, 2)
+    assert 0 < r.counts < r.send_base < r.recv_offs < r.recv < r.out < r.origin < r.ret < r.bytes
+    assert r.counts >= 3 * _native.EP_MAX_WORLD * 4  # the barrier flags sit in front of the tables
+    assert r.send_base - r.counts >= 2 * world * experts * 4
+    assert r.recv_offs - r.send_base >= experts * 4
+    assert r.recv - r.recv_offs >= experts // world * 4
+    assert r.out - r.recv >= capacity * hidden * 2 and r.origin - r.out >= capacity * hidden * 2
+    assert r.ret - r.origin >= capacity * 8 and r.bytes - r.ret >= slots * hidden * 2
+    for offset in (r.counts, r.send_base, r.recv_offs):
+        assert offset % 256 == 0
+    for offset in (r.recv, r.out, r.origin, r.ret, r.bytes):
+        assert offset % 1024 == 0
+    for bad in ((0, experts, hidden, capacity, slots, 2), (_native.EP_MAX_WORLD + 1, 256, 8, 8, 8, 2),
+                (3, 256, hidden, capacity, slots, 2), (world, experts, 0, capacity, slots, 2),
+                (world, experts, hidden, -1, slots, 2), (world, experts, hidden, capacity, -1, 2)):
+        with pytest.raises(_native.NativeLaunchError, match="invalid argument"):
+            _native.ep_region_layout(*bad)

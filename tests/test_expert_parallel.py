@@ -366,6 +366,66 @@ def test_route_permute_combine_kernels():
     assert err < BF16_TOL, err
 
 
+@pytest.mark.gpu
+@pytest.mark.skipif(not cuda_ready(), reason="needs a CUDA GPU")
+def test_peer_that_never_arrives_times_out_and_reports():
+    """A two-rank configuration on one GPU whose second rank never runs (its
+    region is a second local allocation nothing signals from): every barrier
+    gives up after its 50 ms deadline and reports error bit 9, the exchange
+    drops every slot instead of writing anywhere, and the context stays usable."""
+    _setup_paths()
+    from kernels import _native, launch_grouped_mm
+
+    world, experts, hidden, top_k, tokens = 2, 4, 64, 2, 8
+    slots = tokens * top_k
+    capacity = world * slots
+    layout = _native.ep_region_layout(world, experts, hidden, capacity, slots, 2)
+    own, _ = _native.ep_shared_alloc(layout.bytes, with_handle=False)
+    silent, _ = _native.ep_shared_alloc(layout.bytes, with_handle=False)
+    try:
+        _native.read_and_clear_error_word(0)
+        peers = torch.tensor([own, silent], dtype=torch.int64, device="cuda")
+        cfg = _native.EpConfig(0, world, experts, 2, hidden, capacity, 50_000_000, slots)
+        gen = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn((tokens, hidden), device="cuda", generator=gen).to(torch.bfloat16)
+        ids = torch.randint(0, experts, (tokens, top_k), device="cuda", generator=gen, dtype=torch.int32)
+        w = torch.rand((tokens, top_k), device="cuda", generator=gen)
+        counts = torch.zeros(experts, dtype=torch.int32, device="cuda")
+        position = torch.empty(slots, dtype=torch.int32, device="cuda")
+        out = torch.full((tokens, hidden), 7.0, dtype=torch.bfloat16, device="cuda")
+        stream = torch.cuda.current_stream().cuda_stream
+        _native.route_layout(ids.data_ptr(), tokens, top_k, experts, counts.data_ptr(), position.data_ptr(), stream)
+        _native.ep_exchange_counts(counts.data_ptr(), peers.data_ptr(), cfg, stream)
+        _native.ep_dispatch(x.data_ptr(), hidden, ids.data_ptr(), position.data_ptr(), tokens, top_k,
+                            peers.data_ptr(), cfg, stream)
+        _native.ep_combine(ids.data_ptr(), w.data_ptr(), position.data_ptr(), tokens, top_k, peers.data_ptr(), cfg,
+                           out.data_ptr(), hidden, stream)
+        torch.cuda.synchronize()
+        word = _native.read_and_clear_error_word(0)
+        assert word & (1 << 9), _native.describe_error_word(word)
+        assert torch.count_nonzero(out.float()) == 0, "a failed exchange must drop every slot"
+        send_base = torch.as_tensor(_view_int32(own + layout.send_base, experts))
+        assert torch.all(send_base == capacity)
+        # The context still computes.
+        a = torch.randn((96, 64), device="cuda", generator=gen).to(torch.bfloat16)
+        b = torch.randn((2, 64, 128), device="cuda", generator=gen).to(torch.bfloat16)
+        offs = torch.tensor([40, 96], dtype=torch.int32, device="cuda")
+        got = launch_grouped_mm(a, b, offs)
+        expected = torch.cat((a[:40].float() @ b[0].float(), a[40:].float() @ b[1].float()))
+        assert torch.allclose(got.float(), expected, rtol=2e-2, atol=2e-2)
+        assert _native.read_and_clear_error_word(0) == 0
+    finally:
+        torch.cuda.synchronize()
+        _native.ep_shared_free(own)
+        _native.ep_shared_free(silent)
+
+
+def _view_int32(ptr, count):
+    from expert_parallel import _view
+
+    return _view(ptr, (count,), "<i4", torch.device("cuda", 0))
+
+
 def _two_rank_worker(rank, world, port, result_dir):
     _setup_paths()
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
