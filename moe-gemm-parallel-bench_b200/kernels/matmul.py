@@ -290,11 +290,12 @@ def native_candidates(max_m: int, max_k: int | None = None) -> tuple[KernelConfi
     rows), 128-token x 256-column tiles at M <= 128, and CTA-pair tiles beyond.
     The 256 x 512 pair tile moves 25% fewer bytes from L2 per MMA than the
     256 x 256 one but has a single TMEM accumulator (no epilogue overlap) and
-    half as many tiles.  It wins from M = 512, and at M = 256 on short K
-    (K <= 1024: W2 TP, K = 256), where the epilogue dominates and half as
-    many tiles halve the per-problem tensor-map rebuilds; at M = 256 with
-    longer K (W13, K = 7168; W2 EP, K = 2048) the 256 x 256 tile's overlapped
-    epilogue wins.  Timing candidates alone at boost clocks (the reference's hot
+    half as many tiles.  It wins from M = 512; at M = 256 the 256 x 256
+    tile's overlapped epilogue wins (W13, K = 7168; W2 EP, K = 2048).  On
+    short K (K <= 1024: W2 TP, K = 256) the epilogue dominates every tile and
+    the 128 x 256 one-CTA tile, whose two accumulators let the epilogue of one
+    tile run under the next tile's MMAs, beats both pair tiles at every M
+    above 128 (4-8% on whole W2 TP steps).  Timing candidates alone at boost clocks (the reference's hot
     autotune) picks tiles that lose once the GPU is power-capped, so the
     policy is fixed rather than re-timed per shape.
     """
@@ -306,7 +307,9 @@ def native_candidates(max_m: int, max_k: int | None = None) -> tuple[KernelConfi
         return (TILE_SWAP_64x256,)
     if max_m <= 128:
         return (TILE_TOKENS_128x256,)
-    if max_m > 256 or (max_k is not None and max_k <= 1024):
+    if max_k is not None and max_k <= 1024:
+        return (TILE_TOKENS_128x256,)
+    if max_m > 256:
         return (TILE_PAIR_256x512,)
     return (TILE_PAIR_256x256,)
 

@@ -138,7 +138,8 @@ def test_native_tile_policy():
     assert native_candidates(256) == (mm.TILE_PAIR_256x256,)
     assert native_candidates(256, 2048) == (mm.TILE_PAIR_256x256,)
     assert native_candidates(1024, 2048) == (mm.TILE_PAIR_256x512,)
-    assert native_candidates(256, 256) == (mm.TILE_PAIR_256x512,)
+    assert native_candidates(256, 256) == (mm.TILE_TOKENS_128x256,)
+    assert native_candidates(1024, 256) == (mm.TILE_TOKENS_128x256,)
     assert native_candidates(512, 7168) == (mm.TILE_PAIR_256x512,)
     assert native_candidates(1024) == (mm.TILE_PAIR_256x512,)
 
