@@ -32,7 +32,9 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REFERENCE = Path(os.environ.get("REFERENCE_PATH", "/root/reference"))
+if "REFERENCE_PATH" not in os.environ:
+    raise SystemExit("set REFERENCE_PATH to the reference checkout (see the module docstring)")
+REFERENCE = Path(os.environ["REFERENCE_PATH"])
 
 
 def _import_reference():

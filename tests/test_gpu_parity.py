@@ -714,7 +714,7 @@ def _sampled_rows_check(ws, dtype_name, rows_per_problem=24, seed=0, gate_up=Fal
 @pytest.mark.parametrize("proj,k,n", [("W13_EP", 7168, 4096), ("W13_TP", 7168, 512), ("W2_EP", 2048, 7168),
                                       ("W2_TP", 256, 7168)])
 def test_deepseek_v3_rank_shapes(m_e, proj, k, n):
-    """DeepSeek-V3 P=8 rank shapes with 3 experts, the autotuned
+    """DeepSeek-V3 P=8 rank shapes (utils/metrics.py:40-72) with 3 experts, the autotuned
     launch, A ~ N(0,1), B ~ N(0, 1/sqrt(K)); oracle on sampled rows."""
     torch = _torch()
     from kernels import check_device_errors, launch_grouped
