@@ -518,6 +518,43 @@ def test_aggregate_layout_uneven_experts_every_tile(dtype_name):
         _aggregate_check(out, mat_a, mat_b, sizes, dtype_name)
 
 
+def test_aggregate_segments_sharing_expert_weights():
+    """offs with S = P * E segments (P senders' blocks, each sorted by the E
+    experts, as an expert-parallel rank receives them): segment s multiplies
+    mat_b[s % E] (grouped_gemm_offsets_launch_ex, b_count = E), for a plain
+    and a scattered output."""
+    torch = _torch()
+    from kernels import KernelConfig, launch_grouped_mm, launch_grouped_mm_scatter
+    from oracle import gemm as oracle
+
+    experts, k, n = 3, 128, 264
+    sizes = [5, 0, 70, 33, 12, 0, 1, 130, 9]  # 3 senders x 3 experts
+    gen = torch.Generator(device="cuda").manual_seed(17)
+    total = sum(sizes)
+    mat_a = _randn((total, k), torch.bfloat16, gen, 1.0)
+    mat_b = _randn((experts, k, n), torch.bfloat16, gen, 0.1)
+    offs = torch.tensor(np.cumsum(sizes), device="cuda", dtype=torch.int32)
+    starts = np.concatenate([[0], np.cumsum(sizes)[:-1]])
+    for cfg in (KernelConfig(16, 256, 64, 4, 8, 4), KernelConfig(128, 256, 64, 8, 8, 4),
+                KernelConfig(256, 128, 64, 8, 8, 4)):
+        out = launch_grouped_mm(mat_a, mat_b, offs, config=cfg)
+        dst = torch.zeros((total, n), dtype=torch.bfloat16, device="cuda")
+        peers = torch.tensor([dst.data_ptr()], dtype=torch.int64, device="cuda")
+        origin = torch.arange(total - 1, -1, -1, dtype=torch.int64, device="cuda")  # reversed rows
+        launch_grouped_mm_scatter(mat_a, mat_b, offs, origin, peers, 0, n * 2, config=cfg)
+        torch.cuda.synchronize()
+        host_out, host_dst = _host(out), _host(dst)
+        for s_idx, (start, size) in enumerate(zip(starts, sizes)):
+            if size == 0:
+                continue
+            a = _host(mat_a[start:start + size])
+            expected = oracle.matmul(a, _host(mat_b[s_idx % experts]), "bf16")
+            got = host_out[start:start + size]
+            assert oracle.relative_frobenius(got, expected) <= REL_FRO["bf16"], (cfg, s_idx)
+            scattered = host_dst[total - start - size:total - start][::-1]
+            assert np.array_equal(scattered, got), (cfg, s_idx)
+
+
 def test_aggregate_layout_padding_precisions_and_swiglu():
     """Padded row pitches (C not TMA-addressable -> staged stores), fp32 on the
     generic kernel and on TF32 tensor cores, the fused SwiGLU epilogue, and a
