@@ -171,10 +171,25 @@ int simt_launch_typed(int dtype, const GroupedParams& p, int grid, cudaStream_t 
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
-// Upper bound on the tiles of a launch: problems x tiles of the largest problem.
-int grid_for(int64_t problems, int64_t m, int64_t n, int tm, int tn, int64_t cap) {
+// Persistent grid for `tiles` schedule units and at most `cap` schedulers.
+// With an exact tile count the grid is wave-balanced: the fewest schedulers
+// that still finish in ceil(tiles / cap) rounds, so every scheduler walks the
+// same number of tiles (512 tiles on 148 SMs: 128 CTAs x 4 rather than
+// 148 CTAs of which 68 take a fourth tile while the rest idle).  An upper
+// bound (ragged groups) keeps min(tiles, cap): balancing against an
+// overestimate could add a round to the real walk.
+int grid_of(int64_t tiles, int64_t cap, bool exact) {
+  cap = std::max<int64_t>(1, cap);
+  tiles = std::max<int64_t>(1, tiles);
+  if (!exact) return static_cast<int>(std::min<int64_t>(tiles, cap));
+  const int64_t rounds = cdiv(tiles, cap);
+  return static_cast<int>(std::min<int64_t>(cdiv(tiles, rounds), cap));
+}
+
+// Tiles of a launch: problems x tiles of the largest problem.
+int grid_for(int64_t problems, int64_t m, int64_t n, int tm, int tn, int64_t cap, bool exact) {
   const int64_t tiles = problems * cdiv(std::max<int64_t>(m, 1), tm) * cdiv(std::max<int64_t>(n, 1), tn);
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(tiles, cap)));
+  return grid_of(tiles, cap, exact);
 }
 
 // Tiles per schedule unit for a grouped tensor-core launch (see TileWalk):
@@ -272,8 +287,8 @@ struct TileBound {
   }
 };
 
-int grid_from(const TileBound& b, int tm, int tn, int64_t n, int64_t cap) {
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(b.tiles(tm, tn, n), cap)));
+int grid_from(const TileBound& b, int tm, int tn, int64_t n, int64_t cap, bool exact) {
+  return grid_of(b.tiles(tm, tn, n), cap, exact);
 }
 
 // The launch of a filled GroupedParams (tables or aggregate layout): the
@@ -299,8 +314,10 @@ int launch_grouped_params(GroupedParams& p, const DeviceState& ds, const TileBou
     }
     TcVariantInfo vi;
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
-    const int grid = v.pair ? 2 * grid_from(bound, v.tm, v.tn, n, std::max(1, vi.max_clusters))
-                            : grid_from(bound, v.tm, v.tn, n, ds.sm_count);
+    // Single and homogeneous groups know their tile count exactly.
+    const bool exact = p.single || p.homogeneous;
+    const int grid = v.pair ? 2 * grid_from(bound, v.tm, v.tn, n, std::max(1, vi.max_clusters), exact)
+                            : grid_from(bound, v.tm, v.tn, n, ds.sm_count, exact);
     const size_t maps_bytes = static_cast<size_t>(p.problem_count) * kMapsPerProblem * kMapBytes;
     const size_t need = maps_bytes + (static_cast<size_t>(p.problem_count) + 1) * sizeof(int64_t);
     if (scratch == nullptr || scratch_bytes < need || reinterpret_cast<uintptr_t>(scratch) % 128 != 0) {
@@ -338,7 +355,7 @@ int launch_grouped_params(GroupedParams& p, const DeviceState& ds, const TileBou
     fill_info(info, 0, v, vi, grid);
     return MGB_OK;
   }
-  const int grid = grid_from(bound, mgb::kSimtBM, mgb::kSimtBN, n, 4ll * ds.sm_count);
+  const int grid = grid_from(bound, mgb::kSimtBM, mgb::kSimtBN, n, 4ll * ds.sm_count, false);
   const int e = simt_launch_typed(dtype, p, grid, s);
   if (e != 0) return MGB_ERR_CUDA;
   fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0}, grid);
@@ -578,8 +595,9 @@ int grouped_gemm_fp8_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const 
   // (contiguous A [M, K], B [N, K], C [M, N]), so no stride table is read.
 
   const TileBound bound{problem_count, m, 0};
-  const int grid = v.pair ? 2 * grid_from(bound, v.tm, v.tn, n, std::max(1, vi.max_clusters))
-                          : grid_from(bound, v.tm, v.tn, n, ds.sm_count);
+  const bool exact = homogeneous != 0;
+  const int grid = v.pair ? 2 * grid_from(bound, v.tm, v.tn, n, std::max(1, vi.max_clusters), exact)
+                          : grid_from(bound, v.tm, v.tn, n, ds.sm_count, exact);
   const size_t maps_bytes = static_cast<size_t>(problem_count) * kMapsPerProblem * kMapBytes;
   const size_t need = maps_bytes + (static_cast<size_t>(problem_count) + 1) * sizeof(int64_t);
   if (scratch == nullptr || scratch_bytes < need || reinterpret_cast<uintptr_t>(scratch) % 128 != 0) {
@@ -667,14 +685,14 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
                 : encode_out(&out, dtype, a, 128 / es, 32, 128))) {
       return MGB_ERR_CUDA;
     }
-    const int grid = v.pair ? 2 * grid_for(1, m, n, v.tm, v.tn, std::max(1, vi.max_clusters))
-                            : grid_for(1, m, n, v.tm, v.tn, ds.sm_count);
+    const int grid = v.pair ? 2 * grid_for(1, m, n, v.tm, v.tn, std::max(1, vi.max_clusters), true)
+                            : grid_for(1, m, n, v.tm, v.tn, ds.sm_count, true);
     const int e = tc_launch_typed(dtype, v, act, wgt, out, p, grid, s);
     if (e != 0) return MGB_ERR_CUDA;
     fill_info(info, 0, v, vi, grid);
     return MGB_OK;
   }
-  const int grid = grid_for(1, m, n, mgb::kSimtBM, mgb::kSimtBN, 4ll * ds.sm_count);
+  const int grid = grid_for(1, m, n, mgb::kSimtBM, mgb::kSimtBN, 4ll * ds.sm_count, false);
   const int e = simt_launch_typed(dtype, p, grid, s);
   if (e != 0) return MGB_ERR_CUDA;
   fill_info(info, 1, TcVariant{false, 0, 0}, TcVariantInfo{0, 0, 0}, grid);
