@@ -43,6 +43,14 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Relaxed arrive (no release fence) for arrivals that only report finished
+// TMEM reads: tcgen05.wait::ld has completed them and
+// tcgen05.fence::before_thread_sync orders them before the arrive, so no
+// memory needs publishing and the release would only stall the warp.
+__device__ __forceinline__ void mbar_arrive_relaxed(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.relaxed.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t done;
   asm volatile(
@@ -288,12 +296,8 @@ __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
-// Arrive on an mbarrier anywhere in the cluster (address from mapa_shared).
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
-}
-
-// Relaxed arrive on an mbarrier anywhere in the cluster: no release fence.  For
+// Relaxed arrive on an mbarrier anywhere in the cluster (address from
+// mapa_shared): no release fence.  For
 // arrivals that only report finished TMEM reads (tcgen05.wait::ld has
 // completed them, and tcgen05.fence::before_thread_sync orders them), where a
 // release at cluster scope would stall the warp on every arrival.

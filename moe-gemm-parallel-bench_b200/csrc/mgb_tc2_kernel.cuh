@@ -311,7 +311,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[buf]), 0));
+      if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&acc_empty[buf]), 0));
       ++acc_it;
     }
     if (lane == 0) bulk_wait_group_all();  // tensor stores done before the CTA's shared memory goes away

@@ -862,7 +862,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
               }
             }
             tc_fence_before();
-            mbar_arrive(&acc_empty[buf]);
+            mbar_arrive_relaxed(&acc_empty[buf]);
             ++acc_it;
             continue;
           }
@@ -920,7 +920,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[buf]);
+      mbar_arrive_relaxed(&acc_empty[buf]);
       ++acc_it;
     }
     if (lane == 0) bulk_wait_group_all();  // tensor stores done before the CTA's shared memory goes away
