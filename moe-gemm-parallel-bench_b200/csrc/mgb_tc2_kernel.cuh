@@ -16,7 +16,11 @@
 //                (the even CTA's producer posts the expected byte count);
 //   empty[s]     in each CTA: the MMA commit multicasts to both;
 //   acc_full[b]  in each CTA: the MMA commit multicasts to both epilogues;
-//   acc_empty[b] in CTA 0 only: the 8 epilogue warps of the pair arrive.
+//   acc_empty[b] in CTA 0 only: the 8 epilogue warps of the pair arrive.  The
+//                256 x 256 tile double-buffers its accumulator (b = buffer);
+//                the 256 x 512 tile's single accumulator is freed by halves
+//                (b = 256-column half), so the next tile's half-0 MMAs of its
+//                first k-blocks run while the epilogue still drains half 1.
 // Every wait is bounded; loads carry no multicast.
 #pragma once
 
@@ -208,14 +212,56 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         if (!tile_legal<T>(p, q) || q.k <= 0) continue;
         const int64_t kblocks = (q.k + BK - 1) / BK;
         const int buf = static_cast<int>(acc_it % NB);
-        if (!mbar_wait(&acc_empty[buf], ((acc_it / NB) & 1u) ^ 1u, budget, abort)) {
+        const uint32_t acc_phase = ((acc_it / NB) & 1u) ^ 1u;
+        if (!mbar_wait(&acc_empty[buf], acc_phase, budget, abort)) {
           raise_error(p, kErrWaitAccEmpty, abort);
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * Cfg::kAccCols);
-        for (int64_t kb = 0; kb < kblocks; ++kb) {
+        // MMAs of one 256-column half h over the four k-steps of stage s.
+        auto issue_half = [&](int s, int h, bool first_kb) {
+          const uint32_t a_base = smem_u32(ring + s * Cfg::kStageBytes);
+          const uint32_t w_base = a_base + Cfg::kActBytes + h * Cfg::kHalfWgtBytes;
+#pragma unroll
+          for (int ks = 0; ks < Cfg::kKSteps; ++ks) {
+            const uint64_t act_desc = smem_desc(a_base + ks * 32, 16, 1024, kLayoutSw128);
+            const uint64_t wgt_desc = smem_desc(w_base + ks * Cfg::kKStep * 128, Cfg::kBoxBytes, 1024, kLayoutSw128);
+            mma_f16_pair(d_tmem + h * 256, act_desc, wgt_desc, Cfg::kIdesc, (!first_kb || ks > 0) ? 1u : 0u);
+          }
+        };
+        int64_t held = 0;
+        if constexpr (NH == 2) {
+          // Half 0 is free (acc_empty[0]): run the half-0 MMAs of the first
+          // `held` k-blocks, keeping their stages, then wait for half 1
+          // (acc_empty[1]) and finish those k-blocks before the usual order.
+          held = kblocks < S ? kblocks : S;
+          for (int64_t kb = 0; kb < held; ++kb) {
+            const uint32_t j = it + static_cast<uint32_t>(kb);
+            if (!mbar_wait(&full[j % S], (j / S) & 1u, budget, abort)) {
+              raise_error(p, kErrWaitFull, abort);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_half(static_cast<int>(j % S), 0, kb == 0);
+          }
+          if (!ok) break;
+          if (!mbar_wait(&acc_empty[1], acc_phase, budget, abort)) {
+            raise_error(p, kErrWaitAccEmpty, abort);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          for (int64_t kb = 0; kb < held; ++kb) {
+            const int s = static_cast<int>((it + static_cast<uint32_t>(kb)) % S);
+            issue_half(s, 1, kb == 0);
+            mma_commit_pair(&empty[s], 0x3);  // frees stage s in both CTAs
+          }
+          it += static_cast<uint32_t>(held);
+        }
+        for (int64_t kb = held; kb < kblocks; ++kb) {
           const int s = static_cast<int>(it % S);
           if (!mbar_wait(&full[s], (it / S) & 1u, budget, abort)) {
             raise_error(p, kErrWaitFull, abort);
@@ -301,6 +347,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         } else {
           store_rows_scalar_swiglu<T, Cfg::kTileN / 2>(q, taddr, m0 + quarter * 32, n0, lane);
         }
+      } else if (NH == 2 && (p.scatter_origin != nullptr || cmap != nullptr)) {
+        // By halves: each 256-column half is released as soon as it is drained.
+        const int64_t row0 = m0 + quarter * 32;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t th = taddr + static_cast<uint32_t>(h * 256);
+          const int64_t nh = n0 + h * 256;
+          if (p.scatter_origin != nullptr) {
+            store_rows_scatter<T, 256>(p, q, th, row0, nh, my_blocks, lane);
+          } else {
+            store_rows_tma<T, 256, Cfg::kEpiBlocks>(q, cmap, th, static_cast<int32_t>(row0), static_cast<int32_t>(nh),
+                                                    my_blocks, lane, chunk_seq, pol_out, p.error_word);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&acc_empty[h]), 0));
+        }
+        ++acc_it;
+        continue;
       } else if (p.scatter_origin != nullptr) {
         store_rows_scatter<T, Cfg::kTileN>(p, q, taddr, m0 + quarter * 32, n0, my_blocks, lane);
       } else if (cmap != nullptr) {
@@ -311,7 +376,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&acc_empty[buf]), 0));
+      if (lane == 0) {
+        if constexpr (NH == 2) {
+          // Drained as a whole (SwiGLU pairs columns across the halves): free both.
+          mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&acc_empty[0]), 0));
+          mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&acc_empty[1]), 0));
+        } else {
+          mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&acc_empty[buf]), 0));
+        }
+      }
       ++acc_it;
     }
     if (lane == 0) bulk_wait_group_all();  // tensor stores done before the CTA's shared memory goes away
