@@ -192,6 +192,23 @@ int grid_for(int64_t problems, int64_t m, int64_t n, int tm, int tn, int64_t cap
   return grid_of(tiles, cap, exact);
 }
 
+// A CTA-pair 256 x 512 launch with an exact tile count, one tile per unit and
+// a last wave at most half full: that wave's tiles run as two 256-column half
+// items each (GroupedParams::tail_split), one item per cluster, on every
+// cluster the device holds, instead of one more round of wide tiles.  Returns
+// the grid (CTAs) to launch; other launches keep `grid` and no split.
+int tail_split_grid(GroupedParams& p, bool pair, int tn, int64_t tiles, int max_clusters, int grid) {
+  if (!pair || tn != 512 || p.swiglu || p.scatter_origin != nullptr || p.unit_tiles > 1 || max_clusters <= 0) {
+    return grid;
+  }
+  const int64_t rem = tiles % max_clusters;
+  if (rem == 0 || 2 * rem > max_clusters) return grid;
+  p.tail_split = 1;
+  p.tail_from = tiles - rem;
+  const int64_t items = p.tail_from + 2 * rem;
+  return static_cast<int>(2 * std::min<int64_t>(max_clusters, items));
+}
+
 // Tiles per schedule unit for a grouped tensor-core launch (see TileWalk):
 // enough tiles that a unit holds about 16 k-blocks of MMA work, so the
 // per-problem tensor-map rebuild is amortised, but no more than keeps 16
@@ -316,8 +333,8 @@ int launch_grouped_params(GroupedParams& p, const DeviceState& ds, const TileBou
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
     // Single and homogeneous groups know their tile count exactly.
     const bool exact = p.single || p.homogeneous;
-    const int grid = v.pair ? 2 * grid_from(bound, v.tm, v.tn, n, std::max(1, vi.max_clusters), exact)
-                            : grid_from(bound, v.tm, v.tn, n, ds.sm_count, exact);
+    int grid = v.pair ? 2 * grid_from(bound, v.tm, v.tn, n, std::max(1, vi.max_clusters), exact)
+                      : grid_from(bound, v.tm, v.tn, n, ds.sm_count, exact);
     const size_t maps_bytes = static_cast<size_t>(p.problem_count) * kMapsPerProblem * kMapBytes;
     const size_t need = maps_bytes + (static_cast<size_t>(p.problem_count) + 1) * sizeof(int64_t);
     if (scratch == nullptr || scratch_bytes < need || reinterpret_cast<uintptr_t>(scratch) % 128 != 0) {
@@ -325,6 +342,7 @@ int launch_grouped_params(GroupedParams& p, const DeviceState& ds, const TileBou
     }
     p.desc_slots = static_cast<uint8_t*>(scratch);
     p.unit_tiles = unit_tiles_for(bound.tiles(v.tm, v.tn, n), k, vi.bk, v.pair ? grid / 2 : grid);
+    if (exact) grid = tail_split_grid(p, v.pair, v.tn, bound.tiles(v.tm, v.tn, n), vi.max_clusters, grid);
     if (!p.homogeneous && !p.single) {
       // Heterogeneous groups: the map builder also writes the walk's unit
       // prefix sums after the maps, for this tile shape.
@@ -685,8 +703,9 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
                 : encode_out(&out, dtype, a, 128 / es, 32, 128))) {
       return MGB_ERR_CUDA;
     }
-    const int grid = v.pair ? 2 * grid_for(1, m, n, v.tm, v.tn, std::max(1, vi.max_clusters), true)
-                            : grid_for(1, m, n, v.tm, v.tn, ds.sm_count, true);
+    int grid = v.pair ? 2 * grid_for(1, m, n, v.tm, v.tn, std::max(1, vi.max_clusters), true)
+                      : grid_for(1, m, n, v.tm, v.tn, ds.sm_count, true);
+    grid = tail_split_grid(p, v.pair, v.tn, cdiv(m, v.tm) * cdiv(n, v.tn), vi.max_clusters, grid);
     const int e = tc_launch_typed(dtype, v, act, wgt, out, p, grid, s);
     if (e != 0) return MGB_ERR_CUDA;
     fill_info(info, 0, v, vi, grid);

@@ -45,6 +45,12 @@ struct GroupedParams {
   int32_t b_count;  // > 0: problem e uses B[e % b_count] (segments of several senders share an expert)
   int32_t elem_bytes;
   int32_t unit_tiles;     // tensor-core kernels: consecutive tiles of one problem a CTA takes at a time
+  // CTA-pair 256 x 512 launches with an exact tile count and one tile per
+  // unit: tail_split = 1 splits every global tile from tail_from on into two
+  // 256 x 256 items (one per 256-column half), so a short last wave of wide
+  // tiles runs as at most one half-width item per cluster.  0: no split.
+  int32_t tail_split;
+  int64_t tail_from;
   // Heterogeneous tensor-core launches: unit_start[e] = units of problems
   // [0, e) (E + 1 entries, written by the map builder before the GEMM kernel
   // runs) for the tile shape walk_tm x walk_tn, so the walk finds a unit's

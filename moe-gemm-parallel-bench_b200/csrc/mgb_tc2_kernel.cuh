@@ -70,6 +70,30 @@ struct Tc2Cfg {
   static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
+// This cluster's next work item (items first, first + stride, ...).  Without
+// a tail split an item is one tile of the unit walk (half = -1).  With one
+// (256 x 512 tile, exact tile count, one tile per unit) item i below
+// p.tail_from is global tile i, and from there on consecutive items are the
+// two 256-column halves (half = 0, 1) of one tile: a half item accumulates in
+// TMEM columns [0, 256) from the weight columns of its half, which the
+// producer loads into the first weight slot of the stage.
+template <int NH, class Walk>
+__device__ __forceinline__ bool next_item(Walk& walk, const GroupedParams& p, int64_t first, int64_t stride,
+                                          int64_t& item, int64_t& t, int& half) {
+  half = -1;
+  if (NH != 2 || !p.tail_split) return walk.next_tile(p, first, stride, t);
+  item = item < 0 ? first : item + stride;
+  int64_t tile = item;
+  if (item >= p.tail_from) {
+    tile = p.tail_from + ((item - p.tail_from) >> 1);
+    half = static_cast<int>((item - p.tail_from) & 1);
+  }
+  int64_t t0 = 0, t1 = 0;
+  if (!walk.seek_unit(p, tile, 1, t0, t1)) return false;
+  t = t0;
+  return true;
+}
+
 template <typename T, int NH>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     tc2_grouped_kernel(const __grid_constant__ CUtensorMap act_tmpl, const __grid_constant__ CUtensorMap wgt_tmpl,
@@ -145,7 +169,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     uint32_t it = 0;
     int built = -1;
     bool ok = true;
-    for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
+    int64_t item = -1;
+    int half = -1;
+    for (int64_t t = 0; ok && next_item<NH>(walk, p, cluster, clusters, item, t, half);) {
       const Problem& q = walk.prob;
       if (!tile_legal<T>(p, q)) {
         if (lane == 0 && walk.problem != built) atomicOr(p.error_word, kErrMisaligned);
@@ -179,15 +205,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
           uint8_t* st_wgt = st_act + Cfg::kActBytes;
           const int32_t kx = static_cast<int32_t>(kb * BK);
           const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
-          if (leader) mbar_arrive_expect_tx(&full[s], 2 * Cfg::kStageBytes);
+          // A half item loads one 256-column half of weights (into slot 0).
+          const int slots = half < 0 ? NH : 1;
+          if (leader) mbar_arrive_expect_tx(&full[s], 2 * (Cfg::kActBytes + slots * Cfg::kHalfWgtBytes));
           tma_load_2d_pair(act_map, bar, st_act, kx, m0, pol_act);
 #pragma unroll
           for (int h = 0; h < NH; ++h) {
+            if (h >= slots) break;
+            const int hc = half < 0 ? h : half;  // weight half loaded into slot h
 #pragma unroll
             for (int j = 0; j < Cfg::kHalf / BK; ++j) {
-              // Tile-local column 256 h + 128 rank + 64 j (CTA rank's half of MMA half h).
+              // Tile-local column 256 hc + 128 rank + 64 j (CTA rank's half of MMA half hc).
               tma_load_2d_pair(wgt_map, bar, st_wgt + h * Cfg::kHalfWgtBytes + j * Cfg::kBoxBytes,
-                               weight_col<Cfg::kTileN>(p, q, nb, 256 * h + Cfg::kHalf * rank + j * BK), kx,
+                               weight_col<Cfg::kTileN>(p, q, nb, 256 * hc + Cfg::kHalf * rank + j * BK), kx,
                                pol_wgt);
             }
           }
@@ -212,7 +242,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       uint32_t it = 0;
       uint32_t acc_it = 0;
       bool ok = true;
-      for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
+      int64_t item = -1;
+      int half = -1;
+      for (int64_t t = 0; ok && next_item<NH>(walk, p, cluster, clusters, item, t, half);) {
         const Problem& q = walk.prob;
         if (!tile_legal<T>(p, q) || q.k <= 0) continue;
         const int64_t kblocks = (q.k + BK - 1) / BK;
@@ -236,6 +268,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
             mma_f16_pair(d_tmem + h * 256, act_desc, wgt_desc, Cfg::kIdesc, (!first_kb || ks > 0) ? 1u : 0u);
           }
         };
+        if (NH == 2 && half >= 0) {
+          // Half item: every k-block on accumulator half 0 (free above).
+          for (int64_t kb = 0; kb < kblocks; ++kb) {
+            const int s = static_cast<int>(it % S);
+            if (!mbar_wait(&full[s], (it / S) & 1u, budget, abort)) {
+              raise_error(p, kErrWaitFull, abort);
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_half(s, 0, kb == 0);
+            mma_commit_pair(&empty[s], 0x3);
+            ++it;
+          }
+          if (!ok) break;
+          // The epilogue arrives on both halves' barriers every item; wait on
+          // half 1 as well (before this item's accumulator-full commit, so
+          // that barrier is never two phases ahead of this wait).
+          if (!mbar_wait(&acc_empty[1], acc_phase, budget, abort)) {
+            raise_error(p, kErrWaitAccEmpty, abort);
+            ok = false;
+            break;
+          }
+          mma_commit_pair(&acc_full[buf], 0x3);
+          ++acc_it;
+          continue;
+        }
         int64_t held = 0;
         if constexpr (NH == 2) {
           // Half 0 is free (acc_empty[0]): run the half-0 MMAs of the first
@@ -313,7 +372,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     const uint64_t pol_out = policy_evict_first();
     uint32_t chunk_seq = 0;
     bool ok = true;
-    for (int64_t t = 0; ok && walk.next_tile(p, cluster, clusters, t);) {
+    int64_t item = -1;
+    int half = -1;
+    for (int64_t t = 0; ok && next_item<NH>(walk, p, cluster, clusters, item, t, half);) {
       if (!tile_legal<T>(p, walk.prob)) continue;
       Problem q = walk.prob;
       q.n = out_cols(p, q);  // the epilogue addresses C: N/2 columns with SwiGLU
@@ -344,6 +405,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       tc_fence_after();
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                              static_cast<uint32_t>(buf * Cfg::kAccCols);
+      if (NH == 2 && half >= 0) {
+        // Half item: TMEM half 1 is unused, free it at once; half 0 holds
+        // output columns [n0 + 256 half, + 256).
+        if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&acc_empty[1]), 0));
+        const int64_t row0 = m0 + quarter * 32;
+        const int64_t nh = n0 + half * 256;
+        if (p.scatter_origin != nullptr) {
+          store_rows_scatter<T, 256>(p, q, taddr, row0, nh, my_blocks, lane);
+        } else if (cmap != nullptr) {
+          store_rows_tma<T, 256, Cfg::kEpiBlocks>(q, cmap, taddr, static_cast<int32_t>(row0), static_cast<int32_t>(nh),
+                                                  my_blocks, lane, chunk_seq, pol_out, p.error_word);
+        } else {
+          store_rows_staged<T, 256>(q, taddr, row0, nh, my_blocks, lane);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster_relaxed(mapa_shared(smem_u32(&acc_empty[0]), 0));
+        ++acc_it;
+        continue;
+      }
       if (p.swiglu) {
         if (cmap != nullptr) {
           store_rows_tma_swiglu<T, Cfg::kTileN / 2, Cfg::kEpiBlocks>(q, cmap, taddr, static_cast<int32_t>(m0 + quarter * 32),

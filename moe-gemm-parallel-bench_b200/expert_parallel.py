@@ -155,7 +155,8 @@ class ExpertParallelMoE:
     def tile_configs(self, tokens: int) -> tuple[KernelConfig, KernelConfig]:
         """Native tiles of the two grouped GEMMs for `tokens` per rank."""
         rows = expected_rows_per_expert(tokens, self.top_k, self.local_experts)
-        return native_candidates(rows, self.hidden)[0], native_candidates(rows, self.ffn)[0]
+        return (native_candidates(rows, self.hidden, split_tail=False)[0],
+                native_candidates(rows, self.ffn, split_tail=False)[0])
 
     def forward(self, x, topk_ids, topk_weights, out=None, *, configs=None, phase_events=None):
         """out [T, H] bf16 = sum_j topk_weights[t, j] * expert_{topk_ids[t, j]}(x[t]).
@@ -288,7 +289,8 @@ class NcclAllToAllMoE:
 
     def tile_configs(self, tokens: int) -> tuple[KernelConfig, KernelConfig]:
         rows = expected_rows_per_expert(tokens, self.top_k, self.local_experts)
-        return native_candidates(rows, self.hidden)[0], native_candidates(rows, self.ffn)[0]
+        return (native_candidates(rows, self.hidden, split_tail=False)[0],
+                native_candidates(rows, self.ffn, split_tail=False)[0])
 
     def _all_to_all(self, out, inp, out_splits=None, in_splits=None):
         if self.world == 1:

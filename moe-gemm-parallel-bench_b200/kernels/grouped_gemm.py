@@ -434,7 +434,8 @@ def launch_grouped(
         workspace.shape_signature, workspace.problem_count, workspace.device_signature, workspace.homogeneous,
         aligned, input_precision, workspace.a[0].dtype,
     )
-    candidates = native_candidates(workspace.max_m, workspace.max_k)
+    candidates = native_candidates(workspace.max_m, workspace.max_k,
+                                   split_tail=workspace.homogeneous and workspace.operation != "swiglu")
     best, _ = autotune_over(
         candidates, lambda c: _launch_native(workspace, c, input_precision, aligned), key, _GROUPED_TUNED
     )
@@ -504,7 +505,7 @@ def launch_grouped_mm(mat_a, mat_b, offs, out=None, *, config: KernelConfig | No
         scratch = torch.empty(_native.scratch_bytes(segments, 0), dtype=torch.uint8, device=mat_a.device)
         _AGGREGATE_SCRATCH[key] = scratch
     global _last_aggregate_info
-    cfg = config or native_candidates(max(1, -(-total // segments)), k)[0]
+    cfg = config or native_candidates(max(1, -(-total // segments)), k, split_tail=False)[0]
     with torch.cuda.device(mat_a.device):
         info = _native.offsets_launch(
             mat_a.data_ptr(), mat_b.data_ptr(), out.data_ptr(), offs.data_ptr(), segments, total, n, k,
@@ -541,7 +542,7 @@ def launch_grouped_mm_scatter(mat_a, mat_b, offs, row_origin, peer_regions, dst_
     if scratch is None:
         scratch = torch.empty(_native.scratch_bytes(segments, 0), dtype=torch.uint8, device=mat_a.device)
         _AGGREGATE_SCRATCH[key] = scratch
-    cfg = config or native_candidates(max(1, -(-total // segments)), k)[0]
+    cfg = config or native_candidates(max(1, -(-total // segments)), k, split_tail=False)[0]
     with torch.cuda.device(mat_a.device):
         _native.offsets_scatter_launch(
             mat_a.data_ptr(), mat_b.data_ptr(), offs.data_ptr(), segments,

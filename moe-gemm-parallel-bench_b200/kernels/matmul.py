@@ -279,9 +279,11 @@ TILE_PAIR_256x256 = KernelConfig(256, 128, 64, 8, 8, 4)  # CTA pair for fp16/bf1
 TILE_PAIR_256x512 = KernelConfig(256, 256, 64, 8, 8, 4)  # CTA pair, two 256-column halves (fp16/bf16)
 
 
-def native_candidates(max_m: int, max_k: int | None = None) -> tuple[KernelConfig, ...]:
+def native_candidates(max_m: int, max_k: int | None = None, *, split_tail: bool = True) -> tuple[KernelConfig, ...]:
     """The native tile ``autotune=True`` launches for ``max_m`` token rows
-    (and reduction depth ``max_k``).
+    (and reduction depth ``max_k``).  ``split_tail`` says whether the launch
+    can run a short last wave of 256 x 512 tiles as half-width items (an
+    exact tile count: a single GEMM or a homogeneous group, no SwiGLU).
 
     Measured on B200 over whole DeepSeek-V3 W13 and W2 steps (``bench.py
     --tile-map``), where the GPU sits at its power cap and every launch's
@@ -289,9 +291,12 @@ def native_candidates(max_m: int, max_k: int | None = None) -> tuple[KernelConfi
     16 / 32 / 64 tokens x 256 weight columns, so no MMA work is spent on padding
     rows), 128-token x 256-column tiles at M <= 128, and CTA-pair tiles beyond.
     The 256 x 512 pair tile moves 25% fewer bytes from L2 per MMA than the
-    256 x 256 one but has a single TMEM accumulator (no epilogue overlap) and
-    half as many tiles.  It wins from M = 512; at M = 256 the 256 x 256
-    tile's overlapped epilogue wins (W13, K = 7168; W2 EP, K = 2048).  On
+    256 x 256 one but has a single TMEM accumulator, freed by halves (only
+    the first k-blocks of the next tile overlap the drain), and half as many
+    tiles; a short last wave of them runs as half-width items.  It wins from
+    M = 512, and at M = 256 on deep K (W13, K = 7168: 4% on the EP and TP
+    launches); at M = 256 with K = 2048 (W2 EP) the 256 x 256 tile's fully
+    overlapped epilogue keeps it level or ahead.  On
     short K (K <= 1024: W2 TP, K = 256) the epilogue dominates every tile and
     the 128 x 256 one-CTA tile, whose two accumulators let the epilogue of one
     tile run under the next tile's MMAs, beats both pair tiles at every M
@@ -315,7 +320,7 @@ def native_candidates(max_m: int, max_k: int | None = None) -> tuple[KernelConfi
         return (TILE_SWAP_64x256,)
     if max_m <= 128:
         return (TILE_TOKENS_128x256,)
-    if max_m > 256:
+    if max_m > 256 or (split_tail and max_k is not None and max_k >= 4096):
         return (TILE_PAIR_256x512,)
     return (TILE_PAIR_256x256,)
 

@@ -282,6 +282,54 @@ def test_pair_tiles_on_ragged_problems(dtype_name):
             _oracle_check(c, a, b, dtype_name)
 
 
+@pytest.mark.parametrize("dtype_name", ["fp16", "bf16"])
+@pytest.mark.parametrize("m,k,n", [(256, 320, 512), (200, 200, 384), (256, 128, 1536)])
+def test_wide_pair_tile_splits_a_short_last_wave(dtype_name, m, k, n):
+    """256 x 512 pair tiles on a homogeneous group whose last wave holds at
+    most half as many tiles as the device has clusters: each of those tiles
+    runs as two 256-column half items, one per cluster, and the launch uses
+    every cluster.  Ragged cases: M, K inside a block, and N = 384, whose
+    second half item holds 128 valid columns."""
+    torch = _torch()
+    from kernels import KernelConfig, check_device_errors, launch_grouped
+
+    clusters = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count // 2
+    n_blocks = -(-n // 512)
+    tail = max(1, clusters // 4)
+    problems = -(-(clusters + tail) // n_blocks)
+    tiles = problems * n_blocks
+    assert 0 < tiles % clusters <= clusters // 2
+    ws = _workspace([(m, k, n)] * problems, dtype_name, seed=21 + n)
+    assert ws.homogeneous
+    launch_grouped(ws, config=KernelConfig(256, 256, 64, 8, 8, 4), autotune=False)
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert ws.launch_info["path"] == "tcgen05_tma_pair" and ws.launch_info["tile_n"] == 512, ws.launch_info
+    assert ws.launch_info["grid"] == 2 * clusters, ws.launch_info
+    for a, b, c in ws.problem_tensors():
+        _oracle_check(c, a, b, dtype_name)
+
+
+@pytest.mark.parametrize("dtype_name", ["fp16", "bf16"])
+def test_wide_pair_tile_split_single_gemm(dtype_name):
+    """One masked GEMM on the 256 x 512 pair tile whose tile count leaves a
+    short last wave (half items), M ending inside a block."""
+    torch = _torch()
+    from kernels import KernelConfig, launch_matmul
+
+    clusters = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count // 2
+    m_blocks = 3
+    n_blocks = -(-(clusters + max(1, clusters // 8)) // m_blocks)
+    m, k, n = 256 * m_blocks - 40, 192, 512 * n_blocks
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    a = _randn((m, k), _dtype(dtype_name), gen)
+    b = _randn((k, n), _dtype(dtype_name), gen)
+    c = torch.full((m, n), float("nan"), device="cuda", dtype=_dtype(dtype_name))
+    launch_matmul(a, b, c, config=KernelConfig(256, 256, 64, 8, 8, 4), autotune=False)
+    torch.cuda.synchronize()
+    _oracle_check(c, a, b, dtype_name)
+
+
 def test_grouped_homogeneous_persistent_fast_path():
     """tests/test_gpu.py:117-125."""
     torch = _torch()

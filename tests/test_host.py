@@ -125,7 +125,8 @@ def test_torch_tensors_shard_too():
 def test_native_tile_policy():
     """The fixed tile policy of autotune=True launches: exact-fit swap-AB tiles
     up to 64 tokens, 128-token tiles at 128, CTA-pair tiles beyond (256 x 512
-    from M = 512); short K (<= 1024) takes the 128-token tile from M = 32."""
+    from M = 512, and at M = 256 when K >= 4096); short K (<= 1024) takes the
+    128-token tile from M = 32."""
     from kernels import native_candidates
     from kernels import matmul as mm
 
@@ -134,7 +135,7 @@ def test_native_tile_policy():
     assert native_candidates(32) == (mm.TILE_SWAP_32x256,)
     assert native_candidates(64, 7168) == (mm.TILE_SWAP_64x256,)
     assert native_candidates(128, 7168) == (mm.TILE_TOKENS_128x256,)
-    assert native_candidates(256, 7168) == (mm.TILE_PAIR_256x256,)
+    assert native_candidates(256, 7168) == (mm.TILE_PAIR_256x512,)
     assert native_candidates(256) == (mm.TILE_PAIR_256x256,)
     assert native_candidates(256, 2048) == (mm.TILE_PAIR_256x256,)
     assert native_candidates(1024, 2048) == (mm.TILE_PAIR_256x512,)
