@@ -192,17 +192,23 @@ int grid_for(int64_t problems, int64_t m, int64_t n, int tm, int tn, int64_t cap
   return grid_of(tiles, cap, exact);
 }
 
-// A CTA-pair 256 x 512 launch with an exact tile count, one tile per unit and
-// a last wave at most half full: that wave's tiles run as two 256-column half
-// items each (GroupedParams::tail_split), one item per cluster, on every
-// cluster the device holds, instead of one more round of wide tiles.  Returns
-// the grid (CTAs) to launch; other launches keep `grid` and no split.
+// A short CTA-pair 256 x 512 launch (at most kSplitRounds rounds of tiles)
+// with an exact tile count, one tile per unit and a last wave at most half
+// full: that wave's tiles run as two 256-column half items each
+// (GroupedParams::tail_split), one item per cluster, on every cluster the
+// device holds, instead of one more round of wide tiles.  The half round
+// saved is then at least a tenth of the launch (W13 M_e = 256: 4 rounds,
+// 4% faster); on long launches (W2 EP M_e = 512 / 1024: 13 / 25 rounds) the
+// split measured 1-4% slower under the power cap, as a half item spends
+// more energy per FLOP than a wide tile.  Returns the grid (CTAs) to
+// launch; other launches keep `grid` and no split.
+constexpr int64_t kSplitRounds = 5;
 int tail_split_grid(GroupedParams& p, bool pair, int tn, int64_t tiles, int max_clusters, int grid) {
   if (!pair || tn != 512 || p.swiglu || p.scatter_origin != nullptr || p.unit_tiles > 1 || max_clusters <= 0) {
     return grid;
   }
   const int64_t rem = tiles % max_clusters;
-  if (rem == 0 || 2 * rem > max_clusters) return grid;
+  if (rem == 0 || 2 * rem > max_clusters || tiles / max_clusters + 1 > kSplitRounds) return grid;
   p.tail_split = 1;
   p.tail_from = tiles - rem;
   const int64_t items = p.tail_from + 2 * rem;

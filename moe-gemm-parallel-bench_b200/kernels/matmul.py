@@ -297,12 +297,13 @@ def native_candidates(max_m: int, max_k: int | None = None, *, split_tail: bool 
     M = 512, and at M = 256 on deep K (W13, K = 7168: 4% on the EP and TP
     launches); at M = 256 with K = 2048 (W2 EP) the 256 x 256 tile's fully
     overlapped epilogue keeps it level or ahead.  On
-    short K (K <= 1024: W2 TP, K = 256) the epilogue dominates every tile and
-    the 128 x 256 one-CTA tile, whose two accumulators let the epilogue of one
-    tile run under the next tile's MMAs, beats both pair tiles at every M
-    above 128 (4-8% on whole W2 TP steps), and from M = 32 it also beats the
-    swap-AB tiles, whose column-per-lane stores suit outputs that are small
-    next to the weights.  Timing candidates alone at boost clocks (the reference's hot
+    short K (K <= 1024: W2 TP, K = 256) the epilogue dominates every tile:
+    above M = 128 the 256 x 512 pair (its drain overlapped by the next tile's
+    first k-blocks, a four-stage ring) beats the one-CTA 128 x 256 tile by
+    9-17% per launch (whole W2 TP step 609 against 543 TFLOP/s), and from
+    M = 32 to 128 the 128 x 256 tile beats the swap-AB tiles, whose
+    column-per-lane stores suit outputs that are small next to the weights.
+    Timing candidates alone at boost clocks (the reference's hot
     autotune) picks tiles that lose once the GPU is power-capped, so the
     policy is fixed rather than re-timed per shape.
     """
@@ -310,10 +311,10 @@ def native_candidates(max_m: int, max_k: int | None = None, *, split_tail: bool 
         return (TILE_SWAP_16x256,)
     if max_k is not None and max_k <= 1024:
         # Short K (W2 TP, K = 256): output writes dominate, and the row
-        # tile's TMA-store epilogue beats the swap-AB tiles' column-per-lane
+        # tiles' TMA-store epilogues beat the swap-AB tiles' column-per-lane
         # stores from M = 32 (tile sweep: 0.75 vs 0.63 of roofline at M = 32,
         # 0.79 vs 0.46 at M = 64).
-        return (TILE_TOKENS_128x256,)
+        return (TILE_PAIR_256x512,) if max_m > 128 else (TILE_TOKENS_128x256,)
     if max_m <= 32:
         return (TILE_SWAP_32x256,)
     if max_m <= 64:

@@ -126,7 +126,7 @@ def test_native_tile_policy():
     """The fixed tile policy of autotune=True launches: exact-fit swap-AB tiles
     up to 64 tokens, 128-token tiles at 128, CTA-pair tiles beyond (256 x 512
     from M = 512, and at M = 256 when K >= 4096); short K (<= 1024) takes the
-    128-token tile from M = 32."""
+    128-token tile from M = 32 to 128 and the 256 x 512 pair above."""
     from kernels import native_candidates
     from kernels import matmul as mm
 
@@ -139,12 +139,13 @@ def test_native_tile_policy():
     assert native_candidates(256) == (mm.TILE_PAIR_256x256,)
     assert native_candidates(256, 2048) == (mm.TILE_PAIR_256x256,)
     assert native_candidates(1024, 2048) == (mm.TILE_PAIR_256x512,)
-    assert native_candidates(256, 256) == (mm.TILE_TOKENS_128x256,)
+    assert native_candidates(256, 256) == (mm.TILE_PAIR_256x512,)
+    assert native_candidates(128, 256) == (mm.TILE_TOKENS_128x256,)
     assert native_candidates(16, 256) == (mm.TILE_SWAP_16x256,)
     assert native_candidates(32, 256) == (mm.TILE_TOKENS_128x256,)
     assert native_candidates(64, 256) == (mm.TILE_TOKENS_128x256,)
     assert native_candidates(64, 2048) == (mm.TILE_SWAP_64x256,)
-    assert native_candidates(1024, 256) == (mm.TILE_TOKENS_128x256,)
+    assert native_candidates(1024, 256) == (mm.TILE_PAIR_256x512,)
     assert native_candidates(512, 7168) == (mm.TILE_PAIR_256x512,)
     assert native_candidates(1024) == (mm.TILE_PAIR_256x512,)
 
