@@ -99,6 +99,8 @@ def parse_args(argv=None):
     p.add_argument("--ep-transport", choices=("peer", "peer-pull", "nccl"), default="peer",
                    help="--moe-layer exchange: peer-memory kernels with W2 returning rows from its epilogue, "
                         "peer-memory kernels with the combine pulling rows, or the NCCL all_to_all_single baseline")
+    p.add_argument("--ref-providers", type=str, default="triton,torch_grouped_mm",
+                   help="--impl reference-gpu: subset of triton,torch_grouped_mm to time beside the native launch")
     p.add_argument("--tile-sweep", action="store_true",
                    help="time every native tile per shape, alone and right after a heavy launch (diagnosis)")
     return p.parse_args(argv)
@@ -1043,8 +1045,11 @@ def reference_gpu_arm(args, rank: int, world: int) -> None:
             row["native_ms"] = round(median_ms(lambda: launch_grouped(ws)), 4)
             native_c = [c.clone() for c in ws.c[:4]]
             del ws
+            providers = args.ref_providers.split(",")
             progress(f"{par} M_e={m}: reference Triton (hot autotune)")
             try:
+                if "triton" not in providers:
+                    raise RuntimeError("not requested (--ref-providers)")
                 rws = ref.build_grouped_workspace(shapes, torch.bfloat16, seed=0)
                 ref.launch_grouped(rws)
                 torch.cuda.synchronize()
@@ -1061,6 +1066,8 @@ def reference_gpu_arm(args, rank: int, world: int) -> None:
             torch.cuda.empty_cache()
             progress(f"{par} M_e={m}: torch grouped_mm")
             try:
+                if "torch_grouped_mm" not in providers:
+                    raise RuntimeError("not requested (--ref-providers)")
                 tws = ref.build_torch_grouped_workspace(shapes, torch.bfloat16, seed=0)
                 row["torch_grouped_mm_ms"] = round(median_ms(lambda: ref.launch_torch_grouped(tws)), 4)
                 del tws
