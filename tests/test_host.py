@@ -136,6 +136,8 @@ def test_native_tile_policy():
     assert native_candidates(64, 7168) == (mm.TILE_SWAP_64x256,)
     assert native_candidates(128, 7168) == (mm.TILE_TOKENS_128x256,)
     assert native_candidates(256, 7168) == (mm.TILE_PAIR_256x512,)
+    # Without a splittable tail (ragged groups, SwiGLU, aggregate layout) M = 256 keeps 256 x 256.
+    assert native_candidates(256, 7168, split_tail=False) == (mm.TILE_PAIR_256x256,)
     assert native_candidates(256) == (mm.TILE_PAIR_256x256,)
     assert native_candidates(256, 2048) == (mm.TILE_PAIR_256x256,)
     assert native_candidates(1024, 2048) == (mm.TILE_PAIR_256x512,)
