@@ -83,3 +83,18 @@ def test_fused_swiglu_and_fp8_byte_models():
     assert bench.fp8_launch_bytes(m, k, n) == m * k + n * k + 4 * (m * 56 + 32 * 56) + 2 * m * n
     fp8, bound = bench.roofline_ms(m, k, n, 1, NOMINAL, fp8=True)
     assert bound == "hbm" and fp8 < full
+
+
+def test_reference_arm_prints_the_contract_line(capsys):
+    """`bench.py --impl reference` times the reference's per-expert
+    torch.matmul on the host and prints one JSON line with the arm's keys."""
+    import json
+
+    bench = _bench()
+    assert bench.main(["--impl", "reference", "--steps", "1", "--warmup", "3", "--m-values", "16"]) == 0
+    line = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["metric"] == bench.METRIC and line["unit"] == "TFLOP/s"
+    assert line["value"] > 0 and line["higher_is_better"] is True
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
+    assert line["e2e"] == {"value": line["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
