@@ -98,3 +98,75 @@ def test_reference_arm_prints_the_contract_line(capsys):
     assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["cores"] >= 1
     assert line["e2e"] == {"value": line["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
+
+
+MEASURED = {"bf16_tflops": 1694.4, "bf16_tflops_sustained": 1434.9, "hbm_gbs": 6468.3, "sm_max_mhz": 1965.0,
+            "sustained_sm_mhz": 1380.0}
+
+
+@pytest.mark.parametrize("mhz,expected,kind", [
+    (1965.0, 1694.4, "burst"),        # a short region at boost clock: the burst figure
+    (1890.0, 1694.4, "burst"),        # within 5% of the maximum
+    (1380.0, 1434.9, "sustained"),    # at the clock the sustained figure was measured at
+    (1222.0, 1434.9, "sustained"),    # below it (power-capped step)
+    (None, 1694.4, "burst"),          # no clock record: the larger denominator
+])
+def test_tensor_peak_follows_the_sampled_clock(mhz, expected, kind):
+    """The roofline's tensor peak is chosen from the SM clock sampled in the
+    timed region, never the sustained figure alone for a boost-clock run."""
+    bench = _bench()
+    clocks = None if mhz is None else {"sm_mhz": mhz}
+    peak, source = bench.tensor_peak(MEASURED, clocks)
+    assert peak == pytest.approx(expected)
+    assert source.startswith(kind)
+
+
+def test_tensor_peak_interpolates_between_the_two_figures():
+    bench = _bench()
+    hi = 0.95 * MEASURED["sm_max_mhz"]
+    mid = (hi + MEASURED["sustained_sm_mhz"]) / 2
+    peak, source = bench.tensor_peak(MEASURED, {"sm_mhz": mid})
+    assert peak == pytest.approx((1694.4 + 1434.9) / 2)
+    assert source.startswith("interpolated")
+
+
+def test_dominant_kernel_fraction_at_burst_clock_matches_the_record():
+    """The round's driver record: W13 EP M_e = 1024 at 1.5852 ms with a
+    1965 MHz median is 1213.8 TFLOP/s, 0.72 of the burst peak (not 0.846 of
+    the sustained one)."""
+    bench = _bench()
+    from moe_parallel import gemm_flops
+
+    achieved = gemm_flops(1024, 7168, 4096) * 32 / 1.5852e-3 / 1e12
+    peak, _ = bench.tensor_peak(MEASURED, {"sm_mhz": 1965.0})
+    assert achieved == pytest.approx(1213.8, rel=1e-3)
+    assert achieved / peak == pytest.approx(0.716, abs=2e-3)
+
+
+def test_clock_summary_counts_only_the_timed_region():
+    bench = _bench()
+    sw_cap, hw_slow = 0x4, 0x8
+    samples = [(0.5, 1965.0, 1965.0, 300.0, 0)]  # before the region
+    samples += [(1.0 + 0.01 * i, 1400.0 + i, 1965.0, 900.0, sw_cap if i % 2 else 0) for i in range(21)]
+    samples += [(5.0, 600.0, 1965.0, 100.0, hw_slow)]  # after it
+    rec = bench.summarize_clock_samples(samples, window=(1.0, 1.3), interval_s=0.005)
+    assert rec["samples_in_timed_region"] == 21 and rec["samples"] == 21
+    assert rec["sm_mhz"] == 1410.0 and rec["sm_mhz_min"] == 1400.0
+    assert rec["reasons"] == ["sw_power_cap"] and rec["reason_samples"] == {"sw_power_cap": 10}
+    assert rec["power_w_median"] == 900.0
+
+
+def test_default_step_is_w13_hot_and_w2_rotating_cold():
+    """The default line covers both projections the metric names: W13 hot
+    and W2 in rotating-cold mode."""
+    bench = _bench()
+    args = bench.parse_args([])
+    projections = bench.selected_projections(args)
+    assert projections == ("W1", "W2")
+    assert bench.cold_projections(args, projections) == ("W2",)
+    text = bench.workload_text(projections, ("W2",))
+    assert "one step = 28 grouped launches" in text and "rotating-cold" in text
+    only_w13 = bench.parse_args(["--fp8"])
+    assert bench.selected_projections(only_w13) == ("W1",)
+    with pytest.raises(SystemExit):
+        bench.selected_projections(bench.parse_args(["--fp8", "--projection", "W2"]))
