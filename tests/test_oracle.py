@@ -151,3 +151,34 @@ def test_fp8_block_scaled_oracle_is_dequantized_product():
             b[i * 128:(i + 1) * 128, j * 128:(j + 1) * 128] *= sb[i, j]
     expected = oracle.round_to_dtype(a @ b.T, "bf16")
     np.testing.assert_array_equal(got, expected)
+
+
+BF16_CASES = __import__("tests.golden_data", fromlist=["load_bf16_checker_cases"]).load_bf16_checker_cases()
+
+
+@pytest.mark.parametrize("case", BF16_CASES, ids=[c["name"] for c in BF16_CASES])
+def test_oracle_reproduces_reference_checker_in_bf16(case):
+    """bf16 pin: the reference's own checker (per-expert torch.matmul,
+    benchmark_moe.py:259-266) on DeepSeek-V3 miniature groups, stored by
+    tests/golden/make_bf16_golden.py.  torch accumulates in fp32 and the
+    oracle in float64, each rounding once to bf16, so they differ by at most
+    an output ulp on a few elements: measured relative Frobenius <= 9e-5."""
+    from tests.golden_data import bf16_checker_inputs
+
+    a, b = bf16_checker_inputs(case)
+    assert len(a) == len(case["c"]) == case["experts"]
+    for e in range(case["experts"]):
+        a64 = a[e].float().numpy().astype(np.float64)
+        b64 = b[e].float().numpy().astype(np.float64)
+        if case["projection"] == "W1":
+            expected = oracle.gate_up(a64, b64, "bf16")
+        else:
+            expected = oracle.matmul(a64, b64, "bf16")
+        got = case["c"][e].astype(np.float64)
+        assert got.shape == (case["m"], case["n"])
+        assert oracle.relative_frobenius(got, expected) <= 5e-4
+        # Elementwise: one bf16 ulp of the larger magnitude apart at most, plus
+        # torch's fp32 accumulation error on results that nearly cancel
+        # (measured <= 3.6e-7 absolute with |C| ~ 1 and K <= 7168).
+        ulp = np.exp2(np.floor(np.log2(np.maximum(np.abs(expected), np.abs(got)) + 1e-300)) - 7)
+        assert np.all(np.abs(got - expected) <= ulp * 1.0001 + 1e-6)
