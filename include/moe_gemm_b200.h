@@ -13,8 +13,9 @@
  *   dtype      fp16 | bf16 | fp32           utils/benchmark.py:35-38
  *   precision  "ieee" | "tf32"              kernels/matmul.py:268, grouped_gemm.py:389,475
  *   tile       KernelConfig fields          kernels/matmul.py:19-32
- * All launches are asynchronous on `stream`, allocate nothing, synchronise
- * nothing, and may be recorded into a CUDA graph.
+ * All launches are asynchronous on `stream` and synchronise nothing.  Those
+ * that take their scratch from the caller allocate nothing and may be
+ * recorded into a CUDA graph.
  */
 #ifndef MOE_GEMM_B200_H
 #define MOE_GEMM_B200_H
@@ -310,21 +311,24 @@ int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r,
  * counterpart in the reference (its Triton launches need no scratch).
  *
  * Same arguments and result as grouped_gemm_launch, minus the scratch buffer:
- * the tensor maps live in a fixed MGB_NOALLOC_SCRATCH_BYTES array inside
- * this library, so the call allocates and frees nothing.  It serves callers
- * with no device allocator of their own -- a plugin in a process whose
- * framework owns all device memory, a launch made while a CUDA graph is being
- * captured (cudaMalloc is not permitted there), a launch path that must never
- * block in the driver's allocator.
+ * the per-problem tensor maps and tile-walk offsets live in a fixed
+ * MGB_NOALLOC_SCRATCH_BYTES array inside this library, so the call allocates
+ * and frees nothing.  It serves callers with no device allocator of their
+ * own: a plugin in a process whose framework owns all device memory and hands
+ * it only the input and output tensors, or a launch path that must never
+ * enter the driver's allocator.
  *   - The first call on a device looks up the array's device address (once per
- *     device, with that device current); make that first call before any
- *     stream capture.
- *   - A launch that needs more than MGB_NOALLOC_SCRATCH_BYTES (more than 2674
- *     problems) is refused with MGB_ERR_SCRATCH.
+ *     device, with that device current, cached for the process); make that
+ *     first call before any stream capture, and do not call this again on a
+ *     device after cudaDeviceReset() in the same process.
+ *   - A group of more than 2674 problems (whose maps would exceed
+ *     MGB_NOALLOC_SCRATCH_BYTES) is refused with MGB_ERR_SCRATCH, whichever
+ *     kernel would have run it.
  *   - Every call shares the one array and leaves its last contents behind;
- *     nothing in it has to start at zero (each launch writes every map before
- *     reading it), but calls that overlap on the GPU -- other streams, other
- *     threads -- race on it and must be serialised by the caller. */
+ *     nothing in it has to start at zero (each launch writes every map and
+ *     offset before reading it), but calls that overlap on the GPU -- other
+ *     streams, other threads -- race on it and must be serialised by the
+ *     caller. */
 int grouped_gemm_launch_noalloc(const int64_t* a_ptrs, const int64_t* b_ptrs, const int64_t* c_ptrs,
                                 const int32_t* dims, const int64_t* strides, int32_t problem_count,
                                 int32_t homogeneous, int64_t m, int64_t n, int64_t k, int32_t dtype,

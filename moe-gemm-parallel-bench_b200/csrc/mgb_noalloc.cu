@@ -1,19 +1,25 @@
 // grouped_gemm_launch_noalloc: the grouped GEMM launch for callers that cannot
 // allocate device memory.
 //
-// Some callers have no way to obtain a device buffer for the launch's scratch
-// (the per-CTA tensor-map slots of the tensor-core path): a plugin inside a
-// host process whose framework owns every byte of device memory, code that
-// launches while a CUDA graph is being captured (cudaMalloc is not permitted
-// there), or a real-time launch path that must never block in the driver's
-// allocator.  This entry point takes its scratch from a fixed array compiled
-// into the library instead, so it allocates nothing and frees nothing.
+// The tensor-core path of a grouped launch needs scratch in global memory: the
+// A, B and C tensor maps of every problem (3 x 128 bytes each) and, after them,
+// problem_count + 1 int64 tile-walk offsets, all written by the map-builder
+// kernel just before the GEMM kernel reads them.  grouped_gemm_launch takes
+// that buffer from its caller.  Some callers have no way to obtain one: a
+// plugin inside a host process whose framework owns every byte of device
+// memory and hands the plugin only its input and output tensors, or a launch
+// path that must never enter the driver's allocator (which can block or
+// fail).  This entry point takes its scratch from a fixed array compiled into
+// the library instead, so it allocates nothing and frees nothing.
 //
 // The array is a file-scope __device__ object: every GPU that loads this
 // library holds kNoAllocScratchBytes of it until the process exits.  In host
 // code its name is only a host-side stand-in, never a device address, so the
 // device address is looked up once per device (cudaGetSymbolAddress, with that
-// device current) and that address is what the kernels receive.
+// device current) and that address is what the kernels receive.  The lookup is
+// cached for the life of the process: after cudaDeviceReset() on a device the
+// cached address is stale, so a process that resets a device must not call
+// this entry point on it again.
 #include <cuda_runtime.h>
 
 #include <cstdint>
@@ -63,8 +69,10 @@ int grouped_gemm_launch_noalloc(const int64_t* a_ptrs, const int64_t* b_ptrs, co
   void* scratch = scratch_address(&dev);
   if (scratch == nullptr) return MGB_ERR_CUDA;
   if (cudaDeviceGetAttribute(&sm_count, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return MGB_ERR_CUDA;
-  // The launch never needs more than grouped_gemm_scratch_bytes(); refuse a
-  // group whose maps would not fit the fixed array.
+  // The launch never needs more than grouped_gemm_scratch_bytes(); a group
+  // whose maps would not fit the fixed array is refused before any kernel is
+  // chosen, so it is refused whichever path (tensor-core or generic) would
+  // have run it.
   if (grouped_gemm_scratch_bytes(problem_count, sm_count) > kNoAllocScratchBytes) return MGB_ERR_SCRATCH;
   return grouped_gemm_launch(a_ptrs, b_ptrs, c_ptrs, dims, strides, problem_count, homogeneous, m, n, k, dtype,
                              precision, operands_tma_aligned, config, scratch, kNoAllocScratchBytes, stream, info);

@@ -1,22 +1,26 @@
 """GPU test of grouped_gemm_launch_noalloc, the grouped launch for callers
 that cannot allocate device memory.
 
-Such callers -- a plugin whose host framework owns all device memory, a launch
-made while a CUDA graph is being captured, a launch path that must not block
-in the driver's allocator -- cannot hand the library a scratch buffer, so this
-entry point takes the tensor-map slots from a fixed array inside the library.
-This file is collected last (its name sorts last), so a run that stops at the
-first failure has already run every other test; it also passes alone in a
-fresh process, where its first call performs the once-per-device set-up.
+Such callers -- a plugin whose host framework owns all device memory and hands
+it only its input and output tensors, or a launch path that must never enter
+the driver's allocator -- cannot hand the library a scratch buffer, so this
+entry point takes the tensor-map scratch from a fixed array inside the
+library.  This file is collected last (its name sorts last), so a run that
+stops at the first failure has already run every other test; it also passes
+alone in a fresh process, where its first call performs the once-per-device
+set-up.
 
-The check: through the C ABI, two calls in a row of the no-alloc entry point
-give the same output as the existing grouped_gemm_launch on the same inputs
-(within the bf16 tolerance the parity tests use: relative Frobenius <= 1e-2),
-and the device error word stays clear.
+The checks, through the C ABI, on two calls in a row: the no-alloc entry
+point gives the same output as the existing grouped_gemm_launch on the same
+inputs and matches the float64 oracle (both within the bf16 tolerance the
+parity tests use: relative Frobenius <= 1e-2), the device error word stays
+clear, and the second call (after the set-up) changes neither torch's
+allocated bytes nor the device's free memory.
 """
 
 from __future__ import annotations
 
+import numpy as np
 import pytest
 
 from tests.conftest import cuda_ready
@@ -49,6 +53,7 @@ def test_noalloc_entry_matches_existing_entry_on_two_calls(shapes):
 
     from kernels import KernelConfig, _native, launch_grouped
     from kernels.grouped_gemm import operands_tma_aligned
+    from oracle import gemm as oracle
 
     ws = _inputs(shapes, seed=31)
     config = KernelConfig(16, 128, 64, 4, 4, 3)
@@ -59,22 +64,33 @@ def test_noalloc_entry_matches_existing_entry_on_two_calls(shapes):
     torch.cuda.synchronize()
     expected = [c.clone() for c in ws.c]
     assert ws.launch_info["path"].startswith("tcgen05_tma")
+    oracle_out = [oracle.matmul(a.double().cpu().numpy(), b.double().cpu().numpy(), "bf16")
+                  for a, b in zip(ws.a, ws.b)]
 
     if ws.homogeneous:
         m, k, n = ws.shapes[0]
     else:
         m, k, n = ws.max_m, ws.max_k, ws.max_n
+    stream = torch.cuda.current_stream().cuda_stream
     for call in range(2):
         for c in ws.c:
             c.fill_(float("nan"))
+        torch.cuda.synchronize()
+        allocated, (free, _) = torch.cuda.memory_allocated(), torch.cuda.mem_get_info()
         info = _native.grouped_launch_noalloc(
             ws.a_ptrs.data_ptr(), ws.b_ptrs.data_ptr(), ws.c_ptrs.data_ptr(), ws.dims.data_ptr(),
             ws.strides.data_ptr(), ws.problem_count, ws.homogeneous, m, n, k, "bf16", "ieee",
-            operands_tma_aligned(ws), config, torch.cuda.current_stream().cuda_stream,
+            operands_tma_aligned(ws), config, stream,
         )
         torch.cuda.synchronize()
+        if call == 1:  # after the once-per-device set-up of the first call
+            assert torch.cuda.memory_allocated() == allocated
+            assert torch.cuda.mem_get_info()[0] == free, "the no-alloc launch changed the device's free memory"
         assert info.path == 0, "the no-alloc entry point must run the tensor-core kernel"
         assert _native.read_and_clear_error_word(device) == 0
-        for got, want in zip(ws.c, expected):
+        for e, (got, want) in enumerate(zip(ws.c, expected)):
             assert torch.isfinite(got.float()).all(), f"call {call}: unwritten outputs"
             assert _rel_fro(got, want) <= REL_FRO_BF16, f"call {call}"
+            got_np = got.double().cpu().numpy()
+            err = float(np.linalg.norm(got_np - oracle_out[e]) / np.linalg.norm(oracle_out[e]))
+            assert err <= REL_FRO_BF16, f"call {call}, problem {e}: {err:.3e} against the oracle"
