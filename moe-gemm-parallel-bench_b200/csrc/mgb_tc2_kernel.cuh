@@ -66,6 +66,17 @@ struct Tc2Cfg {
   static constexpr uint32_t kIdesc = instr_desc(kFmt, 0, 1, kTileM, 256);  // one MMA: M = 256, N = 256
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 2048 + 1024;
   static_assert(kAccBufs * kAccCols <= kTmemCols, "accumulators fit in TMEM");
+  // The epilogue is exactly four warps (2-5), one per TMEM lane quarter
+  // (warp & 3 = 2, 3, 0, 1): the staging blocks are sized for four warps, each
+  // warp's blocks start at quarter * kEpiBlocks * kEpiWarpBytes < kEpiBytes,
+  // and an accumulator half is released by kEpiArrivals = 2 CTAs x 4 warps
+  // arrivals.  A layout with more epilogue warps must resize all three.
+  static constexpr int kEpiWarps = (kTcThreads - 64) / 32;
+  static constexpr int kEpiArrivals = 2 * kEpiWarps;
+  static_assert(kEpiWarps == 4, "one epilogue warp per TMEM lane quarter");
+  static_assert(kEpiBytes == kEpiWarps * kEpiBlocks * kEpiWarpBytes, "staging blocks of every epilogue warp");
+  // TMEM columns an epilogue warp reads: buf * kAccCols + h * 256 + [0, 256).
+  static_assert((kAccBufs - 1) * kAccCols + kTileN <= kTmemCols, "accumulator columns inside the allocation");
   static_assert(kStages >= 3, "operand ring depth");
   static_assert(kSmemBytes <= 232448, "shared memory");
 };
@@ -131,7 +142,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 8);
+      mbar_init(&acc_empty[b], Cfg::kEpiArrivals);
     }
     mbar_init(test_bar, 1);
     mbar_init(drain_bar, 1);
