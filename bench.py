@@ -1278,6 +1278,12 @@ def main(argv=None) -> int:
     if world > 1:
         from datetime import timedelta
 
+        # NCCL's communicator lines (rank, nRanks, transport) on stderr, so a
+        # run's log shows how many ranks the verification gather spans;
+        # stdout keeps only the JSON line.
+        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
     if args.moe_layer:
         moe_layer_bench(args, rank, world, local_rank, device)
