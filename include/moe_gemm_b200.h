@@ -28,7 +28,11 @@ extern "C" {
 #endif
 
 enum mgb_dtype { MGB_FP16 = 0, MGB_BF16 = 1, MGB_FP32 = 2 };
-enum mgb_precision { MGB_IEEE = 0, MGB_TF32 = 1 };
+/* MGB_TF32_FP32ACC (fp32 only, tensor-core path): TF32 products with the
+ * tensor core accumulating at most 256 K at a time, the partial sums added in
+ * fp32 registers; for operands that are exact in TF32, such as the halves
+ * matrix_split_tf32x3 writes.  No counterpart in the reference. */
+enum mgb_precision { MGB_IEEE = 0, MGB_TF32 = 1, MGB_TF32_FP32ACC = 2 };
 
 enum mgb_status {
   MGB_OK = 0,
@@ -302,6 +306,20 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
  * its Triton kernel reads every element through masked loads. */
 int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r, int64_t stride_c, void* dst,
                   int64_t dst_pitch, int32_t elem_bytes, void* stream);
+
+/* The 3xTF32 operand split behind input_precision="ieee" fp32 GEMMs on the
+ * tensor cores (kernels/matmul.py:268 in the reference asks for full fp32
+ * products; its Triton kernel runs them as fp32 FMAs).  Each fp32 element x
+ * becomes hi = tf32(x) and lo = tf32(x - hi) (round to nearest even, kept in
+ * fp32 words with the low 13 bits zero), laid out along K so that one TF32
+ * GEMM of depth 3K computes hi(A) hi(B) + lo(A) hi(B) + hi(A) lo(B):
+ *   side 0, A [rows = M, cols = K]: dst [M, 3K] = [hi | lo | hi]
+ *   side 1, B [rows = K, cols = N]: dst [3K, N] = [hi ; hi ; lo]
+ * src has arbitrary element strides; dst is row-major with a row pitch of
+ * dst_pitch elements (>= 3 cols for side 0, >= cols for side 1).  No
+ * counterpart in the reference. */
+int matrix_split_tf32x3(const float* src, int64_t rows, int64_t cols, int64_t stride_r, int64_t stride_c, float* dst,
+                        int64_t dst_pitch, int32_t side, void* stream);
 
 /* Size of the scratch array compiled into the library for
  * grouped_gemm_launch_noalloc (bytes, per GPU that loads the library). */

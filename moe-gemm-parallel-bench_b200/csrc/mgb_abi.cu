@@ -115,7 +115,9 @@ bool encode_2d(CUtensorMap* map, int dtype, const void* base, uint64_t inner, ui
 // kernel's 256 x 256 cluster tile, and block_n >= 256 its 256 x 512 tile (the
 // reference's configs keep block_n <= 256); block_m >= 256 with a narrower
 // block_n (and every fp32 case) the one-CTA swap-AB 256 x 128 tile.
-TcVariant pick_variant(const mgb_tile_config* cfg, int dtype) {
+TcVariant pick_variant(const mgb_tile_config* cfg, int dtype, int precision = MGB_IEEE) {
+  // fp32 with chunked, register-promoted accumulation: the 128 x 128 tile.
+  if (dtype == MGB_FP32 && precision == MGB_TF32_FP32ACC) return TcVariant{false, 128, 128, false, true};
   const int bm = cfg ? cfg->block_m : 64;
   const int bn = cfg ? cfg->block_n : 128;
   const int wide = bn >= 256 ? 256 : 128;
@@ -239,7 +241,7 @@ void fill_info(mgb_launch_info* info, int path, const TcVariant& v, const TcVari
 
 bool valid_dtype(int dtype, int precision) {
   return (dtype == MGB_FP16 || dtype == MGB_BF16 || dtype == MGB_FP32) &&
-         (precision == MGB_IEEE || precision == MGB_TF32);
+         (precision == MGB_IEEE || precision == MGB_TF32 || (precision == MGB_TF32_FP32ACC && dtype == MGB_FP32));
 }
 
 // dst[r, c] = src[r * stride_r + c * stride_c], one 32-column x 8-row block
@@ -257,9 +259,74 @@ __global__ void __launch_bounds__(256) repack_kernel(const E* __restrict__ src, 
   }
 }
 
+// Round-to-nearest-even of an fp32 value to TF32 (10 explicit mantissa bits),
+// kept in fp32 with the low 13 bits zero.  Infinities and NaNs pass through; a
+// finite value whose rounding would overflow is truncated instead.
+__device__ __forceinline__ float round_to_tf32(float x) {
+  const uint32_t u = __float_as_uint(x);
+  if ((u & 0x7F800000u) == 0x7F800000u) return x;
+  const uint32_t r = (u + 0x0FFFu + ((u >> 13) & 1u)) & 0xFFFFE000u;
+  return (r & 0x7F800000u) == 0x7F800000u ? __uint_as_float(u & 0xFFFFE000u) : __uint_as_float(r);
+}
+
+// The 3xTF32 operand split (Ootomo & Yokota, "Recovering single precision
+// accuracy from Tensor Cores while surpassing the FP32 theoretical peak
+// performance", IJHPCA 2022): x = hi + lo with hi = tf32(x) and
+// lo = tf32(x - hi), so A B ~ hi(A) hi(B) + lo(A) hi(B) + hi(A) lo(B) with an
+// error of order 2^-22 |A| |B|.  The three products are laid out along K, so
+// one TF32 GEMM of depth 3K on the tensor cores computes their sum:
+//   side 0 (A, [rows, K]): dst[r, c] = hi, dst[r, K + c] = lo, dst[r, 2K + c] = hi
+//   side 1 (B, [K, cols]):  dst[r, c] = hi, dst[K + r, c] = hi, dst[2K + r, c] = lo
+// One 32-column x 8-row block per CTA iteration (grid-stride), coalesced
+// along rows.
+__global__ void __launch_bounds__(256) split_tf32x3_kernel(const float* __restrict__ src, int64_t rows, int64_t cols,
+                                                           int64_t stride_r, int64_t stride_c, float* __restrict__ dst,
+                                                           int64_t pitch, int side) {
+  const int64_t col_blocks = (cols + 31) / 32;
+  const int64_t blocks = ((rows + 7) / 8) * col_blocks;
+  for (int64_t b = blockIdx.x; b < blocks; b += gridDim.x) {
+    const int64_t r = (b / col_blocks) * 8 + threadIdx.y;
+    const int64_t c = (b % col_blocks) * 32 + threadIdx.x;
+    if (r >= rows || c >= cols) continue;
+    const float x = src[r * stride_r + c * stride_c];
+    const float hi = round_to_tf32(x);
+    const float lo = round_to_tf32(x - hi);
+    if (side == 0) {
+      float* row = dst + r * pitch;
+      row[c] = hi;
+      row[cols + c] = lo;
+      row[2 * cols + c] = hi;
+    } else {
+      dst[r * pitch + c] = hi;
+      dst[(rows + r) * pitch + c] = hi;
+      dst[(2 * rows + r) * pitch + c] = lo;
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" {
+
+int matrix_split_tf32x3(const float* src, int64_t rows, int64_t cols, int64_t stride_r, int64_t stride_c, float* dst,
+                        int64_t dst_pitch, int32_t side, void* stream) {
+  if (rows < 0 || cols < 0 || (side != 0 && side != 1) ||
+      (rows > 0 && cols > 0 && (src == nullptr || dst == nullptr))) {
+    return MGB_ERR_INVALID;
+  }
+  if (dst_pitch < (side == 0 ? 3 * cols : cols)) return MGB_ERR_INVALID;
+  if (rows == 0 || cols == 0) return MGB_OK;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    return MGB_ERR_CUDA;
+  }
+  const int64_t blocks = ((rows + 7) / 8) * ((cols + 31) / 32);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, 16ll * sms)));
+  split_tf32x3_kernel<<<grid, dim3(32, 8), 0, static_cast<cudaStream_t>(stream)>>>(src, rows, cols, stride_r,
+                                                                                   stride_c, dst, dst_pitch, side);
+  return cudaGetLastError() == cudaSuccess ? MGB_OK : MGB_ERR_CUDA;
+}
 
 int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r, int64_t stride_c, void* dst,
                   int64_t dst_pitch, int32_t elem_bytes, void* stream) {
@@ -323,11 +390,12 @@ int launch_grouped_params(GroupedParams& p, const DeviceState& ds, const TileBou
                           const mgb_tile_config* config, void* scratch, size_t scratch_bytes, cudaStream_t s,
                           mgb_launch_info* info) {
   const bool swiglu = p.swiglu != 0;
-  const bool tensor_core = operands_tma_aligned && (dtype != MGB_FP32 || precision == MGB_TF32) && m > 0 &&
+  const bool tensor_core = operands_tma_aligned && (dtype != MGB_FP32 || precision != MGB_IEEE) && m > 0 &&
                            n > 0 && k > 0;
   if (swiglu && !tensor_core) return MGB_ERR_UNSUPPORTED;  // the fused epilogue exists on the tensor-core path only
+  if (precision == MGB_TF32_FP32ACC && (swiglu || !tensor_core)) return MGB_ERR_UNSUPPORTED;
   if (tensor_core) {
-    TcVariant v = pick_variant(config, dtype);
+    TcVariant v = pick_variant(config, dtype, precision);
     if (swiglu && !v.pair) {
       // The SwiGLU epilogue pairs gate and up inside one tile: swap-AB tiles
       // need two 128-column weight chunks, row tiles at least 64 output columns.
@@ -693,9 +761,10 @@ int matmul_launch(const void* a, const void* b, void* c, int64_t m, int64_t n, i
                        stride_ak == 1 && stride_bn == 1 && stride_am > 0 && stride_bk > 0 &&
                        (stride_am * es) % 16 == 0 && (stride_bk * es) % 16 == 0 && m < (1ll << 31) &&
                        n < (1ll << 31) && k < (1ll << 31);
-  const bool tensor_core = aligned && k > 0 && (dtype != MGB_FP32 || precision == MGB_TF32);
+  const bool tensor_core = aligned && k > 0 && (dtype != MGB_FP32 || precision != MGB_IEEE);
+  if (precision == MGB_TF32_FP32ACC && !tensor_core) return MGB_ERR_UNSUPPORTED;
   if (tensor_core) {
-    const TcVariant v = pick_variant(config, dtype);
+    const TcVariant v = pick_variant(config, dtype, precision);
     TcVariantInfo vi;
     if (!variant_info(dtype, v, &vi)) return MGB_ERR_UNSUPPORTED;
     // C gets a real output map when TMA can address it (the kernel applies

@@ -88,6 +88,20 @@ struct Problem {
   int64_t sam, sak, sbk, sbn, scm, scn;
 };
 
+// A problem of a homogeneous table launch from its three pointers: every
+// other field is the launch's (contiguous operands; C has N columns, or N/2
+// with the SwiGLU epilogue).
+__device__ __forceinline__ Problem homogeneous_problem(const GroupedParams& p, const char* a, const char* b, char* c) {
+  Problem q;
+  q.row0 = 0;
+  q.a = a;
+  q.b = b;
+  q.c = c;
+  q.m = p.m; q.n = p.n; q.k = p.k;
+  q.sam = p.k; q.sak = 1; q.sbk = p.n; q.sbn = 1; q.scm = p.swiglu ? p.n / 2 : p.n; q.scn = 1;
+  return q;
+}
+
 __device__ __forceinline__ Problem load_problem(const GroupedParams& p, int e) {
   Problem q;
   q.row0 = 0;
@@ -112,14 +126,14 @@ __device__ __forceinline__ Problem load_problem(const GroupedParams& p, int e) {
     q.sam = p.sam; q.sak = 1; q.sbk = p.sbk; q.sbn = 1; q.scm = p.scm; q.scn = 1;
     return q;
   }
+  if (p.homogeneous) {
+    return homogeneous_problem(p, reinterpret_cast<const char*>(p.a_ptrs[e]),
+                               reinterpret_cast<const char*>(p.b_ptrs[e]), reinterpret_cast<char*>(p.c_ptrs[e]));
+  }
   q.a = reinterpret_cast<const char*>(p.a_ptrs[e]);
   q.b = reinterpret_cast<const char*>(p.b_ptrs[e]);
   q.c = reinterpret_cast<char*>(p.c_ptrs[e]);
-  if (p.homogeneous) {
-    // Contiguous operands; C has N columns, or N/2 with the SwiGLU epilogue.
-    q.m = p.m; q.n = p.n; q.k = p.k;
-    q.sam = p.k; q.sak = 1; q.sbk = p.n; q.sbn = 1; q.scm = p.swiglu ? p.n / 2 : p.n; q.scn = 1;
-  } else {
+  {
     q.m = p.dims[3 * e + 0];
     q.n = p.dims[3 * e + 1];
     q.k = p.dims[3 * e + 2];
@@ -156,6 +170,27 @@ struct TileWalk {
   int64_t ucount = 0;  // units of `problem` (seek_unit)
   int64_t m_blocks = 1;
   Problem prob;
+  // Lookahead of homogeneous table launches: the table pointers of the
+  // problem holding this CTA's next unit, loaded while the current unit runs,
+  // so a problem switch does not stall a role on a global-memory round trip
+  // (the MMA issuer sits on the tensor pipe's critical path there).
+  int ahead_problem = -1;
+  const char* ahead_a = nullptr;
+  const char* ahead_b = nullptr;
+  char* ahead_c = nullptr;
+
+  // Issues the loads of the pointers of the problem that holds unit `u`
+  // (`unit` tiles each) when it is not the current one; homogeneous table
+  // launches only (every problem's shape is known without a load).
+  __device__ __forceinline__ void prefetch_unit(const GroupedParams& p, int64_t u, int64_t unit) {
+    if (p.single || !p.homogeneous || p.offs != nullptr || count <= 0) return;
+    const int64_t e = u / ceil_div64(count, unit);
+    if (e >= p.problem_count || e == problem || e == ahead_problem) return;
+    ahead_problem = static_cast<int>(e);
+    ahead_a = reinterpret_cast<const char*>(p.a_ptrs[e]);
+    ahead_b = reinterpret_cast<const char*>(p.b_ptrs[e]);
+    ahead_c = reinterpret_cast<char*>(p.c_ptrs[e]);
+  }
 
   // Moves to the problem holding global unit `u` of `unit` tiles each and
   // returns its global tile range [t0, t1); false when `u` is past the end.
@@ -163,10 +198,9 @@ struct TileWalk {
   __device__ __forceinline__ bool seek_unit(const GroupedParams& p, int64_t u, int64_t unit, int64_t& t0,
                                             int64_t& t1) {
     if (p.single || p.homogeneous) {
-      if (problem < 0) {
-        Problem q = load_problem(p, 0);
-        m_blocks = ceil_div64(q.m, TM);
-        count = (q.m > 0 && q.n > 0) ? m_blocks * ceil_div64(q.n, TN) : 0;
+      if (problem < 0) {  // every problem is p.m x p.n: no table load needed
+        m_blocks = ceil_div64(p.m, TM);
+        count = (p.m > 0 && p.n > 0) ? m_blocks * ceil_div64(p.n, TN) : 0;
       }
       const int total_problems = p.single ? 1 : p.problem_count;
       if (count == 0) return false;
@@ -176,7 +210,11 @@ struct TileWalk {
       if (e != problem) {
         problem = static_cast<int>(e);
         first = e * count;
-        prob = load_problem(p, problem);
+        if (problem == ahead_problem) {
+          prob = homogeneous_problem(p, ahead_a, ahead_b, ahead_c);
+        } else {
+          prob = load_problem(p, problem);
+        }
       }
       ufirst = e * ucount;
     } else if (p.unit_start != nullptr) {
@@ -239,7 +277,9 @@ struct TileWalk {
     }
     unit_index = unit_index < 0 ? first_unit : unit_index + stride;
     int64_t t0 = 0, t1 = 0;
-    if (!seek_unit(p, unit_index, p.unit_tiles > 0 ? p.unit_tiles : 1, t0, t1)) return false;
+    const int64_t unit = p.unit_tiles > 0 ? p.unit_tiles : 1;
+    if (!seek_unit(p, unit_index, unit, t0, t1)) return false;
+    prefetch_unit(p, unit_index + stride, unit);
     t = t0;
     unit_next = t0 + 1;
     unit_end = t1;

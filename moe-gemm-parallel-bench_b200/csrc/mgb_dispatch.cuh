@@ -17,6 +17,7 @@ struct TcVariant {
   int tm;
   int tn;
   bool pair = false;
+  bool promote = false;  // fp32 only: accumulator chunks summed in registers (tc_grouped_kernel PROMOTE)
 };
 
 // Compile-time facts of a variant the host needs (box sizes, ring depth, slots),

@@ -5,6 +5,9 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <type_traits>
+#include <utility>
+
 #include "mgb_dispatch.cuh"
 #include "mgb_simt_kernel.cuh"
 #include "mgb_tc2_kernel.cuh"
@@ -26,7 +29,27 @@ namespace mgb {
   X(false, 128, 128)            \
   X(false, 128, 256)
 
-template <typename T, bool SWAP, int TM, int TN>
+// Launches a GEMM kernel on `stream`.  Grouped launches (maps built by
+// build_maps_kernel just before) carry programmatic stream serialization, so
+// the GEMM grid launches and sets up while the map builder still runs; the
+// kernel waits for it (grid_dependency_wait) before reading global memory.
+template <typename... Params, typename... Args>
+static cudaError_t launch_gemm(void (*kernel)(Params...), int grid, int smem, cudaStream_t stream, bool after_maps,
+                               Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(kTcThreads, 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = after_maps ? attr : nullptr;
+  cfg.numAttrs = after_maps ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+template <typename T, bool SWAP, int TM, int TN, bool PROMOTE = false>
 static int launch_variant(const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
                           const GroupedParams& p, int grid, cudaStream_t stream) {
   using Cfg = TcCfg<T, SWAP, TM, TN>;
@@ -35,13 +58,14 @@ static int launch_variant(const CUtensorMap& act, const CUtensorMap& wgt, const 
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 128) return static_cast<int>(cudaErrorInvalidDevice);
   if (!configured[dev]) {
-    const cudaError_t e = cudaFuncSetAttribute(tc_grouped_kernel<T, SWAP, TM, TN>,
+    const cudaError_t e = cudaFuncSetAttribute(tc_grouped_kernel<T, SWAP, TM, TN, PROMOTE>,
                                                cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes);
     if (e != cudaSuccess) return static_cast<int>(e);
     configured[dev] = true;
   }
-  tc_grouped_kernel<T, SWAP, TM, TN><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(act, wgt, out, p);
-  return static_cast<int>(cudaGetLastError());
+  const cudaError_t e = launch_gemm(tc_grouped_kernel<T, SWAP, TM, TN, PROMOTE>, grid, Cfg::kSmemBytes, stream,
+                                    !p.single, act, wgt, out, p);
+  return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
 }
 
 // The CTA-pair kernel exists for 16-bit types only.
@@ -101,8 +125,9 @@ static int launch_pair(const CUtensorMap& act, const CUtensorMap& wgt, const CUt
       if (e != cudaSuccess) return static_cast<int>(e);
       configured[dev] = true;
     }
-    tc2_grouped_kernel<T, NH><<<grid, kTcThreads, Cfg::kSmemBytes, stream>>>(act, wgt, out, p);
-    return static_cast<int>(cudaGetLastError());
+    const cudaError_t e = launch_gemm(tc2_grouped_kernel<T, NH>, grid, Cfg::kSmemBytes, stream, !p.single, act, wgt,
+                                      out, p);
+    return static_cast<int>(e != cudaSuccess ? e : cudaGetLastError());
   }
 }
 
@@ -120,6 +145,14 @@ static bool pair_variant_info(const TcVariant& v, TcVariantInfo* info) {
 
 template <>
 bool tc_variant_info<MGB_ELEM>(const TcVariant& v, TcVariantInfo* info) {
+  if (v.promote) {
+    if constexpr (std::is_same<MGB_ELEM, float>::value) {
+      using Cfg = TcCfg<float, false, 128, 128>;
+      *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSmemBytes, 0, 128, 128};
+      return v.tm == 128 && v.tn == 128 && !v.swap && !v.pair;
+    }
+    return false;
+  }
   if (v.pair) return v.tn > 256 ? pair_variant_info<MGB_ELEM, 2>(v, info) : pair_variant_info<MGB_ELEM, 1>(v, info);
 #define MGB_INFO(S, M, N)                                                               \
   if (v.swap == S && v.tm == M && v.tn == N) {                                          \
@@ -135,6 +168,12 @@ bool tc_variant_info<MGB_ELEM>(const TcVariant& v, TcVariantInfo* info) {
 template <>
 int tc_launch<MGB_ELEM>(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
                         const GroupedParams& p, int grid, cudaStream_t stream) {
+  if (v.promote) {
+    if constexpr (std::is_same<MGB_ELEM, float>::value) {
+      return launch_variant<float, false, 128, 128, true>(act, wgt, out, p, grid, stream);
+    }
+    return static_cast<int>(cudaErrorInvalidValue);
+  }
   if (v.pair) {
     return v.tn > 256 ? launch_pair<MGB_ELEM, 2>(act, wgt, out, p, grid, stream)
                       : launch_pair<MGB_ELEM, 1>(act, wgt, out, p, grid, stream);

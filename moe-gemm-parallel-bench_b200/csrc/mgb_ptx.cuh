@@ -177,6 +177,15 @@ __device__ __forceinline__ void tmap_publish(void* gmem_map, void* smem_map) {
       : "memory");
 }
 
+// Programmatic dependent launch.  A kernel launched with programmatic stream
+// serialization may start while the kernel before it on the stream still
+// runs; griddepcontrol.wait blocks until that kernel has completed and its
+// memory operations are visible, so it must come before any global-memory
+// read of data the earlier kernel writes.  launch_dependents lets the next
+// kernel start early (a block that exits counts as having triggered it).
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ void tmap_acquire(const void* gmem_map) {
   asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(gmem_map) : "memory");
 }

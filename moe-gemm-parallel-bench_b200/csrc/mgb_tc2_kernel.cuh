@@ -101,6 +101,8 @@ __device__ __forceinline__ bool next_item(Walk& walk, const GroupedParams& p, in
   }
   int64_t t0 = 0, t1 = 0;
   if (!walk.seek_unit(p, tile, 1, t0, t1)) return false;
+  const int64_t next = item + stride;
+  walk.prefetch_unit(p, next < p.tail_from ? next : p.tail_from + ((next - p.tail_from) >> 1), 1);
   t = t0;
   return true;
 }
@@ -160,6 +162,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const long long budget = p.wait_budget;
+  // Programmatic dependent launch behind build_maps_kernel: global memory is
+  // read only from here on (see tc_grouped_kernel).
+  grid_dependency_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -179,6 +184,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
     TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
     uint32_t it = 0;
     int built = -1;
+    int ahead_acquired = -1;  // problem whose maps were acquired one unit early
     bool ok = true;
     int64_t item = -1;
     int half = -1;
@@ -202,7 +208,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         }
         if (kb == 0 && !p.single && walk.problem != built) {
           const CUtensorMap* g = problem_maps(p, walk.problem);  // built by build_maps_kernel
-          if (lane == 0) {
+          if (lane == 0 && walk.problem != ahead_acquired) {
             tmap_acquire(&g[0]);
             tmap_acquire(&g[1]);
           }
@@ -232,6 +238,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
                                pol_wgt);
             }
           }
+          if (kb == 0) acquire_ahead_maps(p, walk.ahead_problem, ahead_acquired, 2);
         }
         __syncwarp();
         ++it;

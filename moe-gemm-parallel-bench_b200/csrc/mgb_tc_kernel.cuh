@@ -438,6 +438,43 @@ __device__ __forceinline__ void store_rows_scalar_swiglu(const Problem& qo, uint
   }
 }
 
+// Writes the warp's staged 32 x 128-byte block (rows row0.., columns col0..,
+// in the 128-byte swizzle of write_chunk_smem) to C through C's strides:
+// every global store instruction writes four whole 128-byte row segments;
+// columns past C and rows past M are skipped.
+template <typename T>
+__device__ __forceinline__ void flush_block_rows(const Problem& q, const uint8_t* block, int64_t row0, int64_t col0,
+                                                 int lane) {
+  constexpr int E = static_cast<int>(sizeof(T));
+  constexpr int kUnitCols = 16 / E;  // columns per 16-byte unit
+  const int j = lane & 7;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = 4 * i + (lane >> 3);
+    const uint4 val = *reinterpret_cast<const uint4*>(block + r * 128 + ((j ^ (r & 7)) << 4));
+    const int64_t row = row0 + r;
+    const int64_t col = col0 + j * kUnitCols;
+    if (row < q.m) {
+      char* dst = q.c + (row * q.scm + col * q.scn) * static_cast<int64_t>(E);
+      if (q.scn == 1 && col + kUnitCols <= q.n && (reinterpret_cast<uint64_t>(dst) % 16 == 0)) {
+        *reinterpret_cast<uint4*>(dst) = val;
+      } else {
+        const uint32_t parts[4] = {val.x, val.y, val.z, val.w};
+#pragma unroll
+        for (int e = 0; e < kUnitCols; ++e) {
+          if (col + e >= q.n) break;
+          char* d = q.c + (row * q.scm + (col + e) * q.scn) * static_cast<int64_t>(E);
+          if constexpr (E == 4) {
+            *reinterpret_cast<uint32_t*>(d) = parts[e];
+          } else {
+            *reinterpret_cast<uint16_t*>(d) = static_cast<uint16_t>(parts[e / 2] >> (16 * (e % 2)));
+          }
+        }
+      }
+    }
+  }
+}
+
 // Row-tile epilogue of one warp without TMA (C not addressable by a tensor
 // map): the chunk goes through `block` and is read back so that every global
 // store instruction writes four whole 128-byte row segments.
@@ -446,7 +483,6 @@ __device__ __forceinline__ void store_rows_staged(const Problem& q, uint32_t tad
                                                   uint8_t* block, int lane) {
   constexpr int E = static_cast<int>(sizeof(T));
   constexpr int kChunkCols = 128 / E;
-  constexpr int kUnitCols = 16 / E;  // columns per 16-byte unit
   static_assert(TN % kChunkCols == 0, "tile width is a whole number of chunks");
   if (lane == 0) bulk_wait_group_read<0>();  // no tensor store of this warp still reads its blocks
   __syncwarp();
@@ -457,34 +493,58 @@ __device__ __forceinline__ void store_rows_staged(const Problem& q, uint32_t tad
     tmem_ld_wait();
     write_chunk_smem<T>(v, block, lane);
     __syncwarp();
-    const int j = lane & 7;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int r = 4 * i + (lane >> 3);
-      const uint4 val = *reinterpret_cast<const uint4*>(block + r * 128 + ((j ^ (r & 7)) << 4));
-      const int64_t row = row0 + r;
-      const int64_t col = n0 + c * kChunkCols + j * kUnitCols;
-      if (row < q.m) {
-        char* dst = q.c + (row * q.scm + col * q.scn) * static_cast<int64_t>(E);
-        if (q.scn == 1 && col + kUnitCols <= q.n && (reinterpret_cast<uint64_t>(dst) % 16 == 0)) {
-          *reinterpret_cast<uint4*>(dst) = val;
-        } else {
-          const uint32_t parts[4] = {val.x, val.y, val.z, val.w};
-#pragma unroll
-          for (int e = 0; e < kUnitCols; ++e) {
-            if (col + e >= q.n) break;
-            char* d = q.c + (row * q.scm + (col + e) * q.scn) * static_cast<int64_t>(E);
-            if constexpr (E == 4) {
-              *reinterpret_cast<uint32_t*>(d) = parts[e];
-            } else {
-              *reinterpret_cast<uint16_t*>(d) = static_cast<uint16_t>(parts[e / 2] >> (16 * (e % 2)));
-            }
-          }
-        }
-      }
-    }
+    flush_block_rows<T>(q, block, row0, n0 + c * kChunkCols, lane);
     __syncwarp();  // the block is rewritten by the next chunk
   }
+}
+
+// Row-tile epilogue of one warp from fp32 registers (the promoted
+// accumulator of an fp32 tile): row `lane` of the warp's 32 rows holds TN
+// columns in acc.  Each 32-column chunk is staged in the warp's blocks in the
+// 128-byte swizzle and written by a tensor store when C has a map (`cmap`),
+// else read back and written as 128-byte row segments (store_rows_staged).
+template <int TN, int NB>
+__device__ __forceinline__ void store_rows_regs(const Problem& q, const void* cmap, const float (&acc)[TN],
+                                                int64_t row0, int64_t n0, uint8_t* blocks, int lane, uint32_t& seq,
+                                                uint64_t policy, uint32_t* error_word) {
+  static_assert(TN % 32 == 0, "whole 32-column chunks");
+  if (row0 >= q.m || n0 >= q.n) return;
+  const int64_t cols_left = q.n - n0;
+  const int chunks = cols_left >= TN ? TN / 32 : static_cast<int>((cols_left + 31) / 32);
+  if (cmap == nullptr) {
+    if (lane == 0) bulk_wait_group_read<0>();  // no tensor store of this warp still reads its blocks
+    __syncwarp();
+  }
+#pragma unroll
+  for (int c = 0; c < TN / 32; ++c) {
+    if (c >= chunks) break;
+    uint32_t v[2][16];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i / 16][i % 16] = __float_as_uint(acc[c * 32 + i]);
+    if (cmap != nullptr) {
+      uint8_t* block = blocks + ((seq + static_cast<uint32_t>(c)) % NB) * kEpiWarpBytes;
+      if (lane == 0) bulk_wait_group_read<NB - 1>();  // the store last issued from `block` has read it
+      __syncwarp();
+      write_chunk_smem<float>(v, block, lane);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int64_t x = n0 + c * 32;
+        if (x >= 0 && row0 >= 0 && x < q.n && row0 < q.m) {
+          tma_store_2d(cmap, block, static_cast<int32_t>(x), static_cast<int32_t>(row0), policy);
+          bulk_commit_group();
+        } else {
+          atomicOr(error_word, kErrBadStore);
+        }
+      }
+    } else {
+      write_chunk_smem<float>(v, blocks, lane);
+      __syncwarp();
+      flush_block_rows<float>(q, blocks, row0, n0 + c * 32, lane);
+      __syncwarp();  // the block is rewritten by the next chunk
+    }
+  }
+  if (cmap != nullptr) seq += static_cast<uint32_t>(chunks);
 }
 
 // Tensor maps of problem e in the scratch buffer: [A, B, C].
@@ -492,8 +552,25 @@ __device__ __forceinline__ const CUtensorMap* problem_maps(const GroupedParams& 
   return reinterpret_cast<const CUtensorMap*>(p.desc_slots) + static_cast<int64_t>(kMapsPerProblem) * e;
 }
 
+// Lookahead on the tensormap side (lane 0 of a role): acquires and prefetches
+// `count` maps of the problem the walk looked up ahead (`ahead`, -1: none),
+// starting at map `first_map`, once, so the switch to that problem neither
+// waits on the acquire fence nor on the descriptor fetch.  `acquired` records
+// the problem done.
+__device__ __forceinline__ void acquire_ahead_maps(const GroupedParams& p, int ahead, int& acquired, int count,
+                                                   int first_map = 0) {
+  if (p.single || ahead < 0 || ahead == acquired) return;
+  const CUtensorMap* g = problem_maps(p, ahead) + first_map;
+  for (int i = 0; i < count; ++i) {
+    tmap_acquire(&g[i]);
+    prefetch_tmap(&g[i]);
+  }
+  acquired = ahead;
+}
+
 // The output map of the epilogue's current problem: the launch's own map for a
-// single GEMM, else problem e's C map, acquired when the warp first meets e.
+// single GEMM, else problem e's C map, acquired when the warp first meets e
+// (before the accumulator wait, so the fence overlaps the tile's MMAs).
 __device__ __forceinline__ const void* out_map_for(const GroupedParams& p, const CUtensorMap& single_map, int e,
                                                    int& built, int lane) {
   if (p.single) return &single_map;
@@ -551,6 +628,9 @@ __global__ void __launch_bounds__(32)
   __shared__ alignas(128) CUtensorMap staging[kMapsPerProblem];
   const int e = blockIdx.x;
   const int lane = threadIdx.x;
+  // The GEMM kernel that follows may launch now: it only sets up its shared
+  // memory and TMEM before waiting for this grid (grid_dependency_wait).
+  grid_launch_dependents();
   if (e == p.problem_count && p.unit_start != nullptr) {
     write_unit_prefix(p, lane);
     return;
@@ -591,13 +671,26 @@ __global__ void __launch_bounds__(32)
   for (int i = 0; i < kMapsPerProblem; ++i) tmap_publish(&g[i], &staging[i]);
 }
 
-template <typename T, bool SWAP, int TM, int TN>
+// K blocks per accumulator chunk of a PROMOTE launch (256 fp32 K).
+constexpr int kPromoteBlocks = 8;
+
+// PROMOTE (fp32, 128-token tiles): the tensor core accumulates at most
+// kPromoteBlocks k-blocks into a TMEM accumulator, alternating between the two
+// accumulators chunk by chunk; the epilogue warps add every chunk into fp32
+// registers (round-to-nearest) and store the sum at the end of the tile.
+// Long TF32 accumulations inside the tensor core lose accuracy in proportion
+// to K (measured: 1.9e-5 relative at K = 8191 for exactly representable
+// inputs); chunking bounds that to one 256-deep chunk, which the 3xTF32 split
+// of fp32 "ieee" GEMMs needs to reach fp32 accuracy.
+template <typename T, bool SWAP, int TM, int TN, bool PROMOTE = false>
 __global__ void __launch_bounds__(kTcThreads, 1)
     tc_grouped_kernel(const __grid_constant__ CUtensorMap act_tmpl, const __grid_constant__ CUtensorMap wgt_tmpl,
                       const __grid_constant__ CUtensorMap out_tmpl, const GroupedParams p) {
   using Cfg = TcCfg<T, SWAP, TM, TN>;
   constexpr int S = Cfg::kStages;
   constexpr int BK = Cfg::kBK;
+  static_assert(!PROMOTE || (std::is_same<T, float>::value && !SWAP && TM == 128 && TN <= 128),
+                "promoted accumulation: fp32 128-token tiles of at most 128 columns");
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -640,6 +733,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const long long budget = p.wait_budget;
+  // Launched right behind build_maps_kernel with programmatic serialization:
+  // nothing above read global memory; everything below may (tables, maps,
+  // operands).  Without a programmatic dependency this returns at once.
+  grid_dependency_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -659,6 +756,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     TileWalk<TM, TN> walk;
     uint32_t it = 0;
     int built = -1;
+    int ahead_acquired = -1;  // problem whose maps were acquired one unit early
     bool ok = true;
     for (int64_t t = 0; ok && walk.next_tile(p, blockIdx.x, gridDim.x, t);) {
       const Problem& q = walk.prob;
@@ -680,9 +778,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         if (kb == 0 && !p.single && walk.problem != built) {
           // Entering a new problem: its maps were built before this kernel
-          // started (build_maps_kernel); acquire them for the tensormap proxy.
+          // started (build_maps_kernel); acquire them for the tensormap proxy
+          // (done a unit early when the walk looked this problem up ahead).
           const CUtensorMap* g = problem_maps(p, walk.problem);
-          if (lane == 0) {
+          if (lane == 0 && walk.problem != ahead_acquired) {
             tmap_acquire(&g[0]);
             tmap_acquire(&g[1]);
           }
@@ -702,6 +801,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tma_load_2d(wgt_map, &full[s], st_wgt + j * Cfg::kBoxBytes, weight_col<TN>(p, q, nb, j * BK), kx,
                         pol_wgt);
           }
+          if (kb == 0) acquire_ahead_maps(p, walk.ahead_problem, ahead_acquired, 2);
         }
         __syncwarp();
         ++it;
@@ -728,6 +828,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const Problem& q = walk.prob;
         if (!tile_legal<T>(p, q) || q.k <= 0) continue;
         const int64_t kblocks = (q.k + BK - 1) / BK;
+        // One accumulator per tile, or per chunk of kPromoteBlocks k-blocks.
+        const int64_t chunk_blocks = PROMOTE ? kPromoteBlocks : kblocks;
+        for (int64_t kb0 = 0; ok && kb0 < kblocks; kb0 += chunk_blocks) {
+        const int64_t kb1 = kb0 + chunk_blocks < kblocks ? kb0 + chunk_blocks : kblocks;
         const int buf = static_cast<int>(acc_it & 1u);
         if (!mbar_wait(&acc_empty[buf], ((acc_it >> 1) & 1u) ^ 1u, budget, abort)) {
           raise_error(p, kErrWaitAccEmpty, abort);
@@ -736,7 +840,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * Cfg::kAccCols);
-        for (int64_t kb = 0; kb < kblocks; ++kb) {
+        for (int64_t kb = kb0; kb < kb1; ++kb) {
           const int s = static_cast<int>(it % S);
           if (!mbar_wait(&full[s], (it / S) & 1u, budget, abort)) {
             raise_error(p, kErrWaitFull, abort);
@@ -748,7 +852,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           const uint32_t w_base = a_base + Cfg::kActBytes;
 #pragma unroll
           for (int ks = 0; ks < Cfg::kKSteps; ++ks) {
-            const uint32_t acc = (kb > 0 || ks > 0) ? 1u : 0u;
+            const uint32_t acc = (kb > kb0 || ks > 0) ? 1u : 0u;
             const uint64_t act_desc = smem_desc(a_base + ks * 32, 16, 1024, kLayoutSw128);
             if constexpr (SWAP) {
 #pragma unroll
@@ -775,8 +879,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           ++it;
         }
         if (!ok) break;
-        mma_commit(&acc_full[buf]);  // accumulator ready for the epilogue
+        mma_commit(&acc_full[buf]);  // accumulator (or chunk) ready for the epilogue
         ++acc_it;
+        }
+        if (!ok) break;
       }
       if (*abort) {
         mma_commit(drain_bar);
@@ -828,6 +934,41 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       const void* cmap = nullptr;
       if constexpr (!SWAP) {
         if (c_tma_legal<T>(q, q.n)) cmap = out_map_for(p, out_tmpl, walk.problem, c_built, lane);
+      }
+      if constexpr (PROMOTE) {
+        // Sum the tile's accumulator chunks in fp32 registers (row `lane` of
+        // the warp's quarter, TN columns), then store the sum.
+        float sum[TN];
+#pragma unroll
+        for (int i = 0; i < TN; ++i) sum[i] = 0.0f;
+        const int64_t kblocks = (q.k + BK - 1) / BK;
+        for (int64_t kb0 = 0; kb0 < kblocks; kb0 += kPromoteBlocks) {
+          const int cbuf = static_cast<int>(acc_it & 1u);
+          if (!mbar_wait_warp(&acc_full[cbuf], (acc_it >> 1) & 1u, budget, abort)) {
+            if (lane == 0) raise_error(p, kErrWaitAccFull, abort);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ctaddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
+                                  static_cast<uint32_t>(cbuf * Cfg::kAccCols);
+          uint32_t v[2][16];  // 16-column units, the next one in flight while one is added
+          tmem_ld16(ctaddr, v[0]);
+#pragma unroll
+          for (int u = 0; u < TN / 16; ++u) {
+            tmem_ld_wait();  // unit u has landed
+            if (u + 1 < TN / 16) tmem_ld16(ctaddr + (u + 1) * 16, v[(u + 1) & 1]);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) sum[u * 16 + i] += __uint_as_float(v[u & 1][i]);
+          }
+          tc_fence_before();
+          mbar_arrive_relaxed(&acc_empty[cbuf]);
+          ++acc_it;
+        }
+        if (!ok) break;
+        store_rows_regs<TN, Cfg::kEpiBlocks>(q, cmap, sum, m0 + quarter * 32, n0, my_blocks, lane, chunk_seq, pol_out,
+                                             p.error_word);
+        continue;
       }
       const int buf = static_cast<int>(acc_it & 1u);
       if (!mbar_wait_warp(&acc_full[buf], (acc_it >> 1) & 1u, budget, abort)) {

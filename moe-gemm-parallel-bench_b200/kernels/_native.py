@@ -18,7 +18,10 @@ LIBRARY_PATH = Path(os.environ.get("MGB_LIBRARY", Path(__file__).resolve().paren
 
 # enum values of include/moe_gemm_b200.h
 DTYPE_CODES = {"fp16": 0, "bf16": 1, "fp32": 2}
-PRECISION_CODES = {"ieee": 0, "tf32": 1}
+PRECISION_CODES = {"ieee": 0, "tf32": 1, "tf32_fp32acc": 2}
+# The precisions of the reference's API (kernels/matmul.py:268); "tf32_fp32acc" is
+# internal: TF32 products with chunked fp32 accumulation, used on 3xTF32 operands.
+PUBLIC_PRECISIONS = ("ieee", "tf32")
 STATUS_OK = 0
 STATUS_INVALID = 1
 STATUS_UNSUPPORTED = 2
@@ -48,6 +51,7 @@ EXPORTED_SYMBOLS = (
     "grouped_gemm_launch_noalloc",
     "matmul_launch",
     "matrix_repack",
+    "matrix_split_tf32x3",
     "read_and_clear_error_word",
     "mgb_set_debug",
     "mgb_status_string",
@@ -238,6 +242,11 @@ def _declare(lib) -> None:
         ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
     ]
     lib.matrix_repack.restype = ctypes.c_int
+    lib.matrix_split_tf32x3.argtypes = [
+        ctypes.c_void_p, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p,
+        ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
+    ]
+    lib.matrix_split_tf32x3.restype = ctypes.c_int
     lib.read_and_clear_error_word.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32)]
     lib.read_and_clear_error_word.restype = ctypes.c_int
     lib.mgb_set_debug.argtypes = [ctypes.c_int64, ctypes.c_int32]
@@ -447,9 +456,12 @@ def grouped_launch_noalloc(
     m: int, n: int, k: int, dtype: str, precision: str, tma_aligned: bool, config, stream: int,
 ) -> LaunchInfo:
     """grouped_gemm_launch_noalloc: the grouped launch for callers that cannot
-    allocate device memory (its scratch is a fixed array inside the library).
-    The first call on a device must come before any stream capture; calls that
-    overlap on the GPU race on the shared array."""
+    allocate device memory (a plugin whose host framework owns all device
+    memory, a launch path that must not enter the driver's allocator): its
+    tensor-map scratch is a fixed array inside the library.  The first call on
+    a device looks the array up and must come before any stream capture;
+    groups of more than 2674 problems are refused; calls that overlap on the
+    GPU race on the shared array."""
     info = LaunchInfo()
     cfg = tile_config(config)
     status = load().grouped_gemm_launch_noalloc(
@@ -480,6 +492,15 @@ def repack(src: int, rows: int, cols: int, stride_r: int, stride_c: int, dst: in
     """matrix_repack: copy a strided matrix into a row-pitched buffer."""
     _check(load().matrix_repack(src, int(rows), int(cols), int(stride_r), int(stride_c), dst, int(dst_pitch),
                                 int(elem_bytes), stream), "matrix_repack")
+
+
+def split_tf32x3(src: int, rows: int, cols: int, stride_r: int, stride_c: int, dst: int, dst_pitch: int,
+                side: int, stream: int) -> None:
+    """matrix_split_tf32x3: the 3xTF32 operand split of an fp32 matrix (side 0:
+    A -> [hi | lo | hi] along its columns; side 1: B -> [hi; hi; lo] along its
+    rows)."""
+    _check(load().matrix_split_tf32x3(src, int(rows), int(cols), int(stride_r), int(stride_c), dst, int(dst_pitch),
+                                      int(side), stream), "matrix_split_tf32x3")
 
 
 def read_and_clear_error_word(device: int) -> int:

@@ -410,7 +410,7 @@ def launch_grouped(
     if torch is None or not torch.cuda.is_available():
         raise RuntimeError("CUDA PyTorch and the native sm_100a library are required")
     _native.load()
-    if input_precision not in _native.PRECISION_CODES:
+    if input_precision not in _native.PUBLIC_PRECISIONS:
         raise ValueError(f"input_precision must be 'ieee' or 'tf32', got {input_precision!r}")
     cfg = config or workspace.config
     if workspace.problem_count == 1 and workspace.operation != "swiglu":
@@ -497,7 +497,7 @@ def launch_grouped_mm(mat_a, mat_b, offs, out=None, *, config: KernelConfig | No
         raise ValueError(f"out must be [{total}, {out_n}] {mat_a.dtype} on {mat_a.device}")
     if mat_a.stride(1) != 1 or mat_b.stride(2) != 1 or out.stride(1) != 1 or mat_b.stride(0) < k * mat_b.stride(1):
         raise ValueError("columns of mat_a, mat_b and out must be contiguous (row padding is allowed)")
-    if input_precision not in _native.PRECISION_CODES:
+    if input_precision not in _native.PUBLIC_PRECISIONS:
         raise ValueError(f"input_precision must be 'ieee' or 'tf32', got {input_precision!r}")
     key = (mat_a.device.index or 0, segments)
     scratch = _AGGREGATE_SCRATCH.get(key)

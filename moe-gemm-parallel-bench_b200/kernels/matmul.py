@@ -217,7 +217,7 @@ def _validate_matrices(a, b, c) -> tuple[int, int, int]:
 
 
 def _check_precision(input_precision: str) -> str:
-    if input_precision not in _native.PRECISION_CODES:
+    if input_precision not in _native.PUBLIC_PRECISIONS:
         raise ValueError(f"input_precision must be 'ieee' or 'tf32', got {input_precision!r}")
     return input_precision
 
@@ -246,9 +246,38 @@ def _repacked(x, stream: int):
     return buffer[:, :cols]
 
 
+def split_operands_3xtf32(a, b, stream: int):
+    """The 3xTF32 operands of an fp32 "ieee" GEMM (matrix_split_tf32x3):
+    A' = [hi(A) | lo(A) | hi(A)] of shape [M, 3K] and B' = [hi(B); hi(B);
+    lo(B)] of shape [3K, N], in buffers whose row pitch is a multiple of 16
+    bytes.  A' @ B' in TF32 = hi hi + lo hi + hi lo, which restores fp32
+    accuracy (Ootomo & Yokota 2022) on the tensor cores."""
+    m, k = a.shape
+    n = b.shape[1]
+    a3 = torch.empty((m, -(-3 * k // 4) * 4), dtype=torch.float32, device=a.device)[:, :3 * k]
+    b3 = torch.empty((3 * k, -(-n // 4) * 4), dtype=torch.float32, device=a.device)[:, :n]
+    _native.split_tf32x3(a.data_ptr(), m, k, a.stride(0), a.stride(1), a3.data_ptr(), a3.stride(0), 0, stream)
+    _native.split_tf32x3(b.data_ptr(), k, n, b.stride(0), b.stride(1), b3.data_ptr(), b3.stride(0), 1, stream)
+    return a3, b3
+
+
 def _launch_once(a, b, c, m: int, n: int, k: int, config: KernelConfig, precision: str) -> dict:
     global _last_launch_info
     stream = torch.cuda.current_stream(a.device).cuda_stream
+    if a.dtype == torch.float32 and precision == "ieee" and 2 * m * n * k >= REPACK_MIN_FLOPS and k > 0:
+        # Full fp32 accuracy on the tensor cores: one TF32 GEMM of depth 3K
+        # over the split operands, its accumulator summed in fp32 registers
+        # every 256 K (the tensor core's own accumulation loses accuracy in
+        # proportion to K).
+        with torch.cuda.device(a.device):
+            a3, b3 = split_operands_3xtf32(a, b, stream)
+            info = _native.matmul_launch(
+                a3.data_ptr(), b3.data_ptr(), c.data_ptr(), m, n, 3 * k,
+                (a3.stride(0), 1, b3.stride(0), 1, c.stride(0), c.stride(1)), "fp32", "tf32_fp32acc", config,
+                stream,
+            )
+        _last_launch_info = {**info.as_dict(), "repacked": True, "split_3xtf32": True}
+        return _last_launch_info
     tensor_core = a.dtype != torch.float32 or precision == "tf32"
     repacked = False
     with torch.cuda.device(a.device):
@@ -262,7 +291,7 @@ def _launch_once(a, b, c, m: int, n: int, k: int, config: KernelConfig, precisio
             (a.stride(0), a.stride(1), b.stride(0), b.stride(1), c.stride(0), c.stride(1)),
             dtype_name(a.dtype), precision, config, stream,
         )
-    _last_launch_info = {**info.as_dict(), "repacked": repacked}
+    _last_launch_info = {**info.as_dict(), "repacked": repacked, "split_3xtf32": False}
     return _last_launch_info
 
 

@@ -12,12 +12,14 @@
   row and u^T C = (u^T A) B per column.  Unlike 1^T C = (1^T A) B they see
   a row or column written to the wrong place.
 * configs[4]'s masked single-GEMM sweep over every {127, 1000, 4095, 8191}^3
-  shape in fp32 with TF32 inputs: sampled rows against the float64 oracle and
-  Freivalds checks of the whole output.
+  shape in fp32, with TF32 inputs and with full fp32 products ("ieee", the
+  3xTF32 split on the tensor cores): sampled rows against the float64 oracle
+  and Freivalds checks of the whole output.
 
 Tolerances: relative Frobenius error bf16 <= 1e-2 (the target's bound) and
 against the stored checker outputs also <= 1e-2; fp32 "ieee" <= 1e-5; fp32
-"tf32" <= 5e-3; Freivalds relative error <= 1e-2 (bf16) / 5e-3 (tf32).
+"tf32" <= 5e-3; Freivalds relative error <= 1e-2 (bf16) / 5e-3 (tf32) /
+1e-5 (fp32 "ieee").
 """
 
 from __future__ import annotations
@@ -184,27 +186,63 @@ def test_full_size_rank_freivalds(rank_kind, m_e):
 SWEEP = (127, 1000, 4095, 8191)
 
 
+@pytest.mark.parametrize("precision", ["tf32", "ieee"])
 @pytest.mark.parametrize("m,k,n", list(itertools.product(SWEEP, SWEEP, SWEEP)),
                          ids=lambda v: str(v))
-def test_masked_sweep_tf32(m, k, n):
-    """One shape of the Qwen3 masked single-GEMM sweep (fp32, TF32 inputs,
-    non-tile-multiple M, N, K): launch_matmul, Freivalds checks of the whole
-    output and the float64 oracle on sampled rows."""
+def test_masked_sweep_fp32(m, k, n, precision):
+    """One shape of the Qwen3 masked single-GEMM sweep (fp32, non-tile-multiple
+    M, N, K) with TF32 inputs, and with full fp32 products ("ieee": the
+    3xTF32 split on the tensor cores for large shapes): launch_matmul,
+    Freivalds checks of the whole output and the float64 oracle on sampled
+    rows."""
     torch = _torch()
     from kernels import check_device_errors, launch_matmul
+    from kernels.matmul import REPACK_MIN_FLOPS, last_launch_info
     from oracle import gemm as oracle
 
+    tol = REL_FRO_TF32 if precision == "tf32" else REL_FRO_FP32_IEEE
     gen = torch.Generator(device="cuda").manual_seed(m * 7 + k * 3 + n)
     a = torch.randn((m, k), device="cuda", generator=gen)
     b = torch.randn((k, n), device="cuda", generator=gen) / math.sqrt(k)
     c = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float32)
-    launch_matmul(a, b, c, input_precision="tf32")
+    launch_matmul(a, b, c, input_precision=precision)
     torch.cuda.synchronize()
     check_device_errors()
+    info = last_launch_info()
+    if 2 * m * n * k >= REPACK_MIN_FLOPS:
+        assert info["path"].startswith("tcgen05_tma"), info
+        assert info["split_3xtf32"] == (precision == "ieee"), info
     assert not torch.isnan(c).any(), "unwritten outputs"
     row, col = _freivalds(a, b, c, torch.Generator(device="cuda").manual_seed(9))
-    assert row <= REL_FRO_TF32 and col <= REL_FRO_TF32, (row, col)
+    assert row <= tol and col <= tol, (row, col)
     rows = torch.tensor(sorted({0, 1, m // 3, m // 2, m - 2, m - 1}), device="cuda")
     got = c.index_select(0, rows).double().cpu().numpy()
     expected = oracle.matmul(a.index_select(0, rows).double().cpu().numpy(), b.double().cpu().numpy(), "fp32")
-    assert _rel_fro(got, expected) <= REL_FRO_TF32
+    assert _rel_fro(got, expected) <= tol
+
+
+def test_split_tf32x3_layout_and_rounding():
+    """matrix_split_tf32x3: hi has its low 13 mantissa bits clear, hi + lo
+    recovers x to within 2^-21 of |x|, and the halves land where the 3K-deep
+    GEMM expects them (A: [hi | lo | hi] along columns, B: [hi; hi; lo] along
+    rows), from a strided source."""
+    torch = _torch()
+    from kernels.matmul import split_operands_3xtf32
+
+    gen = torch.Generator(device="cuda").manual_seed(3)
+    base = torch.randn((37, 2 * 19), device="cuda", generator=gen) * 1e3
+    a = base[:, ::2]  # [37, 19], column stride 2
+    b = torch.randn((19, 23), device="cuda", generator=gen)
+    a3, b3 = split_operands_3xtf32(a, b, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert a3.shape == (37, 57) and b3.shape == (57, 23)
+    assert (a3.stride(0) * 4) % 16 == 0 and (b3.stride(0) * 4) % 16 == 0
+    hi_a, lo_a = a3[:, :19], a3[:, 19:38]
+    assert torch.equal(a3[:, 38:], hi_a)
+    assert torch.equal(b3[:19], b3[19:38])
+    for hi, lo, x in ((hi_a, lo_a, a), (b3[:19], b3[38:], b)):
+        assert (hi.contiguous().view(torch.int32) & 0x1FFF).eq(0).all()
+        assert (lo.contiguous().view(torch.int32) & 0x1FFF).eq(0).all()
+        err = ((hi.double() + lo.double()) - x.double()).abs()
+        assert (err <= x.double().abs() * 2.0 ** -21).all()
+        assert ((hi.double() - x.double()).abs() <= x.double().abs() * 2.0 ** -11).all()
