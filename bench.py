@@ -1204,32 +1204,37 @@ def reference_gpu_arm(args, rank: int, world: int) -> None:
         }), flush=True)
 
 
-def time_alone_ms(fn, reps: int = 15) -> float:
-    """Median CUDA-event time of `fn` launched back to back on the current
-    stream, hot, after three untimed calls."""
+def paired_ms(fn_a, fn_b, reps: int = 15) -> tuple[float, float]:
+    """Median CUDA-event times of `fn_a` and `fn_b` launched alternately
+    (a, b, a, b, ...) back to back on the current stream, hot, after three
+    untimed rounds.  Alternating gives both the same clock and power state,
+    which drifts over a run of heavy launches on a power-capped GPU."""
     import torch
 
     for _ in range(3):
-        fn()
+        fn_a()
+        fn_b()
     torch.cuda.synchronize()
-    pairs = []
+    pairs_a, pairs_b = [], []
     for _ in range(reps):
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        fn()
-        end.record()
-        pairs.append((start, end))
+        for fn, pairs in ((fn_a, pairs_a), (fn_b, pairs_b)):
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            fn()
+            end.record()
+            pairs.append((start, end))
     torch.cuda.synchronize()
-    return statistics.median(s.elapsed_time(e) for s, e in pairs)
+    return (statistics.median(s.elapsed_time(e) for s, e in pairs_a),
+            statistics.median(s.elapsed_time(e) for s, e in pairs_b))
 
 
 def grouped_mm_side_by_side(steps: dict, device) -> dict:
     """Per launch of the step: this package's launch alone and
     torch.nn.functional.grouped_mm on the same operands (the call of the
     reference's torch provider, kernels/torch_grouped_gemm.py:162-174: A
-    [E * M_e, K], B [E, K, N], int32 cumulative offsets), both timed the same
-    way; the relative Frobenius difference of their outputs on the first two
-    experts rides along."""
+    [E * M_e, K], B [E, K, N], int32 cumulative offsets), timed alternately
+    (paired_ms); the relative Frobenius difference of their outputs on the
+    first two experts rides along."""
     import torch
 
     out = {}
@@ -1238,14 +1243,13 @@ def grouped_mm_side_by_side(steps: dict, device) -> dict:
             if (par, m) not in rank_step.stacks:
                 continue
             a2d, b3d, offs = rank_step.stacks[(par, m)]
-            native_ms = time_alone_ms(lambda: launch(ws))
             holder = {}
 
             def run_grouped_mm():
                 holder.pop("c", None)  # lets the caching allocator reuse the previous output's storage
                 holder["c"] = torch.nn.functional.grouped_mm(a2d, b3d, offs=offs)
 
-            gm_ms = time_alone_ms(run_grouped_mm)
+            native_ms, gm_ms = paired_ms(lambda: launch(ws), run_grouped_mm)
             m_rows = ws.shapes[0][0]
             ours = torch.cat([ws.c[i] for i in range(2)]).float()
             theirs = holder["c"][:2 * m_rows].float()
@@ -1542,8 +1546,9 @@ def main(argv=None) -> int:
                 "native_wins": sum(1 for r in compared if r["vs_grouped_mm"] > 1.0), "shapes": len(compared),
                 "step_ms_native_alone": round(sum(r["alone_ms"] for r in compared), 4),
                 "step_ms_grouped_mm": round(sum(r["grouped_mm_ms"] for r in compared), 4),
-                "note": "each launch alone, hot, median of 15 back-to-back CUDA-event-timed calls; grouped_mm = "
-                        "torch.nn.functional.grouped_mm on the same operands (the reference's torch provider)"},
+                "note": "each launch alone, hot, alternating with grouped_mm call by call, median of 15 "
+                        "CUDA-event-timed calls each; grouped_mm = torch.nn.functional.grouped_mm on the same "
+                        "operands (the reference's torch provider)"},
             "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind",
                                                                               "sample")},
             "e2e": {"value": round(rank_flops * world * e2e_steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
