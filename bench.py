@@ -50,21 +50,52 @@ for _p in (str(ROOT), str(PACKAGE_DIR)):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
+# MoE dimensions of the reference's bundled model configs (model_configs/*.json:
+# hidden_size, moe_intermediate_size or intermediate_size, routed experts,
+# experts per token) and the tokens-per-expert sweep BASELINE.json names for each.
+MODELS = {
+    "deepseek-v3": {"hidden": 7168, "ffn": 2048, "experts": 256, "topk": 8,
+                    "m_values": (16, 32, 64, 128, 256, 512, 1024), "label": "DeepSeek-V3"},
+    "mixtral-8x7b": {"hidden": 4096, "ffn": 14336, "experts": 8, "topk": 2, "m_values": (1024,),
+                     "label": "Mixtral-8x7B"},
+    "qwen3-235b-a22b": {"hidden": 4096, "ffn": 1536, "experts": 128, "topk": 8, "m_values": (16, 64, 256, 1024),
+                        "label": "Qwen3-235B-A22B"},
+}
+MODEL = "deepseek-v3"
 HIDDEN, FFN, EXPERTS, TOPK, PARALLEL = 7168, 2048, 256, 8, 8
-M_VALUES = (16, 32, 64, 128, 256, 512, 1024)
+M_VALUES = MODELS[MODEL]["m_values"]
+
+
+def set_model(name: str, parallel: int) -> None:
+    """Makes `name` (a MODELS key) and P = `parallel` the workload of this process."""
+    global MODEL, HIDDEN, FFN, EXPERTS, TOPK, PARALLEL, M_VALUES
+    if name not in MODELS:
+        raise SystemExit(f"unknown --model {name!r}; one of {sorted(MODELS)}")
+    spec = MODELS[name]
+    if spec["experts"] % parallel or spec["ffn"] % parallel:
+        raise SystemExit(f"--parallel-size {parallel} must divide {spec['experts']} experts and F = {spec['ffn']}")
+    MODEL, PARALLEL = name, parallel
+    HIDDEN, FFN, EXPERTS, TOPK = spec["hidden"], spec["ffn"], spec["experts"], spec["topk"]
+    M_VALUES = spec["m_values"]
 METRIC = "grouped-GEMM TFLOP/s per B200 (EP vs TP, W13 & W2) and % of roofline"
 # Used only when MEASURED_PEAKS.json is absent: an earlier measurement on this
 # pool (copy bandwidth; cuBLAS bf16 burst, and sustained at ~1.3 GHz under the
 # 1 kW cap).
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0,
                   "sm_max_mhz": 1965.0, "sustained_sm_mhz": 1300.0}
-WORKLOADS = {
-    "W1": ("DeepSeek-V3 W13 gate+up bf16, P=8 rank shapes: EP 32 x [M_e,7168]@[7168,4096] and "
-           "TP 256 x [M_e,7168]@[7168,512], M_e in {16,32,64,128,256,512,1024}"),
-    "W2": ("DeepSeek-V3 W2 down bf16, P=8 rank shapes: EP 32 x [M_e,2048]@[2048,7168] and "
-           "TP 256 x [M_e,256]@[256,7168] (partial sums), M_e in {16,32,64,128,256,512,1024}"),
-}
 PROJECTION_NAME = {"W1": "W13", "W2": "W2"}
+
+
+def workload_line(projection: str, m_values=None) -> str:
+    """One projection's rank shapes under the current model and P."""
+    label = MODELS[MODEL]["label"]
+    ms = "{" + ",".join(str(m) for m in (m_values or M_VALUES)) + "}"
+    ep, tp = EXPERTS // PARALLEL, EXPERTS
+    if projection == "W1":
+        return (f"{label} W13 gate+up bf16, P={PARALLEL} rank shapes: EP {ep} x [M_e,{HIDDEN}]@[{HIDDEN},{2 * FFN}] "
+                f"and TP {tp} x [M_e,{HIDDEN}]@[{HIDDEN},{2 * FFN // PARALLEL}], M_e in {ms}")
+    return (f"{label} W2 down bf16, P={PARALLEL} rank shapes: EP {ep} x [M_e,{FFN}]@[{FFN},{HIDDEN}] and "
+            f"TP {tp} x [M_e,{FFN // PARALLEL}]@[{FFN // PARALLEL},{HIDDEN}] (partial sums), M_e in {ms}")
 
 
 def projection_dims(projection: str) -> dict:
@@ -87,7 +118,16 @@ def parse_args(argv=None):
     p.add_argument("--skip-cpu-baseline", action="store_true")
     p.add_argument("--skip-grouped-mm", action="store_true",
                    help="leave out the per-shape torch grouped_mm side-by-side")
-    p.add_argument("--m-values", type=str, default=",".join(map(str, M_VALUES)))
+    p.add_argument("--m-values", type=str, default=None,
+                   help="tokens per expert (default: the model's sweep from BASELINE.json)")
+    p.add_argument("--model", choices=sorted(MODELS), default="deepseek-v3",
+                   help="MoE dimensions: deepseek-v3 (configs[1]/[2], the benchmark line), mixtral-8x7b "
+                        "(configs[3]), qwen3-235b-a22b (configs[4])")
+    p.add_argument("--parallel-size", type=int, default=8,
+                   help="P of the EP/TP layout; GPU r runs rank r of it")
+    p.add_argument("--masked-sweep", action="store_true",
+                   help="configs[4]'s masked single-GEMM sweep over {127,1000,4095,8191}^3 in fp32 (TF32 inputs "
+                        "and full fp32 products) next to torch.mm, one JSON line")
     p.add_argument("--projection", choices=("both", "W1", "W2"), default="both",
                    help="both: W13 and W2 in one step (the benchmark line); W1: packed W13 gate+up only "
                         "(BASELINE configs[1]); W2: down projection only (configs[2])")
@@ -753,6 +793,11 @@ def verify_rank_outputs(rank, world, ep, tp, activations, outputs, device, m_val
 
 
 # ------------------------------------------------------------- CPU leg
+def m_values_of(args) -> list[int]:
+    """Tokens per expert of the run: --m-values, else the model's sweep."""
+    return [int(v) for v in args.m_values.split(",")] if args.m_values else list(M_VALUES)
+
+
 def selected_projections(args) -> tuple[str, ...]:
     """Projections of the step: both by default (the metric names W13 and W2);
     the W13-only modes (--fp8, --fused-swiglu, --layout aggregate) run W1."""
@@ -773,12 +818,13 @@ def cold_projections(args, projections) -> tuple[str, ...]:
     return tuple(p for p in projections if p == "W2")
 
 
-def workload_text(projections, cold=()) -> str:
+def workload_text(projections, cold=(), m_values=None) -> str:
     parts = []
     for proj in projections:
         mode = "rotating-cold (two resident workspace sets, step s runs set s % 2)" if proj in cold else "hot"
-        parts.append(f"{WORKLOADS[proj]}, {mode}")
-    return "; ".join(parts) + f"; one step = {14 * len(projections)} grouped launches"
+        parts.append(f"{workload_line(proj, m_values)}, {mode}")
+    launches = 2 * len(m_values or M_VALUES) * len(projections)
+    return "; ".join(parts) + f"; one step = {launches} grouped launches"
 
 
 def cpu_problems(m_values, experts_per_launch: int, seed: int, projections=("W1",)):
@@ -837,7 +883,7 @@ def reference_arm(args, rank: int, world: int) -> None:
 
     from oracle.cpu_baseline import host_threads, per_expert_mm
 
-    m_values = [int(v) for v in args.m_values.split(",")]
+    m_values = m_values_of(args)
     projections = selected_projections(args)
     threads = host_threads()
     torch.set_num_threads(threads)
@@ -857,7 +903,8 @@ def reference_arm(args, rank: int, world: int) -> None:
         "metric": METRIC, "value": round(value, 4), "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(elapsed / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": workload_text(projections, cold_projections(args, projections)), "sample": sample,
+        "config": {"workload": workload_text(projections, cold_projections(args, projections), m_values),
+                   "sample": sample,
                    "parallelism": "host CPU, rank 0 only"},
         "impl": "reference",
         "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads, "kind": "port",
@@ -1107,7 +1154,7 @@ def reference_gpu_arm(args, rank: int, world: int) -> None:
         return
     from kernels import build_grouped_workspace, check_device_errors, launch_grouped
 
-    m_values = [int(v) for v in args.m_values.split(",")]
+    m_values = m_values_of(args)
     parallel = [p for p in ("EP", "TP") if p in args.parallel.split(",")]
     counts = {"EP": EXPERTS // PARALLEL, "TP": EXPERTS}
     providers = args.ref_providers.split(",")
@@ -1193,7 +1240,7 @@ def reference_gpu_arm(args, rank: int, world: int) -> None:
             "impl": "reference-gpu", "metric": METRIC, "unit": "TFLOP/s", "n_gpus": 1, "dtype": "bf16",
             "projection": PROJECTION_NAME[projection],
             "data": "synthetic (the reference's seeded build_grouped_workspace draw, N(0,1)*0.1)",
-            "config": {"workload": WORKLOADS[projection],
+            "config": {"workload": workload_line(projection, m_values),
                        "timing": "hot; median of 10 CUDA-event-timed launches per shape after the first call "
                                  "(the reference's autotune runs in that first call)"},
             "providers": {"native": "this package (C ABI, native tile policy)",
@@ -1262,16 +1309,93 @@ def grouped_mm_side_by_side(steps: dict, device) -> dict:
     return out
 
 
+SWEEP_SIZES = (127, 1000, 4095, 8191)
+
+
+def masked_sweep_bench(args) -> None:
+    """--masked-sweep: BASELINE configs[4]'s masked single GEMM (the
+    reference's launch_matmul, kernels/matmul.py:332-392) over every
+    {127, 1000, 4095, 8191}^3 shape in fp32, with TF32 inputs and with full
+    fp32 products ("ieee": the 3xTF32 split with promoted accumulation on the
+    tensor cores), each timed alternately with torch.mm (cuBLAS) at the same
+    precision.  Rank 0 / cuda:0 only; one JSON line."""
+    import itertools
+
+    import torch
+
+    from kernels import check_device_errors, launch_matmul
+    from kernels.matmul import last_launch_info
+
+    torch.cuda.set_device(0)
+    rows = []
+    totals = {"tf32": [0.0, 0.0, 0.0], "ieee": [0.0, 0.0, 0.0]}  # flops, native ms, torch ms
+    sampler = ClockSampler(0)
+    sampler.start()
+    wall_begin = time.time()
+    for m, k, n in itertools.product(SWEEP_SIZES, SWEEP_SIZES, SWEEP_SIZES):
+        gen = torch.Generator(device="cuda").manual_seed(m * 7 + k * 3 + n)
+        a = torch.randn((m, k), device="cuda", generator=gen)
+        b = torch.randn((k, n), device="cuda", generator=gen) / math.sqrt(k)
+        c = torch.empty((m, n), device="cuda")
+        c_ref = torch.empty((m, n), device="cuda")
+        row = {"m": m, "k": k, "n": n}
+        for precision in ("tf32", "ieee"):
+            def native():
+                launch_matmul(a, b, c, input_precision=precision)
+
+            def reference():
+                torch.backends.cuda.matmul.allow_tf32 = precision == "tf32"
+                torch.mm(a, b, out=c_ref)
+
+            native_ms, torch_ms = paired_ms(native, reference, reps=10)
+            info = last_launch_info()
+            flops = 2 * m * n * k
+            diff = float((c.double() - c_ref.double()).norm() / c_ref.double().norm().clamp_min(1e-300))
+            row[precision] = {"ms": round(native_ms, 4), "tflops": round(flops / native_ms / 1e9, 1),
+                              "torch_mm_ms": round(torch_ms, 4), "vs_torch_mm": round(torch_ms / native_ms, 3),
+                              "path": info["path"] + ("+3xtf32" if info.get("split_3xtf32") else ""),
+                              "rel_diff_vs_torch_mm": float(f"{diff:.2e}")}
+            totals[precision][0] += flops
+            totals[precision][1] += native_ms
+            totals[precision][2] += torch_ms
+        torch.backends.cuda.matmul.allow_tf32 = False
+        rows.append(row)
+        del a, b, c, c_ref
+        torch.cuda.empty_cache()
+    sampler.mark(wall_begin, time.time())
+    clocks = sampler.stop()
+    check_device_errors(0)
+    summary = {p: {"tflops": round(f / t / 1e9, 1), "sweep_ms": round(t, 3), "torch_mm_tflops": round(f / r / 1e9, 1),
+                   "vs_torch_mm": round(r / t, 3),
+                   "native_wins": sum(1 for row in rows if row[p]["vs_torch_mm"] > 1.0)}
+               for p, (f, t, r) in totals.items()}
+    print(json.dumps({
+        "metric": "masked single GEMM TFLOP/s over the {127,1000,4095,8191}^3 sweep, fp32", "unit": "TFLOP/s",
+        "value": summary["ieee"]["tflops"], "value_precision": "ieee (full fp32 products)", "n_gpus": 1,
+        "higher_is_better": True, "dtype": "fp32", "data": "synthetic (A ~ N(0,1), B ~ N(0, 1/sqrt(K)), seeded)",
+        "config": {"workload": "BASELINE configs[4]: launch_matmul over every M, K, N in {127,1000,4095,8191}, "
+                               "fp32 with input_precision tf32 and ieee",
+                   "timing": "each shape alternately with torch.mm at the same precision, median of 10 calls each, "
+                             "sweep time = sum of the medians"},
+        "summary": summary, "shapes": len(rows), "per_shape": rows, "clocks": clocks,
+    }), flush=True)
+
+
 def main(argv=None) -> int:
     args = parse_args(argv)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
+    set_model(args.model, args.parallel_size)
     rank, world, local_rank = dist_env()
     if args.impl == "reference":
         reference_arm(args, rank, world)
         return 0
     if args.impl == "reference-gpu":
         reference_gpu_arm(args, rank, world)
+        return 0
+    if args.masked_sweep:
+        if rank == 0:
+            masked_sweep_bench(args)
         return 0
 
     import torch
@@ -1289,12 +1413,14 @@ def main(argv=None) -> int:
         os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+    if world > PARALLEL:
+        raise SystemExit(f"{world} ranks for a P = {PARALLEL} layout: use --parallel-size >= --gpus")
     if args.moe_layer:
         moe_layer_bench(args, rank, world, local_rank, device)
         if world > 1:
             dist.destroy_process_group()
         return 0
-    m_values = [int(v) for v in args.m_values.split(",")]
+    m_values = m_values_of(args)
     peaks, peak_source = load_peaks()
 
     from kernels import check_device_errors
@@ -1533,8 +1659,9 @@ def main(argv=None) -> int:
             "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(max_ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "e4m3" if args.fp8 else "bf16", "data": "synthetic",
-            "config": {"workload": "; ".join([workload_text(projections, cold)] + modes),
-                       "parallelism": f"GPU r runs rank r of P=8 (EP and TP), {world} rank(s)",
+            "config": {"workload": "; ".join([workload_text(projections, cold, m_values)] + modes),
+                       "model": MODEL, "parallel_size": PARALLEL,
+                       "parallelism": f"GPU r runs rank r of P={PARALLEL} (EP and TP), {world} rank(s)",
                        "cache": ("inputs larger than L2 (0.94-1.88 GB of weights per launch group), no flush"
                                  + ("; rotating-cold: " + ", ".join(PROJECTION_NAME[p] for p in cold)
                                     + " alternate two resident workspace sets step by step" if cold else "")),

@@ -170,3 +170,29 @@ def test_default_step_is_w13_hot_and_w2_rotating_cold():
     assert bench.selected_projections(only_w13) == ("W1",)
     with pytest.raises(SystemExit):
         bench.selected_projections(bench.parse_args(["--fp8", "--projection", "W2"]))
+
+
+@pytest.mark.parametrize("model,parallel,m,ep,tp", [
+    # Mixtral-8x7B (E=8, H=4096, F=14336), T=4096 top-2 -> M_e = 1024; EP P=8 is one expert per rank
+    ("mixtral-8x7b", 8, 1024, ("W1", 1, (1024, 4096, 28672)), ("W1", 8, (1024, 4096, 3584))),
+    ("mixtral-8x7b", 2, 1024, ("W2", 4, (1024, 14336, 4096)), ("W2", 8, (1024, 7168, 4096))),
+    # Qwen3-235B-A22B (E=128, H=4096, F=1536), P=8: T=256 -> M_e = 16
+    ("qwen3-235b-a22b", 8, 16, ("W1", 16, (16, 4096, 3072)), ("W1", 128, (16, 4096, 384))),
+    ("qwen3-235b-a22b", 8, 1024, ("W2", 16, (1024, 1536, 4096)), ("W2", 128, (1024, 192, 4096))),
+])
+def test_model_table_gives_the_reference_rank_shapes(model, parallel, m, ep, tp):
+    """--model / --parallel-size switch the
+    step to the reference's rank shapes for that model (utils/metrics.py:40-72)."""
+    bench = _bench()
+    try:
+        bench.set_model(model, parallel)
+        assert m in bench.M_VALUES
+        for par, (projection, count, shape) in (("EP", ep), ("TP", tp)):
+            (_, _, got, experts), = [s for s in bench.step_shapes([m], projection) if s[0] == par]
+            assert (got, experts) == (shape, count)
+        assert bench.MODELS[model]["label"] in bench.workload_line("W1")
+    finally:
+        bench.set_model("deepseek-v3", 8)
+    with pytest.raises(SystemExit):
+        bench.set_model("mixtral-8x7b", 16)  # 16 ranks cannot split 8 experts
+    bench.set_model("deepseek-v3", 8)
