@@ -1407,12 +1407,29 @@ def main(argv=None) -> int:
         from datetime import timedelta
 
         # NCCL's communicator lines (rank, nRanks, transport) on stderr, so a
-        # run's log shows how many ranks the verification gather spans;
-        # stdout keeps only the JSON line.
+        # run's log shows how many ranks the verification gather spans.  NCCL
+        # logs through C stdio to the process's stdout, so file descriptor 1
+        # points at stderr while the communicator is created (eagerly, with
+        # device_id) and is restored before anything else is printed: stdout
+        # keeps only the JSON line.
         os.environ.setdefault("NCCL_DEBUG", "INFO")
         os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+        sys.stdout.flush()
+        saved_stdout = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=device)
+            dist.barrier()
+        finally:
+            sys.stdout.flush()
+            try:
+                import ctypes
+
+                ctypes.CDLL(None).fflush(None)  # C stdio buffers (NCCL's log lines) go out on stderr too
+            except (OSError, AttributeError):
+                pass
+            os.dup2(saved_stdout, 1)
+            os.close(saved_stdout)
     if world > PARALLEL:
         raise SystemExit(f"{world} ranks for a P = {PARALLEL} layout: use --parallel-size >= --gpus")
     if args.moe_layer:
@@ -1553,16 +1570,39 @@ def main(argv=None) -> int:
     e2e_steps = max(1, args.e2e_steps)
     act_lists = {(proj, m): (a if isinstance(a, list) else [a])
                  for proj in projections for m, a in first[proj].activations.items()}
+    outs = {(proj, m): c for proj in projections for m, c in first[proj].outputs.items()}
+    h2d = sum(t.numel() * t.element_size() for ts in act_lists.values() for t in ts)
+    d2h = sum(t.numel() * t.element_size() for c in outs.values() for t in c)
+    # Every result comes back into one pinned buffer the size of the largest
+    # output (the copies run one after another on the copy stream, and each
+    # overwrites the previous result, as a consumer that reads each result
+    # before the next arrives would see): the ranks of one box share its host
+    # memory (196 GB on the B200 boxes here), and separate buffers for every
+    # output would pin ~17.5 GB per rank.
+    largest = max(t.numel() * t.element_size() for c in outs.values() for t in c)
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+    pinned_need = (h2d + largest) * local_world
+    try:
+        import psutil
+
+        host_available = psutil.virtual_memory().available
+    except ImportError:
+        host_available = None
+    e2e_skip = None
+    if host_available is not None and pinned_need > 0.75 * host_available:
+        e2e_skip = (f"{pinned_need / 1e9:.1f} GB of pinned host buffers for {local_world} rank(s) exceed 75% of the "
+                    f"{host_available / 1e9:.1f} GB of host memory available")
+        act_lists = {}
     host_a = {key: [torch.empty(t.shape, dtype=t.dtype, pin_memory=True).copy_(t) for t in ts]
               for key, ts in act_lists.items()}
-    outs = {(proj, m): c for proj in projections for m, c in first[proj].outputs.items()}
-    host_c = {key: tuple(torch.empty(t.shape, dtype=t.dtype, pin_memory=True) for t in c) for key, c in outs.items()}
-    h2d = sum(t.numel() * t.element_size() for ts in host_a.values() for t in ts)
-    d2h = sum(t.numel() * t.element_size() for pair in host_c.values() for t in pair)
+    result_buf = torch.empty(largest if e2e_skip is None else 0, dtype=torch.uint8, pin_memory=True)
+    host_c = {key: tuple(result_buf[:t.numel() * t.element_size()].view(t.dtype).view(t.shape) for t in c)
+              for key, c in outs.items()} if e2e_skip is None else {}
     by_key = {}
     for proj in projections:
         for par, m, ws in first[proj].workspaces:
-            by_key.setdefault((proj, m), []).append(ws)
+            if e2e_skip is None:
+                by_key.setdefault((proj, m), []).append(ws)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize(device)
@@ -1598,7 +1638,7 @@ def main(argv=None) -> int:
     if world > 1:
         dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
     e2e_ms = float(e2e_t.item())
-    del host_a, host_c
+    del host_a, host_c, result_buf
     check_device_errors(local_rank)
 
     progress("verification")
@@ -1681,8 +1721,9 @@ def main(argv=None) -> int:
             "e2e": {"value": round(rank_flops * world * e2e_steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "note": "launch_grouped per workspace with activations copied in from pinned host memory and "
-                            "outputs copied back every step (on a second stream, beside the next copy in); "
-                            "weights resident"},
+                            "every output copied back every step (on a second stream, beside the next copy in, "
+                            "into one reused pinned result buffer); weights resident"}
+            if e2e_skip is None else {"value": None, "skipped": e2e_skip},
             "gpu_launches": int(launches.item()),
             "clocks": clocks,
             "verification": verification,
