@@ -1412,7 +1412,8 @@ def main(argv=None) -> int:
         # points at stderr while the communicator is created (eagerly, with
         # device_id) and is restored before anything else is printed: stdout
         # keeps only the JSON line.
-        os.environ.setdefault("NCCL_DEBUG", "INFO")
+        if os.environ.get("NCCL_DEBUG", "").upper() not in ("INFO", "TRACE"):
+            os.environ["NCCL_DEBUG"] = "INFO"  # an image default such as VERSION or WARN hides the INIT lines
         os.environ.setdefault("NCCL_DEBUG_SUBSYS", "INIT")
         sys.stdout.flush()
         saved_stdout = os.dup(1)
