@@ -1298,8 +1298,9 @@ def grouped_mm_side_by_side(steps: dict, device) -> dict:
 
             native_ms, gm_ms = paired_ms(lambda: launch(ws), run_grouped_mm)
             m_rows = ws.shapes[0][0]
-            ours = torch.cat([ws.c[i] for i in range(2)]).float()
-            theirs = holder["c"][:2 * m_rows].float()
+            compared = min(2, ws.problem_count)
+            ours = torch.cat([ws.c[i] for i in range(compared)]).float()
+            theirs = holder["c"][:compared * m_rows].float()
             diff = float((ours - theirs).norm() / theirs.norm().clamp_min(1e-30))
             holder.clear()
             out[(proj, par, m)] = {"alone_ms": round(native_ms, 4), "grouped_mm_ms": round(gm_ms, 4),

@@ -224,8 +224,12 @@ def _check_precision(input_precision: str) -> str:
 
 # Single GEMMs at least this large repack operands the TMA cannot address
 # (row pitch not a multiple of 16 bytes, unit-stride violations) so they run
-# on the tensor cores; smaller ones use the generic-stride kernel directly.
-REPACK_MIN_FLOPS = 1 << 28
+# on the tensor cores, and fp32 "ieee" ones take the 3xTF32 split; smaller
+# ones use the generic-stride kernel directly.  The generic kernel has one
+# 64 x 64 tile per CTA and no split of K, so a small output with a long K
+# leaves most SMs idle: 127 x 8191 x 127 (0.26 GFLOP) ran 1.17 ms there
+# against tens of microseconds for one tensor-core CTA after the repack.
+REPACK_MIN_FLOPS = 1 << 24
 
 
 def _tma_addressable(x) -> bool:
