@@ -1310,6 +1310,44 @@ def grouped_mm_side_by_side(steps: dict, device) -> dict:
     return out
 
 
+def paired_graph_ms(fn_a, fn_b, calls: int = 10, reps: int = 5) -> tuple[float, float]:
+    """Per-call device time of `fn_a` and `fn_b`, each captured `calls` times
+    into a CUDA graph and the two graphs replayed alternately `reps` times
+    (median replay / calls): the device time without host launch overhead,
+    the way the reference times its shape sweep (utils/benchmark.py
+    time_cuda, CUDA-graph replay)."""
+    import torch
+
+    for fn in (fn_a, fn_b):  # eager first calls: tile choice, one-time set-up
+        fn()
+    torch.cuda.synchronize()
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    graphs = []
+    with torch.cuda.stream(stream):
+        for fn in (fn_a, fn_b):
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for _ in range(calls):
+                    fn()
+            graphs.append(graph)
+        for graph in graphs:
+            graph.replay()
+        stream.synchronize()
+        times = ([], [])
+        for _ in range(reps):
+            for graph, out in zip(graphs, times):
+                start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                start.record(stream)
+                graph.replay()
+                end.record(stream)
+                out.append((start, end))
+        stream.synchronize()
+    result = tuple(statistics.median(s.elapsed_time(e) for s, e in out) / calls for out in times)
+    del graphs
+    return result
+
+
 SWEEP_SIZES = (127, 1000, 4095, 8191)
 
 
@@ -1348,7 +1386,7 @@ def masked_sweep_bench(args) -> None:
                 torch.backends.cuda.matmul.allow_tf32 = precision == "tf32"
                 torch.mm(a, b, out=c_ref)
 
-            native_ms, torch_ms = paired_ms(native, reference, reps=10)
+            native_ms, torch_ms = paired_graph_ms(native, reference)
             info = last_launch_info()
             flops = 2 * m * n * k
             diff = float((c.double() - c_ref.double()).norm() / c_ref.double().norm().clamp_min(1e-300))
@@ -1376,8 +1414,9 @@ def masked_sweep_bench(args) -> None:
         "higher_is_better": True, "dtype": "fp32", "data": "synthetic (A ~ N(0,1), B ~ N(0, 1/sqrt(K)), seeded)",
         "config": {"workload": "BASELINE configs[4]: launch_matmul over every M, K, N in {127,1000,4095,8191}, "
                                "fp32 with input_precision tf32 and ieee",
-                   "timing": "each shape alternately with torch.mm at the same precision, median of 10 calls each, "
-                             "sweep time = sum of the medians"},
+                   "timing": "per shape: 10 calls of each side captured in a CUDA graph (as the reference's "
+                             "time_cuda does), the two graphs replayed alternately 5 times, median replay / 10; "
+                             "sweep time = sum over shapes"},
         "summary": summary, "shapes": len(rows), "per_shape": rows, "clocks": clocks,
     }), flush=True)
 
