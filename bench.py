@@ -1648,30 +1648,45 @@ def main(argv=None) -> int:
         dist.barrier()
     torch.cuda.synchronize(device)
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # Outputs go back on a second stream, so a launch group's device->host
-    # copy runs beside the next group's host->device copy (PCIe is full
-    # duplex); an output buffer is launched into again only after its copy
-    # has finished.
-    d2h_stream = torch.cuda.Stream(device)
+    # Three streams, so both PCIe directions stay busy (the link is full
+    # duplex): inputs go host -> device on their own stream and run ahead of
+    # the launches, which wait only for their own group's inputs; outputs come
+    # back on a third stream as each group finishes.  A group's device inputs
+    # are overwritten only after the previous step's launches read them, and
+    # its device outputs only after the previous step's copy read them.  W13
+    # and W2 groups alternate, so the big W13 inputs travel while W2 outputs
+    # come back.
+    h2d_stream, d2h_stream = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    order = sorted(by_key, key=lambda key: (key[1], key[0]))
+    computed: dict[tuple[str, int], object] = {}
     copied: dict[tuple[str, int], object] = {}
     with torch.cuda.stream(stream):
         e_start.record(stream)
+        h2d_stream.wait_event(e_start)
+        d2h_stream.wait_event(e_start)
         for _ in range(e2e_steps):
-            for key in by_key:
-                for dev_t, host_t in zip(act_lists[key], host_a[key]):
-                    dev_t.copy_(host_t, non_blocking=True)
+            for key in order:
+                in_ready = torch.cuda.Event()
+                with torch.cuda.stream(h2d_stream):
+                    if key in computed:
+                        h2d_stream.wait_event(computed[key])
+                    for dev_t, host_t in zip(act_lists[key], host_a[key]):
+                        dev_t.copy_(host_t, non_blocking=True)
+                    in_ready.record(h2d_stream)
+                stream.wait_event(in_ready)
                 if key in copied:
                     stream.wait_event(copied[key])
                 for ws in by_key[key]:
                     launch(ws)
-                ready = torch.cuda.Event()
-                ready.record(stream)
-                d2h_stream.wait_event(ready)
+                computed[key] = torch.cuda.Event()
+                computed[key].record(stream)
                 with torch.cuda.stream(d2h_stream):
+                    d2h_stream.wait_event(computed[key])
                     for host_t, dev_t in zip(host_c[key], outs[key]):
                         host_t.copy_(dev_t, non_blocking=True)
                     copied[key] = torch.cuda.Event()
                     copied[key].record(d2h_stream)
+        stream.wait_stream(h2d_stream)
         stream.wait_stream(d2h_stream)
         e_end.record(stream)
     torch.cuda.synchronize(device)
@@ -1762,8 +1777,9 @@ def main(argv=None) -> int:
             "e2e": {"value": round(rank_flops * world * e2e_steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "note": "launch_grouped per workspace with activations copied in from pinned host memory and "
-                            "every output copied back every step (on a second stream, beside the next copy in, "
-                            "into one reused pinned result buffer); weights resident"}
+                            "every output copied back every step (inputs, launches and outputs on three streams, "
+                            "so both PCIe directions overlap; outputs into one reused pinned result buffer); "
+                            "weights resident"}
             if e2e_skip is None else {"value": None, "skipped": e2e_skip},
             "gpu_launches": int(launches.item()),
             "clocks": clocks,
