@@ -78,6 +78,10 @@ struct Tc2Cfg {
   // TMEM columns an epilogue warp reads: buf * kAccCols + h * 256 + [0, 256).
   static_assert((kAccBufs - 1) * kAccCols + kTileN <= kTmemCols, "accumulator columns inside the allocation");
   static_assert(kStages >= 3, "operand ring depth");
+  // Descriptor offsets are whole 16-byte units, and every shared-memory
+  // address fits the descriptor's 14-bit (address >> 4) field.
+  static_assert(kStageBytes % 16 == 0 && kActBytes % 16 == 0 && kHalfWgtBytes % 16 == 0, "16-byte offsets");
+  static_assert(kSmemBytes < (1 << 18), "addresses fit the descriptor field");
   static_assert(kSmemBytes <= 232448, "shared memory");
 };
 
@@ -262,6 +266,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
       bool ok = true;
       int64_t item = -1;
       int half = -1;
+      // Descriptors of stage 0's operands.  A stage, k-step or weight half is
+      // an offset of the 14-bit start-address field (address >> 4); every
+      // shared-memory address keeps that field below 2^14, so the 64-bit add
+      // never carries out of it, and an MMA costs the issuer one add per
+      // operand instead of assembling both descriptors.
+      const uint64_t act_desc0 = smem_desc(smem_u32(ring), 16, 1024, kLayoutSw128);
+      const uint64_t wgt_desc0 = smem_desc(smem_u32(ring) + Cfg::kActBytes, Cfg::kBoxBytes, 1024, kLayoutSw128);
       for (int64_t t = 0; ok && next_item<NH>(walk, p, cluster, clusters, item, t, half);) {
         const Problem& q = walk.prob;
         if (!tile_legal<T>(p, q) || q.k <= 0) continue;
@@ -277,12 +288,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * Cfg::kAccCols);
         // MMAs of one 256-column half h over the four k-steps of stage s.
         auto issue_half = [&](int s, int h, bool first_kb) {
-          const uint32_t a_base = smem_u32(ring + s * Cfg::kStageBytes);
-          const uint32_t w_base = a_base + Cfg::kActBytes + h * Cfg::kHalfWgtBytes;
+          const uint64_t stage = static_cast<uint64_t>(s * (Cfg::kStageBytes >> 4));
 #pragma unroll
           for (int ks = 0; ks < Cfg::kKSteps; ++ks) {
-            const uint64_t act_desc = smem_desc(a_base + ks * 32, 16, 1024, kLayoutSw128);
-            const uint64_t wgt_desc = smem_desc(w_base + ks * Cfg::kKStep * 128, Cfg::kBoxBytes, 1024, kLayoutSw128);
+            const uint64_t act_desc = act_desc0 + stage + ((ks * 32) >> 4);
+            const uint64_t wgt_desc = wgt_desc0 + stage + ((h * Cfg::kHalfWgtBytes + ks * Cfg::kKStep * 128) >> 4);
             mma_f16_pair(d_tmem + h * 256, act_desc, wgt_desc, Cfg::kIdesc, (!first_kb || ks > 0) ? 1u : 0u);
           }
         };
@@ -351,15 +361,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kTcThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(ring + s * Cfg::kStageBytes);
-          const uint32_t w_base = a_base + Cfg::kActBytes;
+          const uint64_t stage = static_cast<uint64_t>(s * (Cfg::kStageBytes >> 4));
 #pragma unroll
           for (int ks = 0; ks < Cfg::kKSteps; ++ks) {
-            const uint64_t act_desc = smem_desc(a_base + ks * 32, 16, 1024, kLayoutSw128);
+            const uint64_t act_desc = act_desc0 + stage + ((ks * 32) >> 4);
 #pragma unroll
             for (int h = 0; h < NH; ++h) {
-              const uint64_t wgt_desc = smem_desc(w_base + h * Cfg::kHalfWgtBytes + ks * Cfg::kKStep * 128,
-                                                  Cfg::kBoxBytes, 1024, kLayoutSw128);
+              const uint64_t wgt_desc = wgt_desc0 + stage + ((h * Cfg::kHalfWgtBytes + ks * Cfg::kKStep * 128) >> 4);
               mma_f16_pair(d_tmem + h * 256, act_desc, wgt_desc, Cfg::kIdesc, (kb > 0 || ks > 0) ? 1u : 0u);
             }
           }
