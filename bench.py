@@ -1476,6 +1476,7 @@ def main(argv=None) -> int:
     if args.moe_layer:
         moe_layer_bench(args, rank, world, local_rank, device)
         if world > 1:
+            stdout_to_stderr_for_good()
             dist.destroy_process_group()
         return 0
     m_values = m_values_of(args)
@@ -1789,10 +1790,27 @@ def main(argv=None) -> int:
         }
         print(json.dumps(line), flush=True)
     if world > 1:
+        stdout_to_stderr_for_good()
         dist.barrier()
         dist.destroy_process_group()
     del graphs, warm_graph, events, warm_events
     return 0
+
+
+def stdout_to_stderr_for_good() -> None:
+    """Points file descriptor 1 at stderr for the rest of the process.
+
+    NCCL logs through C stdio to stdout, also when a communicator is torn down
+    and when its plugins close at exit; called once the JSON line is out, this
+    keeps that line the only thing the run prints on stdout."""
+    sys.stdout.flush()
+    try:
+        import ctypes
+
+        ctypes.CDLL(None).fflush(None)
+    except (OSError, AttributeError):
+        pass
+    os.dup2(2, 1)
 
 
 def traffic_from_profiles(dominant: dict):
