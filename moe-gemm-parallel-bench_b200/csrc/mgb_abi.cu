@@ -658,11 +658,13 @@ int grouped_gemm_fp8_launch(const int64_t* a_ptrs, const int64_t* b_ptrs, const 
     return MGB_OK;
   }
   const int bm = config ? config->block_m : 64;
+  const int bn = config ? config->block_n : 128;
   const TcVariant v = bm <= 16 ? TcVariant{true, 16, 256}
                       : bm <= 32 ? TcVariant{true, 32, 256}
                       : bm <= 64 ? TcVariant{true, 64, 256}
                       : bm < 256 ? TcVariant{false, 128, 128}
-                                 : TcVariant{false, 256, 128, true};
+                      : bn >= 256 ? TcVariant{false, 256, 256, true}
+                                  : TcVariant{false, 256, 128, true};
   TcVariantInfo vi;
   if (!mgb::fp8_variant_info(v, &vi)) return MGB_ERR_UNSUPPORTED;
 

@@ -8,7 +8,8 @@
 namespace mgb {
 
 // swap-AB 16 / 32 / 64 tokens x 256 weight rows, and 128 x 128 row tiles;
-// the CTA-pair 256 x 128 tile (fp8_pair_kernel) is handled beside them.
+// the CTA-pair 256 x 128 and 256 x 256 tiles (fp8_pair_kernel) are handled
+// beside them.
 #define MGB_FOR_EACH_FP8_VARIANT(X) \
   X(true, 16, 256)                  \
   X(true, 32, 256)                  \
@@ -33,39 +34,72 @@ static int launch_fp8_variant(const CUtensorMap& act, const CUtensorMap& wgt, co
   return static_cast<int>(cudaGetLastError());
 }
 
-// Clusters of two the device keeps resident at once for the CTA-pair kernel
-// (queried once per device; SMs / 2 when the query is unavailable).
+// Clusters of two the device keeps resident at once for a CTA-pair kernel
+// (queried once per device; SMs / 2 when the query is unavailable).  For the
+// 256-row tile, 0 (not launchable) unless the compiled kernel's registers per
+// thread cover its setmaxnreg split: a split above the block's launch
+// registers would leave the promotion warps waiting for registers forever.
+template <int TN>
 static int fp8_pair_max_clusters() {
+  using Cfg = Fp8PairCfgT<TN>;
   static int cached[128] = {};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return 0;
   if (cached[dev] == 0) {
-    if (cudaFuncSetAttribute(fp8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Fp8PairCfg::kSmemBytes) != cudaSuccess) {
+    if (cudaFuncSetAttribute(fp8_pair_kernel<TN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::kSmemBytes) != cudaSuccess) {
       return 0;
+    }
+    if constexpr (Cfg::kRegSplit) {
+      cudaFuncAttributes attr = {};
+      if (cudaFuncGetAttributes(&attr, fp8_pair_kernel<TN>) != cudaSuccess) return 0;
+      const long long launched = static_cast<long long>(attr.numRegs) * Cfg::kThreads;
+      const long long split = 128ll * Cfg::kRegsLow + 32ll * Cfg::kEpiWarps * Cfg::kRegsHigh;
+      if (launched < split) {
+        cached[dev] = -1;
+        return 0;
+      }
     }
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(sms & ~1), 1, 1);
-    cfg.blockDim = dim3(Fp8PairCfg::kThreads, 1, 1);
-    cfg.dynamicSmemBytes = Fp8PairCfg::kSmemBytes;
+    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
     int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, fp8_pair_kernel, &cfg) != cudaSuccess || clusters <= 0) {
+    if (cudaOccupancyMaxActiveClusters(&clusters, fp8_pair_kernel<TN>, &cfg) != cudaSuccess || clusters <= 0) {
       cudaGetLastError();
       clusters = sms / 2;
     }
     cached[dev] = clusters;
   }
-  return cached[dev];
+  return cached[dev] > 0 ? cached[dev] : 0;
+}
+
+template <int TN>
+static bool fp8_pair_info(TcVariantInfo* info) {
+  using Cfg = Fp8PairCfgT<TN>;
+  const int clusters = fp8_pair_max_clusters<TN>();
+  if (clusters <= 0) return false;
+  *info = TcVariantInfo{Cfg::kBK, Cfg::kStages, Cfg::kSmemBytes, clusters, Cfg::kHalfM, Cfg::kHalfN};
+  return true;
+}
+
+template <int TN>
+static int fp8_pair_launch(const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
+                           const GroupedParams& p, int grid, cudaStream_t stream) {
+  using Cfg = Fp8PairCfgT<TN>;
+  if (grid % 2 != 0 || fp8_pair_max_clusters<TN>() <= 0) return static_cast<int>(cudaErrorInvalidValue);
+  fp8_pair_kernel<TN><<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(act, wgt, out, p);
+  return static_cast<int>(cudaGetLastError());
 }
 
 bool fp8_variant_info(const TcVariant& v, TcVariantInfo* info) {
   if (v.pair) {
-    if (v.tm != Fp8PairCfg::kTileM || v.tn != Fp8PairCfg::kTileN) return false;
-    *info = TcVariantInfo{Fp8PairCfg::kBK, Fp8PairCfg::kStages, Fp8PairCfg::kSmemBytes, fp8_pair_max_clusters(),
-                          Fp8PairCfg::kHalfM, Fp8PairCfg::kHalfN};
-    return true;
+    if (v.tm != 256) return false;
+    if (v.tn == 128) return fp8_pair_info<128>(info);
+    if (v.tn == 256) return fp8_pair_info<256>(info);
+    return false;
   }
 #define MGB_FP8_INFO(S, M, N)                                                         \
   if (v.swap == S && v.tm == M && v.tn == N) {                                        \
@@ -81,21 +115,9 @@ bool fp8_variant_info(const TcVariant& v, TcVariantInfo* info) {
 int fp8_launch(const TcVariant& v, const CUtensorMap& act, const CUtensorMap& wgt, const CUtensorMap& out,
                const GroupedParams& p, int grid, cudaStream_t stream) {
   if (v.pair) {
-    if (v.tm != Fp8PairCfg::kTileM || v.tn != Fp8PairCfg::kTileN || grid % 2 != 0) {
-      return static_cast<int>(cudaErrorInvalidValue);
-    }
-    static bool configured[128] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 128) return static_cast<int>(cudaErrorInvalidDevice);
-    if (!configured[dev]) {
-      const cudaError_t e = cudaFuncSetAttribute(fp8_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                                 Fp8PairCfg::kSmemBytes);
-      if (e != cudaSuccess) return static_cast<int>(e);
-      configured[dev] = true;
-    }
-    fp8_pair_kernel<<<grid, Fp8PairCfg::kThreads, Fp8PairCfg::kSmemBytes, stream>>>(act, wgt, out, p);
-    return static_cast<int>(cudaGetLastError());
+    if (v.tm == 256 && v.tn == 128) return fp8_pair_launch<128>(act, wgt, out, p, grid, stream);
+    if (v.tm == 256 && v.tn == 256) return fp8_pair_launch<256>(act, wgt, out, p, grid, stream);
+    return static_cast<int>(cudaErrorInvalidValue);
   }
 #define MGB_FP8_LAUNCH(S, M, N) \
   if (v.swap == S && v.tm == M && v.tn == N) return launch_fp8_variant<S, M, N>(act, wgt, out, p, grid, stream);

@@ -526,35 +526,55 @@ __global__ void __launch_bounds__(Fp8Cfg<SWAP, TM, TN>::kThreads, 1)
 //   empty[s]        in each CTA: the MMA commit multicasts to both
 //   part_full[b]    in each CTA: the MMA commit multicasts to both
 //   part_empty[b]   in CTA 0 only: the 16 promotion warps of the pair arrive
-struct Fp8PairCfg {
+template <int TN>
+struct Fp8PairCfgT {
+  static_assert(TN == 128 || TN == 256, "one or two 128-row weight scale blocks per cluster tile");
   static constexpr int kBK = kFp8Block;
-  static constexpr int kTileM = 256;  // tokens per cluster tile
-  static constexpr int kTileN = 128;  // weight rows per cluster tile (one scale block)
-  static constexpr int kHalfM = 128;  // token rows per CTA
-  static constexpr int kHalfN = 64;   // weight rows per CTA
+  static constexpr int kTileM = 256;      // tokens per cluster tile
+  static constexpr int kTileN = TN;       // weight rows per cluster tile
+  static constexpr int kHalfM = 128;      // token rows per CTA
+  static constexpr int kHalfN = TN / 2;   // weight rows per CTA
   static constexpr int kActBytes = kHalfM * 128;
   static constexpr int kWgtBytes = kHalfN * 128;
   static constexpr int kStageBytes = kActBytes + kWgtBytes;
   static constexpr int kEpiWarps = 8;
-  static constexpr int kThreads = 64 + 32 * kEpiWarps;
-  static constexpr int kWarpCols = kTileN / 2;
+  // Warps before the promotion warps.  The 256-row tile keeps whole warpgroups
+  // per role (producer, MMA issuer and two idle warps in warpgroup 0, the
+  // promotion warps in warpgroups 1 and 2), so each warpgroup runs one
+  // setmaxnreg: warpgroup 0 gives registers up, the promotion warpgroups take
+  // them for their 128 accumulators per lane.
+  static constexpr int kFirstEpiWarp = TN == 256 ? 4 : 2;
+  static constexpr int kThreads = 32 * (kFirstEpiWarp + kEpiWarps);
+  static constexpr bool kRegSplit = TN == 256;
+  static constexpr int kRegsLow = 88;    // warpgroup 0 after setmaxnreg.dec
+  static constexpr int kRegsHigh = 208;  // each promotion warpgroup after setmaxnreg.inc
+  static constexpr int kWarpCols = kTileN / 2;  // columns one promotion warp owns (one scale block at TN = 256)
   static constexpr int kBlocksPerWarp = 1;  // as in Fp8Cfg: the freed shared memory deepens the ring
   static constexpr int kEpiBytes = kEpiWarps * kBlocksPerWarp * kEpiWarpBytes;
   static constexpr int kStagesRaw = (kTcSmemBudget - kEpiBytes) / kStageBytes;
   static constexpr int kStages = kStagesRaw > 12 ? 12 : kStagesRaw;
-  static constexpr int kPartCols = kTileN;  // TMEM columns of one partial (this CTA's 128 rows)
-  static constexpr int kPartBufs = 4;       // partials in flight (see Fp8Cfg)
+  static constexpr int kPartCols = kTileN;             // TMEM columns of one partial (this CTA's 128 rows)
+  static constexpr int kPartBufs = TN == 256 ? 2 : 4;  // partials in flight (see Fp8Cfg); 512 TMEM columns
   static constexpr int kTmemCols = kPartBufs * kPartCols;
   static constexpr uint32_t kIdesc = instr_desc(0, 0, 0, kTileM, kTileN);  // E4M3 x E4M3, both K-major
   static constexpr int kSmemBytes = kStages * kStageBytes + kEpiBytes + 2048 + 1024;
   static_assert(kStages >= 3, "operand ring depth");
   static_assert(kSmemBytes <= 232448, "shared memory");
+  static_assert(kTmemCols <= 512, "partials fit in TMEM");
+  // The split hands out no more than the block was launched with: at most
+  // 168 registers a thread for 384 threads (the host also checks the
+  // compiled kernel's count before the first launch).
+  static_assert(!kRegSplit || (kFirstEpiWarp == 4 && 128 * kRegsLow + 32 * kEpiWarps * kRegsHigh <= kThreads * 168),
+                "register split within the launch's registers");
+  static_assert(kRegsLow % 8 == 0 && kRegsHigh % 8 == 0 && kRegsLow >= 24 && kRegsHigh <= 256, "setmaxnreg range");
 };
+using Fp8PairCfg = Fp8PairCfgT<128>;
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8PairCfg::kThreads, 1)
+template <int TN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8PairCfgT<TN>::kThreads, 1)
     fp8_pair_kernel(const __grid_constant__ CUtensorMap act_tmpl, const __grid_constant__ CUtensorMap wgt_tmpl,
                     const __grid_constant__ CUtensorMap out_tmpl, const GroupedParams p) {
-  using Cfg = Fp8PairCfg;
+  using Cfg = Fp8PairCfgT<TN>;
   constexpr int S = Cfg::kStages;
   constexpr int BK = Cfg::kBK;
 
@@ -604,7 +624,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8PairCfg::kThreads
   const uint32_t tmem_base = *tmem_slot;
   const long long budget = p.wait_budget;
 
-  if (warp == 0) {
+  if (warp < Cfg::kFirstEpiWarp) {
+   if constexpr (Cfg::kRegSplit) setmaxnreg_dec<Cfg::kRegsLow>();
+   if (warp == 0) {
     // ------------------------------------------------------------ producer
     const CUtensorMap* act_map = &act_tmpl;
     const CUtensorMap* wgt_map = &wgt_tmpl;
@@ -665,7 +687,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8PairCfg::kThreads
         }
       }
     }
-  } else if (warp == 1) {
+   } else if (warp == 1) {
     // ------------------------------------------- MMA issuer (even CTA only)
     if (lane == 0 && leader) {
       TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
@@ -711,12 +733,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8PairCfg::kThreads
       }
     }
     __syncwarp();
+   }
   } else {
     // ------------------------------------------- promotion and the stores
+    if constexpr (Cfg::kRegSplit) setmaxnreg_inc<Cfg::kRegsHigh>();
     constexpr int W = Cfg::kWarpCols;
-    const int quarter = warp & 3;
-    const int ew = warp - 2;
-    const int half = ew / 4;
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may read
+    const int ew = warp - Cfg::kFirstEpiWarp;
+    const int half = ew / 4;       // columns [W half, W half + W) of the tile
     TileWalk<Cfg::kTileM, Cfg::kTileN> walk;
     uint32_t pit = 0;
     uint8_t* my_blocks = epi_stage + ew * Cfg::kBlocksPerWarp * kEpiWarpBytes;
@@ -737,10 +761,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8PairCfg::kThreads
 #pragma unroll
       for (int i = 0; i < W; ++i) acc[i] = 0.0f;
       const int64_t row = m0 + quarter * 32 + lane;
-      const int64_t nblk = n0 / kFp8Block;
+      // This warp's columns lie in one scale block; on the last N tile of the
+      // 256-row tile they may all lie past N, where no weight scale exists
+      // (those columns are neither computed from real rows nor stored).
+      const int64_t nblk = (n0 + half * W) / kFp8Block;
+      const bool cols_in = n0 + half * W < q.n;
       auto fetch = [&](int64_t kb) -> float {
         const float s_a = row < q.m ? sa[row * kblocks + kb] : 0.0f;
-        return s_a * sb[nblk * kblocks + kb];
+        return cols_in ? s_a * sb[nblk * kblocks + kb] : 0.0f;
       };
       float ring[kScaleAhead];  // scales of the next K blocks in flight, as in fp8_grouped_kernel
 #pragma unroll
@@ -761,14 +789,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8PairCfg::kThreads
         tc_fence_after();
         const uint32_t taddr = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) +
                                static_cast<uint32_t>(pb * Cfg::kPartCols + half * W);
-        uint32_t r0[32], r1[32];
-        tmem_ld32(taddr, r0);
-        tmem_ld32(taddr + 32, r1);
-        tmem_ld_wait();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          acc[i] = fmaf(__uint_as_float(r0[i]), f, acc[i]);
-          acc[32 + i] = fmaf(__uint_as_float(r1[i]), f, acc[32 + i]);
+        for (int g = 0; g < W / 64; ++g) {  // 64 columns (two loads) in flight at a time
+          uint32_t r0[32], r1[32];
+          tmem_ld32(taddr + g * 64, r0);
+          tmem_ld32(taddr + g * 64 + 32, r1);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            acc[g * 64 + i] = fmaf(__uint_as_float(r0[i]), f, acc[g * 64 + i]);
+            acc[g * 64 + 32 + i] = fmaf(__uint_as_float(r1[i]), f, acc[g * 64 + 32 + i]);
+          }
         }
         tc_fence_before();
         __syncwarp();
@@ -778,9 +809,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Fp8PairCfg::kThreads
       }
       if (!ok) break;
       if (cmap != nullptr) {
-        store_acc_rows_tma<Cfg::kBlocksPerWarp, 0>(q, cmap, acc, static_cast<int32_t>(m0 + quarter * 32),
-                                                   static_cast<int32_t>(n0 + half * W), my_blocks, lane, chunk_seq,
-                                                   pol_out, p.error_word);
+        const int32_t row0 = static_cast<int32_t>(m0 + quarter * 32);
+        const int32_t x0 = static_cast<int32_t>(n0 + half * W);
+        store_acc_rows_tma<Cfg::kBlocksPerWarp, 0>(q, cmap, acc, row0, x0, my_blocks, lane, chunk_seq, pol_out,
+                                                   p.error_word);
+        if constexpr (W == 128) {
+          store_acc_rows_tma<Cfg::kBlocksPerWarp, 64>(q, cmap, acc, row0, x0 + 64, my_blocks, lane, chunk_seq,
+                                                      pol_out, p.error_word);
+        }
       }
     }
     if (lane == 0) bulk_wait_group_all();

@@ -37,18 +37,23 @@ FP8_TILE_SWAP_32 = KernelConfig(32, 256, 128, 4, 8, 4)
 FP8_TILE_SWAP_64 = KernelConfig(64, 256, 128, 8, 8, 4)
 FP8_TILE_ROWS_128 = KernelConfig(128, 128, 128, 8, 8, 4)
 FP8_TILE_PAIR_256 = KernelConfig(256, 128, 128, 8, 8, 4)  # CTA pair: 256 tokens x 128 weight rows
+FP8_TILE_PAIR_256x256 = KernelConfig(256, 256, 128, 8, 8, 4)  # CTA pair: 256 tokens x 256 weight rows
 
 
 def fp8_tile_for(max_m: int) -> KernelConfig:
     """Swap-AB tiles (weight rows as MMA M, exact-fit token count) while the
-    launch streams weights from HBM, 128 x 128 token tiles above 64 tokens."""
+    launch streams weights from HBM, 128 x 128 token tiles above 64 tokens,
+    and from 256 tokens the CTA-pair 256 x 256 tile, whose M = 256, N = 256
+    MMAs do four times the work of a 128 x 128 tile's per instruction."""
     if max_m <= 16:
         return FP8_TILE_SWAP_16
     if max_m <= 32:
         return FP8_TILE_SWAP_32
     if max_m <= 64:
         return FP8_TILE_SWAP_64
-    return FP8_TILE_ROWS_128
+    if max_m < 256:
+        return FP8_TILE_ROWS_128
+    return FP8_TILE_PAIR_256x256
 
 
 def _blocks(n: int) -> int:

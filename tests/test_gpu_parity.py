@@ -687,7 +687,7 @@ def test_fp8_block_scaled_every_tile_ragged_group():
     shapes = [(16, 256, 256), (40, 320, 200), (130, 128, 384), (1, 64, 136), (300, 512, 256)]
     ws = build_fp8_workspace(shapes, seed=13)
     assert not ws.homogeneous
-    for bm, bn in ((16, 256), (32, 256), (64, 256), (128, 128), (256, 128)):
+    for bm, bn in ((16, 256), (32, 256), (64, 256), (128, 128), (256, 128), (256, 256)):
         for c in ws.c:
             c.fill_(float("nan"))
         launch_grouped_fp8(ws, config=KernelConfig(bm, bn, 128, 4, 8, 4))
@@ -713,6 +713,26 @@ def test_fp8_block_scaled_deepseek_rank_shapes(m_e, k, n):
     torch.cuda.synchronize()
     check_device_errors()
     rng = np.random.default_rng(k)
+    rows = lambda m: torch.as_tensor(np.unique(np.concatenate([[0, m - 1], rng.integers(0, m, 12)])), device="cuda")
+    _fp8_check(ws, rows=rows)
+
+
+@pytest.mark.parametrize("m_e,k,n", [(512, 7168, 4096), (1024, 2048, 7168), (300, 1024, 384)])
+def test_fp8_pair_256_tile_rank_shapes(m_e, k, n):
+    """The CTA-pair 256 x 256 FP8 tile (KernelConfig(256, 256, ...)) on
+    DeepSeek-V3 W13 / W2 expert shapes, and on a group whose last weight tile
+    is half past N (N = 384) with a partial last token tile."""
+    torch = _torch()
+    from kernels import KernelConfig, build_fp8_workspace, check_device_errors, launch_grouped_fp8
+
+    ws = build_fp8_workspace([(m_e, k, n)] * 3, seed=m_e + n)
+    for c in ws.c:
+        c.fill_(float("nan"))
+    launch_grouped_fp8(ws, config=KernelConfig(256, 256, 128, 8, 8, 4))
+    torch.cuda.synchronize()
+    check_device_errors()
+    assert ws.launch_info["path"] == "tcgen05_tma_pair" and ws.launch_info["tile_n"] == 256, ws.launch_info
+    rng = np.random.default_rng(k + 1)
     rows = lambda m: torch.as_tensor(np.unique(np.concatenate([[0, m - 1], rng.integers(0, m, 12)])), device="cuda")
     _fp8_check(ws, rows=rows)
 
