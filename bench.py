@@ -1275,17 +1275,45 @@ def paired_ms(fn_a, fn_b, reps: int = 15) -> tuple[float, float]:
             statistics.median(s.elapsed_time(e) for s, e in pairs_b))
 
 
-def grouped_mm_side_by_side(steps: dict, device) -> dict:
+def alternating_ms(fns, reps: int = 15) -> float:
+    """Median CUDA-event time of one call when the calls in `fns` take turns
+    (f0, f1, f0, f1, ...), after three untimed rounds: a rotating-cold launch
+    timed alone, each call on the other resident workspace set."""
+    import torch
+
+    for _ in range(3):
+        for fn in fns:
+            fn()
+    torch.cuda.synchronize()
+    pairs = []
+    for _ in range(reps):
+        for fn in fns:
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            fn()
+            end.record()
+            pairs.append((start, end))
+    torch.cuda.synchronize()
+    return statistics.median(s.elapsed_time(e) for s, e in pairs)
+
+
+def grouped_mm_side_by_side(steps: dict, device, cold_sets: dict | None = None) -> dict:
     """Per launch of the step: this package's launch alone and
     torch.nn.functional.grouped_mm on the same operands (the call of the
     reference's torch provider, kernels/torch_grouped_gemm.py:162-174: A
     [E * M_e, K], B [E, K, N], int32 cumulative offsets), timed alternately
     (paired_ms); the relative Frobenius difference of their outputs on the
-    first two experts rides along."""
+    first two experts rides along.
+
+    For projections in `cold_sets` (projection -> the second resident
+    workspace set) the launch is also timed alone with its two workspace sets
+    taking turns (`alone_cold_ms`), as the rotating-cold step runs it."""
     import torch
 
     out = {}
     for proj, rank_step in steps.items():
+        other = (cold_sets or {}).get(proj)
+        others = {(par, m): ws for par, m, ws in other.workspaces} if other is not None else {}
         for par, m, ws in rank_step.workspaces:
             if (par, m) not in rank_step.stacks:
                 continue
@@ -1303,9 +1331,12 @@ def grouped_mm_side_by_side(steps: dict, device) -> dict:
             theirs = holder["c"][:compared * m_rows].float()
             diff = float((ours - theirs).norm() / theirs.norm().clamp_min(1e-30))
             holder.clear()
-            out[(proj, par, m)] = {"alone_ms": round(native_ms, 4), "grouped_mm_ms": round(gm_ms, 4),
-                                   "vs_grouped_mm": round(gm_ms / native_ms, 3),
-                                   "rel_diff_vs_grouped_mm": float(f"{diff:.3e}")}
+            row = {"alone_ms": round(native_ms, 4), "grouped_mm_ms": round(gm_ms, 4),
+                   "vs_grouped_mm": round(gm_ms / native_ms, 3), "rel_diff_vs_grouped_mm": float(f"{diff:.3e}")}
+            if (par, m) in others:
+                ws_other = others[(par, m)]
+                row["alone_cold_ms"] = round(alternating_ms([lambda: launch(ws), lambda: launch(ws_other)]), 4)
+            out[(proj, par, m)] = row
             torch.cuda.empty_cache()
     return out
 
@@ -1718,11 +1749,14 @@ def main(argv=None) -> int:
                     "max_rel_frobenius": max((c["max_rel_frobenius"] for c in ran), default=None),
                     "tolerance": 1e-2, "by_projection": checks}
 
-    side = {}
+    side, side_clocks = {}, None
     if not args.skip_grouped_mm and not args.fp8 and not args.fused_swiglu and args.layout == "tables":
         progress("per-shape side-by-side with torch grouped_mm")
+        side_clock = ClockSampler(local_rank)
+        side_clock.start()
         with torch.cuda.stream(stream):
-            side = grouped_mm_side_by_side(first, device)
+            side = grouped_mm_side_by_side(first, device, {proj: sets[proj][1] for proj in cold})
+        side_clocks = side_clock.stop()
         check_device_errors(local_rank)
     for row in per_shape:
         proj = next(p for p in projections if PROJECTION_NAME[p] == row["projection"])
@@ -1770,9 +1804,11 @@ def main(argv=None) -> int:
                 "native_wins": sum(1 for r in compared if r["vs_grouped_mm"] > 1.0), "shapes": len(compared),
                 "step_ms_native_alone": round(sum(r["alone_ms"] for r in compared), 4),
                 "step_ms_grouped_mm": round(sum(r["grouped_mm_ms"] for r in compared), 4),
+                "clocks": side_clocks,
                 "note": "each launch alone, hot, alternating with grouped_mm call by call, median of 15 "
                         "CUDA-event-timed calls each; grouped_mm = torch.nn.functional.grouped_mm on the same "
-                        "operands (the reference's torch provider)"},
+                        "operands (the reference's torch provider); alone_cold_ms: the rotating-cold launches "
+                        "alone with their two workspace sets taking turns; clocks: NVML over the whole pass"},
             "cpu_baseline": None if cpu is None else {k: cpu[k] for k in ("value", "unit", "cores", "kind",
                                                                               "sample")},
             "e2e": {"value": round(rank_flops * world * e2e_steps / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
