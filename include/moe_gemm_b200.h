@@ -149,7 +149,9 @@ int grouped_gemm_offsets_launch(const void* a, const void* b, void* c, const int
  * multiple of 8; a homogeneous group that breaks it is refused with
  * MGB_ERR_UNSUPPORTED, a heterogeneous entry is skipped and reported in the
  * error word.  config->block_m picks the tile (<= 16 / 32 / 64: swap-AB with
- * that many tokens x 256 weight rows; larger: 128 x 128).  Scratch:
+ * that many tokens x 256 weight rows; up to 255: 128 x 128; from 256: a CTA
+ * pair of 256 tokens x 128 weight rows, or x 256 when config->block_n >= 256,
+ * refused with MGB_ERR_UNSUPPORTED where the device cannot run that tile).  Scratch:
  * grouped_gemm_scratch_bytes(problem_count, *).  No counterpart in the
  * reference, which runs every expert in fp16 / bf16 / fp32 and notes that the
  * model's FP8 quantization is not emulated (README.md:298). */
