@@ -2,7 +2,8 @@
 //
 // Every rank owns one device region (moe_ep_shared_alloc) that its peers map
 // through CUDA IPC; a rank's kernels get the base of every rank's region and
-// move data with plain loads and stores to peer memory (no NCCL, no multicast).
+// move data with loads, stores and (dispatch) bulk shared -> global copies to
+// peer memory (no NCCL, no multicast).
 // Region of one rank (byte offsets from moe_ep_region_layout):
 //
 //   control    uint32 flags[3][MGB_EP_MAX_WORLD] (phase, source rank), the
@@ -282,6 +283,68 @@ __global__ void __launch_bounds__(kThreads)
   }
 }
 
+// Bulk variant of ep_dispatch_kernel for 16-byte-aligned rows of at most
+// kBulkRowBytes: one warp per token stages the row in shared memory (coalesced
+// 16-byte loads), then lane j copies it to slot j's receive row with one
+// cp.async.bulk shared -> global store (peer memory for remote owners), so each
+// row crosses NVLink as one bulk transfer instead of 16-byte stores.  Each warp
+// alternates two row buffers; a buffer is refilled only after the copies issued
+// from it two tokens earlier have read it.  Before the block's completion
+// count, every lane waits for its copies to be performed and fences the async
+// proxy against the generic one.
+constexpr int kBulkWarps = 4;
+constexpr int64_t kBulkRowBytes = 24 * 1024;
+
+__global__ void __launch_bounds__(32 * kBulkWarps)
+    ep_dispatch_bulk_kernel(const uint8_t* __restrict__ x, int64_t x_pitch_bytes, const int32_t* __restrict__ ids,
+                            const int32_t* __restrict__ position, int64_t tokens, int32_t top_k, EpArgs a) {
+  extern __shared__ __align__(128) uint8_t bulk_smem[];
+  char* self = region_of(a, a.rank);
+  uint32_t* control = reinterpret_cast<uint32_t*>(self);
+  const int32_t* send_base = reinterpret_cast<const int32_t*>(self + a.layout.send_base);
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t stride = (a.row_bytes + 127) / 128 * 128;
+  uint8_t* buffers = bulk_smem + static_cast<int64_t>(warp) * 2 * stride;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * kBulkWarps;
+  uint32_t iter = 0;
+  for (int64_t t = blockIdx.x * static_cast<int64_t>(kBulkWarps) + warp; t < tokens; t += warps, ++iter) {
+    uint8_t* buf = buffers + (iter & 1u) * stride;
+    mgb::bulk_wait_group_read<1>();  // this lane's copies from `buf` (two tokens ago) have read it
+    __syncwarp();
+    const uint8_t* src = x + t * x_pitch_bytes;
+    for (int64_t b = lane * 16; b < a.row_bytes; b += 32 * 16) {
+      *reinterpret_cast<uint4*>(buf + b) = *reinterpret_cast<const uint4*>(src + b);
+    }
+    mgb::fence_proxy_async_smem();  // the row's generic writes -> visible to the bulk copies
+    __syncwarp();
+    for (int j = lane; j < top_k; j += 32) {
+      const int64_t i = t * top_k + j;
+      const int64_t row = slot_recv_row(a, send_base, ids, position, i, true);
+      if (row < 0) continue;
+      char* owner = region_of(a, ids[i] / a.local_experts);
+      uint8_t* dst = reinterpret_cast<uint8_t*>(owner + a.layout.recv) + row * a.row_bytes;
+      // The owner's W2 epilogue returns this row to (this rank, slot i).
+      reinterpret_cast<int64_t*>(owner + a.layout.origin)[row] = (static_cast<int64_t>(a.rank) << 40) | i;
+      asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst),
+                   "r"(static_cast<uint32_t>(__cvta_generic_to_shared(buf))), "r"(static_cast<uint32_t>(a.row_bytes))
+                   : "memory");
+    }
+    mgb::bulk_commit_group();
+  }
+  mgb::bulk_wait_group_all();  // this lane's copies are performed
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const uint32_t finished = atomicAdd(control + kDoneWord, 1u);
+    if (finished == gridDim.x - 1) {
+      atomicExch(control + kDoneWord, 0u);
+      signal_and_wait(a, 1, __ldcg(control + kEpochWord));
+    }
+  }
+}
+
 // One thread: barrier 2 (every rank's expert outputs are complete).
 __global__ void ep_barrier_kernel(EpArgs a, int phase) {
   if (threadIdx.x == 0) {
@@ -486,9 +549,30 @@ int moe_ep_dispatch(const void* x, int64_t x_pitch, const int32_t* topk_ids, con
   if (tokens > 0 && (x == nullptr || topk_ids == nullptr || position == nullptr)) return MGB_ERR_INVALID;
   const int64_t pitch_bytes = x_pitch * config->elem_bytes;
   const bool vec16 = aligned16(x) && a.row_bytes % 16 == 0 && pitch_bytes % 16 == 0;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   // Launched even without slots: every rank takes part in barrier 1.
-  ep_dispatch_kernel<<<grid_for(tokens, kThreads / 32), kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<const uint8_t*>(x), pitch_bytes, topk_ids, position, tokens, top_k, vec16, a);
+  if (vec16 && a.row_bytes <= kBulkRowBytes) {
+    const size_t smem = static_cast<size_t>(kBulkWarps) * 2 * static_cast<size_t>((a.row_bytes + 127) / 128 * 128);
+    static bool configured[128] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 128) return MGB_ERR_CUDA;
+    if (!configured[dev]) {
+      if (cudaFuncSetAttribute(ep_dispatch_bulk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(kBulkWarps * 2 * kBulkRowBytes)) != cudaSuccess) {
+        return MGB_ERR_CUDA;
+      }
+      configured[dev] = true;
+    }
+    int sms = 148;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t blocks = (tokens + kBulkWarps - 1) / kBulkWarps;
+    const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, sms)));
+    ep_dispatch_bulk_kernel<<<grid, 32 * kBulkWarps, smem, s>>>(static_cast<const uint8_t*>(x), pitch_bytes,
+                                                                 topk_ids, position, tokens, top_k, a);
+  } else {
+    ep_dispatch_kernel<<<grid_for(tokens, kThreads / 32), kThreads, 0, s>>>(
+        static_cast<const uint8_t*>(x), pitch_bytes, topk_ids, position, tokens, top_k, vec16, a);
+  }
   return cudaGetLastError() == cudaSuccess ? MGB_OK : MGB_ERR_CUDA;
 }
 
