@@ -318,8 +318,8 @@ def native_candidates(max_m: int, max_k: int | None = None, *, split_tail: bool 
     can run a short last wave of 256 x 512 tiles as half-width items (an
     exact tile count: a single GEMM or a homogeneous group, no SwiGLU).
 
-    Measured on B200 over whole DeepSeek-V3 W13 and W2 steps (``bench.py
-    --tile-map``), where the GPU sits at its power cap and every launch's
+    Measured on B200 over whole DeepSeek-V3 W13 and W2 steps (same-box A/B
+    runs of tile maps), where the GPU sits at its power cap and every launch's
     energy sets the clock of the others: the token tile fits M exactly (swap-AB
     16 / 32 / 64 tokens x 256 weight columns, so no MMA work is spent on padding
     rows), 128-token x 256-column tiles at M <= 128, and CTA-pair tiles beyond.
