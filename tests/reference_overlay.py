@@ -5,7 +5,7 @@ The reference's drivers import `kernels.grouped_gemm` and `kernels.matmul`
 (benchmark_moe.py:12-18, benchmark_shapes.py:8-13, compare_grouped_gemm.py:14,
 tests/test_gpu.py:11-17).  The overlay keeps every reference file and replaces
 those two modules, adding their helpers and the native library, exactly as a
-maintainer would install the drop-in (INTEGRATION.md section 2).  The package
+maintainer would install the drop-in.  The package
 files are symlinked, not copied, so a process that loads the library maps the
 in-tree libmoe_gemm_b200.so.
 """
