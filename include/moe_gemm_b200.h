@@ -323,6 +323,16 @@ int matrix_repack(const void* src, int64_t rows, int64_t cols, int64_t stride_r,
 int matrix_split_tf32x3(const float* src, int64_t rows, int64_t cols, int64_t stride_r, int64_t stride_c, float* dst,
                         int64_t dst_pitch, int32_t side, void* stream);
 
+/* The reduction of a single GEMM whose K was split over several problems of
+ * one grouped launch (kernels/matmul.py does this for fp32 GEMMs with too
+ * few output tiles to fill the GPU and a long K): C = sum over s of
+ * partials[s], partials fp32 [splits][rows][cols] contiguous, summed in the
+ * order s = 0, 1, ... in fp32 and rounded once to dtype, C written through
+ * its element strides.  No counterpart in the reference, whose Triton matmul
+ * runs each output tile's whole K in one program (kernels/matmul.py:256-268). */
+int matrix_sum_partials(const float* partials, int32_t splits, int64_t rows, int64_t cols, void* c, int64_t stride_cm,
+                        int64_t stride_cn, int32_t dtype, void* stream);
+
 /* Size of the scratch array compiled into the library for
  * grouped_gemm_launch_noalloc (bytes, per GPU that loads the library). */
 #define MGB_NOALLOC_SCRATCH_BYTES (1u << 20)

@@ -304,6 +304,30 @@ __global__ void __launch_bounds__(256) split_tf32x3_kernel(const float* __restri
   }
 }
 
+// C = sum over s of the fp32 partial products P[s] ([splits][rows][cols],
+// contiguous), added in the order s = 0, 1, ... so the result does not depend
+// on the launch, rounded once to C's type and stored through C's strides.
+template <typename T>
+__global__ void __launch_bounds__(256) sum_partials_kernel(const float* __restrict__ partials, int32_t splits,
+                                                           int64_t rows, int64_t cols, T* __restrict__ c,
+                                                           int64_t stride_cm, int64_t stride_cn) {
+  const int64_t total = rows * cols;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float acc = 0.0f;
+    for (int32_t s = 0; s < splits; ++s) acc += partials[s * total + i];
+    const int64_t r = i / cols, col = i - r * cols;
+    T* dst = c + r * stride_cm + col * stride_cn;
+    if constexpr (std::is_same<T, float>::value) {
+      *dst = acc;
+    } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      *dst = __float2bfloat16_rn(acc);
+    } else {
+      *dst = __float2half_rn(acc);
+    }
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -325,6 +349,34 @@ int matrix_split_tf32x3(const float* src, int64_t rows, int64_t cols, int64_t st
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, 16ll * sms)));
   split_tf32x3_kernel<<<grid, dim3(32, 8), 0, static_cast<cudaStream_t>(stream)>>>(src, rows, cols, stride_r,
                                                                                    stride_c, dst, dst_pitch, side);
+  return cudaGetLastError() == cudaSuccess ? MGB_OK : MGB_ERR_CUDA;
+}
+
+int matrix_sum_partials(const float* partials, int32_t splits, int64_t rows, int64_t cols, void* c, int64_t stride_cm,
+                        int64_t stride_cn, int32_t dtype, void* stream) {
+  if (splits <= 0 || rows < 0 || cols < 0 || (dtype != MGB_FP16 && dtype != MGB_BF16 && dtype != MGB_FP32)) {
+    return MGB_ERR_INVALID;
+  }
+  if (rows == 0 || cols == 0) return MGB_OK;
+  if (partials == nullptr || c == nullptr) return MGB_ERR_INVALID;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    return MGB_ERR_CUDA;
+  }
+  const int64_t blocks = (rows * cols + 255) / 256;
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(blocks, 8ll * sms)));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == MGB_FP32) {
+    sum_partials_kernel<float><<<grid, 256, 0, s>>>(partials, splits, rows, cols, static_cast<float*>(c), stride_cm,
+                                                   stride_cn);
+  } else if (dtype == MGB_BF16) {
+    sum_partials_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(partials, splits, rows, cols,
+                                                           static_cast<__nv_bfloat16*>(c), stride_cm, stride_cn);
+  } else {
+    sum_partials_kernel<__half><<<grid, 256, 0, s>>>(partials, splits, rows, cols, static_cast<__half*>(c), stride_cm,
+                                                    stride_cn);
+  }
   return cudaGetLastError() == cudaSuccess ? MGB_OK : MGB_ERR_CUDA;
 }
 

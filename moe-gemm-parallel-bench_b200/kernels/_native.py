@@ -52,6 +52,7 @@ EXPORTED_SYMBOLS = (
     "matmul_launch",
     "matrix_repack",
     "matrix_split_tf32x3",
+    "matrix_sum_partials",
     "read_and_clear_error_word",
     "mgb_set_debug",
     "mgb_status_string",
@@ -247,6 +248,11 @@ def _declare(lib) -> None:
         ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
     ]
     lib.matrix_split_tf32x3.restype = ctypes.c_int
+    lib.matrix_sum_partials.argtypes = [
+        ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+        ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p,
+    ]
+    lib.matrix_sum_partials.restype = ctypes.c_int
     lib.read_and_clear_error_word.argtypes = [ctypes.c_int32, ctypes.POINTER(ctypes.c_uint32)]
     lib.read_and_clear_error_word.restype = ctypes.c_int
     lib.mgb_set_debug.argtypes = [ctypes.c_int64, ctypes.c_int32]
@@ -501,6 +507,14 @@ def split_tf32x3(src: int, rows: int, cols: int, stride_r: int, stride_c: int, d
     rows)."""
     _check(load().matrix_split_tf32x3(src, int(rows), int(cols), int(stride_r), int(stride_c), dst, int(dst_pitch),
                                       int(side), stream), "matrix_split_tf32x3")
+
+
+def sum_partials(partials: int, splits: int, rows: int, cols: int, c: int, stride_cm: int, stride_cn: int,
+                 dtype: str, stream: int) -> None:
+    """matrix_sum_partials: C = sum over s of the fp32 partials [splits][rows][cols]
+    of a split-K GEMM, rounded once to C's dtype."""
+    _check(load().matrix_sum_partials(partials, int(splits), int(rows), int(cols), c, int(stride_cm), int(stride_cn),
+                                      DTYPE_CODES[dtype], stream), "matrix_sum_partials")
 
 
 def read_and_clear_error_word(device: int) -> int:

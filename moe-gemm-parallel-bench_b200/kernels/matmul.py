@@ -265,6 +265,73 @@ def split_operands_3xtf32(a, b, stream: int):
     return a3, b3
 
 
+# Split-K for fp32 single GEMMs on the tensor cores: an output of few tiles
+# (127 rows or columns) with a long K leaves most SMs idle, e.g.
+# 127 x 8191 @ 8191 x 8191 covers 64 of 148 SMs for its whole K.  From
+# SPLITK_MIN_K such a GEMM runs as one grouped launch over `splits` K slices
+# (problem s multiplies A[:, s kc : (s + 1) kc] by the matching rows of B into
+# fp32 partial s), and matrix_sum_partials adds the partials in a fixed order.
+# fp32 only: the partials keep fp32, so the result is rounded once, as one
+# tensor-core launch rounds it.
+SPLITK_MIN_K = 2048
+_SM_COUNT: dict = {}
+
+
+def _sm_count(device) -> int:
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if index not in _SM_COUNT:
+        _SM_COUNT[index] = torch.cuda.get_device_properties(index).multi_processor_count
+    return _SM_COUNT[index]
+
+
+def splitk_splits(m: int, n: int, k: int, sms: int) -> int:
+    """K slices for an fp32 tensor-core GEMM: 1 (no split) unless the output
+    has at most half as many 128 x 128 tiles as the GPU has SMs and K is at
+    least SPLITK_MIN_K; then enough slices to cover the SMs, at most 8, each
+    at least 1024 deep.  Two slices only from K = 6144: below it the second
+    launch, the partials' traffic and the sum cost more than the second half
+    of the SMs gains (measured on the configs[4] sweep, e.g. 0.76x at
+    127 x 3000 x 8191 and 0.85x at 1000 x 4095 x 1000)."""
+    tiles = -(-m // 128) * -(-n // 128)
+    if k < SPLITK_MIN_K or 2 * tiles > sms:
+        return 1
+    splits = max(1, min(8, sms // tiles, k // 1024))
+    return 1 if splits == 2 and k < 6144 else splits
+
+
+def _launch_split_k(a, b, c, m: int, n: int, k: int, splits: int, precision: str, config, stream: int):
+    """One grouped launch over `splits` K slices of the fp32 GEMM a @ b (both
+    TMA-addressable: unit column stride, 16-byte row pitch) into fp32
+    partials, then their sum into c.  Every table is built on the device, so
+    the launch can be recorded into a CUDA graph."""
+    device = a.device
+    kc = -(-k // splits)
+    kc = -(-kc // 64) * 64  # whole 64-element slices keep every slice base 16-byte aligned
+    splits = -(-k // kc)
+    partials = torch.empty((splits, m, n), dtype=torch.float32, device=device)
+    index = torch.arange(splits, dtype=torch.int64, device=device)
+    a_ptrs = index * (kc * 4) + a.data_ptr()
+    b_ptrs = index * (kc * b.stride(0) * 4) + b.data_ptr()
+    c_ptrs = index * (m * n * 4) + partials.data_ptr()
+    # fill_ on views only: an element assignment would copy a host scalar,
+    # which a CUDA-graph capture refuses.
+    dims = torch.empty((splits, 3), dtype=torch.int32, device=device)
+    for col, value in ((0, m), (1, n), (2, kc)):
+        dims[:, col].fill_(value)
+    dims[splits - 1:, 2].fill_(k - kc * (splits - 1))
+    strides = torch.empty((splits, 6), dtype=torch.int64, device=device)
+    for col, value in enumerate((a.stride(0), 1, b.stride(0), 1, n, 1)):
+        strides[:, col].fill_(value)
+    need = _native.scratch_bytes(splits, _sm_count(device))
+    scratch = torch.empty(need, dtype=torch.uint8, device=device)
+    info = _native.grouped_launch(
+        a_ptrs.data_ptr(), b_ptrs.data_ptr(), c_ptrs.data_ptr(), dims.data_ptr(), strides.data_ptr(), splits,
+        False, m, n, kc, "fp32", precision, True, config, scratch.data_ptr(), need, stream,
+    )
+    _native.sum_partials(partials.data_ptr(), splits, m, n, c.data_ptr(), c.stride(0), c.stride(1), "fp32", stream)
+    return info, splits
+
+
 def _launch_once(a, b, c, m: int, n: int, k: int, config: KernelConfig, precision: str) -> dict:
     global _last_launch_info
     stream = torch.cuda.current_stream(a.device).cuda_stream
@@ -275,27 +342,37 @@ def _launch_once(a, b, c, m: int, n: int, k: int, config: KernelConfig, precisio
         # proportion to K).
         with torch.cuda.device(a.device):
             a3, b3 = split_operands_3xtf32(a, b, stream)
-            info = _native.matmul_launch(
-                a3.data_ptr(), b3.data_ptr(), c.data_ptr(), m, n, 3 * k,
-                (a3.stride(0), 1, b3.stride(0), 1, c.stride(0), c.stride(1)), "fp32", "tf32_fp32acc", config,
-                stream,
-            )
-        _last_launch_info = {**info.as_dict(), "repacked": True, "split_3xtf32": True}
+            splits = splitk_splits(m, n, 3 * k, _sm_count(a.device))
+            if splits > 1:
+                info, splits = _launch_split_k(a3, b3, c, m, n, 3 * k, splits, "tf32_fp32acc", config, stream)
+            else:
+                info = _native.matmul_launch(
+                    a3.data_ptr(), b3.data_ptr(), c.data_ptr(), m, n, 3 * k,
+                    (a3.stride(0), 1, b3.stride(0), 1, c.stride(0), c.stride(1)), "fp32", "tf32_fp32acc", config,
+                    stream,
+                )
+        _last_launch_info = {**info.as_dict(), "repacked": True, "split_3xtf32": True, "split_k": splits}
         return _last_launch_info
     tensor_core = a.dtype != torch.float32 or precision == "tf32"
     repacked = False
+    splits = 1
     with torch.cuda.device(a.device):
         if tensor_core and 2 * m * n * k >= REPACK_MIN_FLOPS and k > 0:
             if not _tma_addressable(a):
                 a, repacked = _repacked(a, stream), True
             if not _tma_addressable(b):
                 b, repacked = _repacked(b, stream), True
-        info = _native.matmul_launch(
-            a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k,
-            (a.stride(0), a.stride(1), b.stride(0), b.stride(1), c.stride(0), c.stride(1)),
-            dtype_name(a.dtype), precision, config, stream,
-        )
-    _last_launch_info = {**info.as_dict(), "repacked": repacked, "split_3xtf32": False}
+            if a.dtype == torch.float32:
+                splits = splitk_splits(m, n, k, _sm_count(a.device))
+        if splits > 1:
+            info, splits = _launch_split_k(a, b, c, m, n, k, splits, precision, config, stream)
+        else:
+            info = _native.matmul_launch(
+                a.data_ptr(), b.data_ptr(), c.data_ptr(), m, n, k,
+                (a.stride(0), a.stride(1), b.stride(0), b.stride(1), c.stride(0), c.stride(1)),
+                dtype_name(a.dtype), precision, config, stream,
+            )
+    _last_launch_info = {**info.as_dict(), "repacked": repacked, "split_3xtf32": False, "split_k": splits}
     return _last_launch_info
 
 

@@ -922,6 +922,74 @@ def test_masked_large_shapes_repack_onto_tensor_cores(dtype_name, precision, sha
     _oracle_check(c, a, b, dtype_name, precision)
 
 
+@pytest.mark.parametrize("m,k,n,precision,masked", [
+    (127, 8191, 4095, "tf32", True),
+    (4095, 8191, 127, "ieee", True),
+    (127, 2048, 127, "ieee", False),
+    (256, 4096, 384, "tf32", False),
+])
+def test_fp32_split_k_single_gemm(m, k, n, precision, masked):
+    """fp32 GEMMs with few output tiles and a long K run as one grouped launch
+    over K slices into fp32 partials plus matrix_sum_partials; sampled rows
+    against the float64 oracle, and a CUDA-graph replay of the same launch
+    gives the same bits."""
+    torch = _torch()
+    from kernels import check_device_errors, launch_matmul
+    from kernels.matmul import last_launch_info
+    from oracle import gemm as oracle
+
+    gen = torch.Generator(device="cuda").manual_seed(m + 3 * k + 7 * n)
+    if masked:  # rows of k (or n) floats: the TMA cannot address them, so they are repacked first
+        a = torch.randn((m, k), device="cuda", generator=gen)
+        b = torch.randn((k, n), device="cuda", generator=gen) / math.sqrt(k)
+    else:
+        a = torch.randn((m, k + 5), device="cuda", generator=gen)[:, :k]
+        a = a.contiguous()
+        b = torch.randn((k, n), device="cuda", generator=gen) / math.sqrt(k)
+    c = torch.full((m, n), float("nan"), device="cuda", dtype=torch.float32)
+    launch_matmul(a, b, c, input_precision=precision)
+    torch.cuda.synchronize()
+    check_device_errors()
+    info = last_launch_info()
+    assert info["split_k"] > 1, info
+    assert not torch.isnan(c).any()
+    rows = torch.tensor(sorted({0, 1, m // 2, m - 1}), device="cuda")
+    got = c.index_select(0, rows).double().cpu().numpy()
+    expected = oracle.matmul(a.index_select(0, rows).double().cpu().numpy(), b.double().cpu().numpy(), "fp32")
+    assert oracle.relative_frobenius(got, expected) <= REL_FRO["tf32" if precision == "tf32" else "fp32"]
+    eager = c.clone()
+    c.fill_(float("nan"))
+    stream = torch.cuda.Stream()
+    stream.wait_stream(torch.cuda.current_stream())
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            launch_matmul(a, b, c, input_precision=precision)
+        graph.replay()
+    stream.synchronize()
+    check_device_errors()
+    assert torch.equal(c, eager)
+    del graph
+
+
+def test_sum_partials_every_output_dtype():
+    """matrix_sum_partials adds the partials in order in fp32 and rounds once,
+    through C's strides, for fp32, bf16 and fp16 outputs."""
+    torch = _torch()
+    from kernels import _native
+
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    partials = torch.randn((3, 37, 45), device="cuda", generator=gen)
+    expected = (partials[0] + partials[1]) + partials[2]
+    stream = torch.cuda.current_stream().cuda_stream
+    for dtype, name in ((torch.float32, "fp32"), (torch.bfloat16, "bf16"), (torch.float16, "fp16")):
+        out = torch.full((45, 37), float("nan"), device="cuda", dtype=dtype).t()  # column-major C
+        _native.sum_partials(partials.data_ptr(), 3, 37, 45, out.data_ptr(), out.stride(0), out.stride(1), name,
+                             stream)
+        torch.cuda.synchronize()
+        assert torch.equal(out, expected.to(dtype)), name
+
+
 @pytest.mark.parametrize("case", [
     # Mixtral-8x7B (E=8, H=4096, F=14336), M_e = 1024: EP P=8 is one expert per rank
     ("mixtral W13 EP P=8", [(1024, 4096, 2 * 14336)], True),

@@ -172,3 +172,18 @@ def test_fp8_quantization_round_trip_and_tiles():
     assert fp8.fp8_tile_for(16).block_m == 16 and fp8.fp8_tile_for(40).block_m == 64
     assert fp8.fp8_tile_for(200).block_m == 128
     assert (fp8.fp8_tile_for(256).block_m, fp8.fp8_tile_for(1024).block_n) == (256, 256)
+
+
+def test_split_k_slices_for_skinny_fp32_gemms():
+    """fp32 tensor-core GEMMs split K only when the output leaves most SMs idle
+    and K is long; at most 8 slices of at least 1024."""
+    from kernels import matmul as mm
+
+    assert mm.splitk_splits(127, 8191, 8191, 148) == 2   # m, n, k: 64 output tiles
+    assert mm.splitk_splits(127, 127, 8191, 148) == 7    # one tile: 8191 // 1024 slices
+    assert mm.splitk_splits(127, 4095, 4096, 148) == 4   # 32 tiles
+    assert mm.splitk_splits(127, 8191, 1000, 148) == 1   # K below SPLITK_MIN_K
+    assert mm.splitk_splits(1000, 1000, 8191, 148) == 2  # 64 tiles
+    assert mm.splitk_splits(1000, 1000, 4095, 148) == 1  # two slices only from K = 6144
+    assert mm.splitk_splits(127, 8191, 3000, 148) == 1   # the 3xTF32 depth of K = 1000
+    assert mm.splitk_splits(8191, 8191, 8191, 148) == 1  # the output fills the GPU
