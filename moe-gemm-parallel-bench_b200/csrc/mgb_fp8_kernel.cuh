@@ -512,16 +512,19 @@ __global__ void __launch_bounds__(Fp8Cfg<SWAP, TM, TN>::kThreads, 1)
 }
 
 // ------------------------------------------------------------------------
-// CTA-pair FP8 tile for token-rich problems: a cluster of two CTAs owns a
-// 256-token x 128-weight-row output tile (one weight scale block).  CTA r
-// loads token rows [128 r, 128 r + 128) and weight rows [64 r, 64 r + 64) of
-// every 128-deep K block into its own shared memory; the even CTA issues
-// tcgen05.mma.cta_group::2.kind::f8f6f4 (M = 256, N = 128), which reads both
-// CTAs' halves and writes rows 0-127 / 128-255 of the partial into CTA 0 / 1's
-// TMEM.  Per CTA and K block that is 24 KB from L2 for 128 x 128 x 128 MACs
-// (175 FLOP per byte) instead of 32 KB for the one-CTA 128 x 128 tile (131).
-// Each CTA's eight promotion warps then work on their own 128 rows exactly as
-// in the one-CTA row tile.  Barriers as in tc2_grouped_kernel:
+// CTA-pair FP8 tiles for token-rich problems: a cluster of two CTAs owns a
+// 256-token x TN-weight-row output tile (TN = 128: one weight scale block;
+// TN = 256: two).  CTA r loads token rows [128 r, 128 r + 128) and weight rows
+// [TN/2 r, TN/2 r + TN/2) of every 128-deep K block into its own shared
+// memory; the even CTA issues tcgen05.mma.cta_group::2.kind::f8f6f4
+// (M = 256, N = TN), which reads both CTAs' halves and writes rows 0-127 /
+// 128-255 of the partial into CTA 0 / 1's TMEM.  Per CTA and K block the
+// 256 x 128 tile reads 24 KB from L2 for 128 x 128 x 128 MACs, the 256 x 256
+// tile 32 KB for twice the MACs, and each of its MMAs does four times the
+// work of a one-CTA 128 x 128 MMA.  Each CTA's eight promotion warps then work
+// on their own 128 rows, two per TMEM lane quarter, each on TN / 2 columns
+// (one scale block at TN = 256, with 128 fp32 accumulators a lane: see
+// Fp8PairCfgT's register split).  Barriers as in tc2_grouped_kernel:
 //   full[s]         in CTA 0 only: both CTAs' TMA bytes for stage s land on it
 //   empty[s]        in each CTA: the MMA commit multicasts to both
 //   part_full[b]    in each CTA: the MMA commit multicasts to both
