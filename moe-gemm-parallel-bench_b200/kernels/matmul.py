@@ -287,15 +287,19 @@ def _sm_count(device) -> int:
 def splitk_splits(m: int, n: int, k: int, sms: int) -> int:
     """K slices for an fp32 tensor-core GEMM: 1 (no split) unless the output
     has at most half as many 128 x 128 tiles as the GPU has SMs and K is at
-    least SPLITK_MIN_K; then enough slices to cover the SMs, at most 8, each
-    at least 1024 deep.  Two slices only from K = 6144: below it the second
-    launch, the partials' traffic and the sum cost more than the second half
-    of the SMs gains (measured on the configs[4] sweep, e.g. 0.76x at
-    127 x 3000 x 8191 and 0.85x at 1000 x 4095 x 1000)."""
+    least SPLITK_MIN_K; then enough slices to cover the SMs, at most 32, each
+    at least 1024 deep, or 256 for an output of at most 8 tiles (a single
+    tile's long K is latency-bound: its ring holds only a few k-blocks in
+    flight).  Two slices only from K = 6144: below it the partials' traffic
+    and the sum cost more than the second half of the SMs gains.  Measured
+    on the configs[4] sweep: 256-deep slices gain 1.1-1.4x on 1-8 tile
+    outputs and lose 0.85x at 32 tiles (127 x 3000 x 4095); two slices lose
+    0.85x at 1000 x 4095 x 1000."""
     tiles = -(-m // 128) * -(-n // 128)
     if k < SPLITK_MIN_K or 2 * tiles > sms:
         return 1
-    splits = max(1, min(8, sms // tiles, k // 1024))
+    depth = 256 if tiles <= 8 else 1024
+    splits = max(1, min(32, sms // tiles, k // depth))
     return 1 if splits == 2 and k < 6144 else splits
 
 

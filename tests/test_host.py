@@ -176,14 +176,18 @@ def test_fp8_quantization_round_trip_and_tiles():
 
 def test_split_k_slices_for_skinny_fp32_gemms():
     """fp32 tensor-core GEMMs split K only when the output leaves most SMs idle
-    and K is long; at most 8 slices of at least 1024."""
+    and K is long; at most 32 slices of at least 1024 (256 for outputs of up
+    to 8 tiles), and two only from K = 6144."""
     from kernels import matmul as mm
 
     assert mm.splitk_splits(127, 8191, 8191, 148) == 2   # m, n, k: 64 output tiles
-    assert mm.splitk_splits(127, 127, 8191, 148) == 7    # one tile: 8191 // 1024 slices
+    assert mm.splitk_splits(127, 127, 8191, 148) == 31   # one tile: 8191 // 256 slices
+    assert mm.splitk_splits(127, 127, 3000, 148) == 11   # the 3xTF32 depth of K = 1000, one tile
     assert mm.splitk_splits(127, 4095, 4096, 148) == 4   # 32 tiles
     assert mm.splitk_splits(127, 8191, 1000, 148) == 1   # K below SPLITK_MIN_K
     assert mm.splitk_splits(1000, 1000, 8191, 148) == 2  # 64 tiles
     assert mm.splitk_splits(1000, 1000, 4095, 148) == 1  # two slices only from K = 6144
     assert mm.splitk_splits(127, 8191, 3000, 148) == 1   # the 3xTF32 depth of K = 1000
     assert mm.splitk_splits(8191, 8191, 8191, 148) == 1  # the output fills the GPU
+    assert mm.splitk_splits(127, 4095, 3000, 148) == 1   # 32 tiles: 1024-deep slices, so only two
+    assert mm.splitk_splits(127, 1000, 4095, 148) == 15  # 8 tiles: 256-deep slices
