@@ -42,16 +42,18 @@ FP8_TILE_PAIR_256x256 = KernelConfig(256, 256, 128, 8, 8, 4)  # CTA pair: 256 to
 
 def fp8_tile_for(max_m: int) -> KernelConfig:
     """Swap-AB tiles (weight rows as MMA M, exact-fit token count) while the
-    launch streams weights from HBM, 128 x 128 token tiles above 64 tokens,
-    and from 256 tokens the CTA-pair 256 x 256 tile, whose M = 256, N = 256
-    MMAs do four times the work of a 128 x 128 tile's per instruction."""
+    launch streams weights from HBM, 128 x 128 token tiles up to 128 tokens,
+    and above that the CTA-pair 256 x 256 tile, whose M = 256, N = 256 MMAs
+    do four times the work of a 128 x 128 tile's per instruction (from 129
+    tokens the 128-row tile needs two row blocks anyway: 1.17-1.27x at
+    M = 160-224 on DeepSeek-V3 W13 / W2 rank shapes)."""
     if max_m <= 16:
         return FP8_TILE_SWAP_16
     if max_m <= 32:
         return FP8_TILE_SWAP_32
     if max_m <= 64:
         return FP8_TILE_SWAP_64
-    if max_m < 256:
+    if max_m <= 128:
         return FP8_TILE_ROWS_128
     return FP8_TILE_PAIR_256x256
 

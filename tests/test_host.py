@@ -170,7 +170,7 @@ def test_fp8_quantization_round_trip_and_tiles():
     assert tuple(sw.shape) == (2, 3)
     assert float((fp8.dequantize_weight(qw, sw) - w).norm() / w.norm()) < 0.05
     assert fp8.fp8_tile_for(16).block_m == 16 and fp8.fp8_tile_for(40).block_m == 64
-    assert fp8.fp8_tile_for(200).block_m == 128
+    assert fp8.fp8_tile_for(128).block_m == 128 and fp8.fp8_tile_for(129).block_m == 256
     assert (fp8.fp8_tile_for(256).block_m, fp8.fp8_tile_for(1024).block_n) == (256, 256)
 
 
