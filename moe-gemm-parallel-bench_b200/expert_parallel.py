@@ -9,8 +9,9 @@ GPU:
     route      moe_route_layout: slots per expert, each slot's position
     exchange   moe_ep_exchange_counts: counts to every rank over peer memory,
                then where each rank's rows land on each owner
-    dispatch   moe_ep_dispatch: token rows stored straight into the owners'
-               receive rows (NVLink peer stores, sorted by local expert)
+    dispatch   moe_ep_dispatch: token rows copied straight into the owners'
+               receive rows (one bulk shared -> global copy per slot over
+               NVLink, sorted by local expert)
     W13        grouped GEMM, fused SiLU(gate) * up epilogue, over the receive
                rows in the aggregate layout (offs = per-expert row ends on the
                device, so no host synchronisation)
